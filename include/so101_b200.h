@@ -1,0 +1,200 @@
+/*
+ * so101_b200.h — C ABI of the B200 SmolVLA chunk kernels (libso101_b200.so).
+ *
+ * Every entry point takes device pointers, element strides, sizes and a cudaStream_t, launches
+ * asynchronously on that stream, allocates nothing, and returns an int status (0 = ok, see
+ * SO101_ERR_*). Nothing here takes or returns a framework type; the Python engine binds these
+ * with ctypes, and any other host language can bind them the same way.
+ *
+ * Each entry point names the reference (so101-smolvla-edge, paths relative to its
+ * src/so101_smolvla_edge/) function or kernel it replaces.
+ */
+#ifndef SO101_B200_H
+#define SO101_B200_H
+
+#include <stdint.h>
+#include <cuda_runtime.h>
+
+#if defined(__GNUC__)
+#define SO101_API __attribute__((visibility("default")))
+#else
+#define SO101_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ---------------------------------------------------------------------- */
+#define SO101_OK 0
+#define SO101_ERR_ARG 1         /* a size, stride, pointer alignment or dtype is unsupported */
+#define SO101_ERR_LAUNCH 2      /* the CUDA launch failed (cudaGetLastError after the launch) */
+#define SO101_ERR_WORKSPACE 3   /* split-K workspace or ticket array too small */
+#define SO101_ERR_TIMEOUT 4     /* a device wait hit its bound (read with so101_device_status) */
+#define SO101_ERR_DRIVER 5      /* the driver entry point for TMA descriptors is unavailable */
+
+/* ---- element types --------------------------------------------------------------------- */
+#define SO101_BF16 0
+#define SO101_F32 1
+#define SO101_I8 2
+
+/* ---- GEMM epilogues -------------------------------------------------------------------- */
+#define SO101_EPI_NONE 0      /* y = acc (+ bias)                                           */
+#define SO101_EPI_GELU 1      /* y = gelu_tanh(acc + bias)                                   */
+#define SO101_EPI_SILU_GATE 2 /* w = [gate; up] (2N x K): y = silu(x@gate^T) * (x@up^T)     */
+
+/* Epilogue operands of so101_gemm, applied in this order to the fp32 (or dequantized int32)
+ * accumulator of output element (m, n):
+ *   v  = acc * x_scale * w_scale[n]            (int8 operands only)
+ *   v += bias[n]                               (bias != NULL)
+ *   v  = gelu(v) | silu(v) * v_up              (epilogue)
+ *   v *= out_scale
+ *   v += residual[(m % r_period) * ldr + n]    (residual != NULL; r_period 0 = no period)
+ *   y[row(m) * ldy + n] = cast(v)              (I8: clamp(rint(v / y_qscale), -128, 127))
+ * row(m) = (m / row_group) * row_stride + m % row_group when row_group > 0, else m.
+ * y may alias residual (each element is read before it is written, by the same thread). */
+typedef struct so101_epilogue {
+  int epilogue;
+  const float* bias;
+  const void* residual;
+  int64_t ldr;
+  int r_type;
+  int64_t r_period;
+  float out_scale;
+  const float* w_scale;
+  float x_scale;
+  float y_qscale;
+  int64_t row_group;
+  int64_t row_stride;
+} so101_epilogue;
+
+/* Tile configuration; zero-initialised fields mean "pick" (the heuristic of so101_gemm_pick). */
+typedef struct so101_gemm_config {
+  int swap;    /* 1: weights on the MMA M side (few token rows), 0: tokens on the M side */
+  int bn;      /* MMA N: 16..256, multiple of 16                                         */
+  int splits;  /* K splits (deterministic: the last CTA reduces in split order)          */
+  int stages;  /* shared-memory pipeline depth                                            */
+} so101_gemm_config;
+
+/* y (M x N) = epilogue(x (M x K) @ w (N x K)^T) on tcgen05 tensor cores, TMA-fed.
+ * Replaces kernels/gemm.py:48-96 (so101_gemm) and :350-398 (linear), the cuBLAS F.linear calls of
+ * model/smolvla.py:152-156 and the TensorRT vision GEMMs (model/trt_vision.py:102-163, int8).
+ * a_type SO101_BF16 (kind::f16, fp32 accumulate) or SO101_I8 (kind::i8, int32 accumulate).
+ * Requires: 16-byte aligned x, w; K * elem_size and ldx, ldw a multiple of 16 bytes.
+ * workspace: fp32 split-K partials; tickets: int32 counters, zero before the first call and left
+ * zero by every call. Bytes needed: so101_gemm_workspace_bytes. cfg may be NULL. */
+SO101_API int so101_gemm(int a_type, const void* x, int64_t ldx, const void* w, int64_t ldw, void* y,
+               int64_t ldy, int y_type, int64_t M, int64_t N, int64_t K,
+               const so101_epilogue* epi, const so101_gemm_config* cfg, void* workspace,
+               int64_t workspace_bytes, int* tickets, int64_t n_tickets, cudaStream_t stream);
+
+/* The configuration so101_gemm would pick for this problem on this device (cfg out). */
+SO101_API int so101_gemm_pick(int a_type, int64_t M, int64_t N, int64_t K, int epilogue,
+                    so101_gemm_config* cfg);
+
+/* Split-K workspace bytes and ticket count a configuration needs. */
+SO101_API int so101_gemm_workspace(int a_type, int64_t M, int64_t N, int64_t K, int epilogue,
+                         const so101_gemm_config* cfg, int64_t* workspace_bytes,
+                         int64_t* n_tickets);
+
+/* Grouped-query flash attention, bf16 in, fp32 online softmax (exp2), P rounded to bf16 for PV.
+ * Replaces kernels/attention.py:27-120 (so101_attention) and the SDPA calls of
+ * model/smolvla.py:182, 298, 303, 312-325.
+ * q: (Lq, >= nq*hd) rows of stride ldq, head h at columns [h*hd, (h+1)*hd); k, v: (Lk, nkv*hd).
+ * Query head h reads kv head h / (nq / nkv). Key j is visible to query i iff
+ * j < causal_from || j <= i + q_offset. cos/sin (Lq x hd/2) rotate q on load (NULL: none).
+ * batch: independent problems at element strides bq, bk, bv, bo. o: (Lq, nq*hd) in o_type
+ * (SO101_BF16, or SO101_I8 quantized by o_qscale). hd: 32, 64 or 128. */
+SO101_API int so101_attention(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v,
+                    int64_t ldv, void* o, int64_t ldo, int o_type, float o_qscale, int64_t Lq,
+                    int64_t Lk, int nq, int nkv, int hd, int64_t causal_from, int64_t q_offset,
+                    const float* cos, const float* sin, int batch, int64_t bq, int64_t bk,
+                    int64_t bv, int64_t bo, cudaStream_t stream);
+
+/* y (rows x n) = x * rsqrt(mean(x^2) + eps) * w, statistics in fp32, one rounding to y_type.
+ * x_type SO101_F32 or SO101_BF16. Replaces kernels/norm.py:14-42 and model/smolvla.py:72-74. */
+SO101_API int so101_rms_norm(const void* x, int64_t ldx, int x_type, const float* w, void* y,
+                   int64_t ldy, int y_type, int64_t rows, int64_t n, float eps,
+                   cudaStream_t stream);
+
+/* LayerNorm (fp32 statistics, fp32 affine) of x (rows x n) fp32 into y_type (SO101_BF16 or
+ * SO101_I8 with y_qscale). shuffle > 1 writes the SmolVLM pixel shuffle of each image's
+ * tokens_per_image rows (model/smolvla.py:105-114) instead of row order. Replaces the
+ * F.layer_norm + pixel_shuffle of model/smolvla.py:174-175, 189. */
+SO101_API int so101_layer_norm(const float* x, int64_t ldx, const float* w, const float* b, void* y,
+                     int64_t ldy, int y_type, float y_qscale, int64_t rows, int64_t n, float eps,
+                     int shuffle, int64_t tokens_per_image, cudaStream_t stream);
+
+/* Rotate the key columns of fused qkv rows into k_out and copy the value columns into v_out
+ * (v_out may be NULL), fp32 rotation, bf16 store. Replaces kernels/rope.py:17-66.
+ * qkv: (rows, (nq + 2 nkv) hd) stride ldqkv; cos/sin: (rows, hd/2); batch strides in elements. */
+SO101_API int so101_rope_kv(const void* qkv, int64_t ldqkv, int nq, int nkv, int hd, const float* cos,
+                  const float* sin, void* k_out, int64_t ldk, void* v_out, int64_t ldv,
+                  int64_t rows, int batch, int64_t b_qkv, int64_t b_k, int64_t b_v,
+                  cudaStream_t stream);
+
+/* Camera frames to SigLIP patch rows: uint8 (n_img, h, w, 3) -> /255 -> bilinear resize
+ * (align_corners=False) to (rh, rw) -> zero pad on the left and top to S x S -> *2-1 -> patches
+ * (n_img * (S/P)^2, 3*P*P) in bf16 (or int8 with y_qscale). Replaces model/engine.py:236-245 and
+ * the patch unfold of model/smolvla.py:166-168. */
+SO101_API int so101_preprocess(const uint8_t* img, int n_img, int h, int w, int rh, int rw, int S, int P,
+                     void* patches, int y_type, float y_qscale, cudaStream_t stream);
+
+/* Dense fp32 linear on CUDA cores (the reference keeps these small MLPs fp32):
+ * y[m, n] = (act_in(x[m, :]) @ w[n, :]) + bias[n] (+ bias2[n]), act_in SiLU when silu_in.
+ * Replaces the fp32 F.linear calls of model/smolvla.py:282-285, 309 and engine.py:251. */
+SO101_API int so101_linear_f32(const float* x, int64_t ldx, const float* w, int64_t ldw, const float* bias,
+                     const float* bias2, float* y, int64_t ldy, int64_t M, int64_t N, int64_t K,
+                     int silu_in, cudaStream_t stream);
+
+/* The expert's output head and Euler step, per row m of e (M x K): x_t[m, :] += dt *
+ * (rms_norm(e[m], norm_w) @ w_out^T + b_out). Replaces model/smolvla.py:308-309 and
+ * engine.py:263-271 (x_t + dt * v_t). */
+SO101_API int so101_expert_out(const float* e, int64_t lde, const float* norm_w, float eps,
+                     const float* w_out, const float* b_out, float* x_t, int64_t ldx,
+                     int64_t M, int64_t N, int64_t K, float dt, cudaStream_t stream);
+
+/* Prefix tail rows per observation: lang rows copied from lang (lang_len x d) and the state row
+ * state_w @ pad((state - mean) / (std + 1e-8)) + state_b written at rows [tail_row, tail_row +
+ * lang_len] of each observation's prefix (stride prefix_rows rows of ldp). Replaces
+ * model/engine.py:247-252. */
+SO101_API int so101_prefix_tail(const float* state, int state_dim, const float* s_mean,
+                      const float* s_std, const float* state_w, int max_state,
+                      const float* state_b, const float* lang, int lang_len, int d,
+                      float* prefix, int64_t ldp, int64_t prefix_rows, int64_t tail_row,
+                      int batch, cudaStream_t stream);
+
+/* Undo the action representation and normalisation: x_t (batch, H, max_action) fp32 ->
+ * out (batch, H, action_dim). repr 0 absolute, 1 delta, 2 velocity (cumulative over H).
+ * Replaces model/engine.py:281-291. */
+SO101_API int so101_finish(const float* x_t, int max_action, const float* state, int state_dim,
+                 const float* s_mean, const float* s_std, const float* r_mean,
+                 const float* r_std, const float* a_mean, const float* a_std, float* out,
+                 int action_dim, int H, int repr, int batch, cudaStream_t stream);
+
+/* Per-tensor max |x| of a (rows x n) matrix (x_type SO101_F32 or SO101_BF16) folded into
+ * *amax with atomicMax (int8 calibration; tests/test_ov_engine.py:222-225 semantics). */
+SO101_API int so101_absmax(const void* x, int64_t ldx, int x_type, int64_t rows, int64_t n, float* amax,
+                 cudaStream_t stream);
+
+/* Per-output-channel symmetric int8 weights: w_q[n, k] = clamp(rint(w[n, k] / s[n]), -127, 127),
+ * s[n] = max(max_k |w[n, k]| / 127, 1e-8), from bf16 or fp32 w (model/trt_vision.py:131-133). */
+SO101_API int so101_quantize_weight(const void* w, int w_type, int64_t N, int64_t K, int8_t* w_q,
+                          float* scale, cudaStream_t stream);
+
+/* Device status word: 0, or the SO101_ERR_* a kernel recorded (bounded waits). Synchronous:
+ * reads a device variable. so101_clear_device_status resets it. */
+SO101_API int so101_device_status(void);
+SO101_API int so101_clear_device_status(void);
+
+/* Programmatic dependent launch for the GEMM kernels (0 off, default; 1 on): each GEMM may start
+ * streaming its weights while the previous kernel on the stream drains. */
+SO101_API int so101_set_pdl(int enable);
+
+/* Library version string and the compute capability it was built for ("sm_100a"). */
+SO101_API const char* so101_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* SO101_B200_H */

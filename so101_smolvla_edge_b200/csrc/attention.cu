@@ -1,0 +1,324 @@
+// Grouped-query flash attention for SigLIP (1024 tokens, no mask), the SmolLM2 prefix (prefix-LM
+// mask) and the action expert (self: prefix keys + causal own rows; cross: the expert's projections
+// of the prefix keys). One CTA = 64 query rows of one head (4 warps x 16 rows); K/V stream through
+// a double-buffered shared-memory ring of 64-key tiles (cp.async); S = Q K^T and O += P V on
+// mma.sync m16n8k16 bf16 with fp32 accumulators; softmax online in fp32 with exp2; P rounded to bf16
+// for PV, row sums from the fp32 P.
+//
+// Mask: key j is visible to query i iff j < Lk && (j < causal_from || j <= i + q_offset). Query
+// head h reads kv head h / (nq / nkv). RoPE rotates q as it is staged (per-operation rounding,
+// then one rounding to bf16).
+#include "common.cuh"
+
+namespace so101 {
+
+struct AttnArgs {
+  const __nv_bfloat16* q;
+  const __nv_bfloat16* k;
+  const __nv_bfloat16* v;
+  void* o;
+  long long ldq, ldk, ldv, ldo;
+  long long bq, bk, bv, bo;
+  int o_type;
+  float o_qscale;
+  int Lq, Lk, nq, nkv;
+  long long causal_from, q_offset;
+  const float* cos;
+  const float* sin;
+  float scale_log2;
+};
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
+__device__ __forceinline__ void mma_bf16_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, int bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+__device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+template <int HD>
+__global__ void __launch_bounds__(128) attention_kernel(const AttnArgs a) {
+  constexpr int BM = 64, BN = 64, LDS = HD + 8, HALF = HD / 2;
+  constexpr int CHUNKS = HD / 8;  // 16-byte chunks per row
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  __nv_bfloat16* sQ = reinterpret_cast<__nv_bfloat16*>(smem_raw);
+  __nv_bfloat16* sK = sQ + BM * LDS;          // [2][BN * LDS]
+  __nv_bfloat16* sV = sK + 2 * BN * LDS;      // [2][BN * LDS]
+
+  grid_dep_wait();
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int q0 = blockIdx.x * BM, h = blockIdx.y, bi = blockIdx.z;
+  const int kvh = h / (a.nq / a.nkv);
+  const __nv_bfloat16* Q = a.q + bi * a.bq + static_cast<long long>(h) * HD;
+  const __nv_bfloat16* K = a.k + bi * a.bk + static_cast<long long>(kvh) * HD;
+  const __nv_bfloat16* V = a.v + bi * a.bv + static_cast<long long>(kvh) * HD;
+
+  // last key any query of this block can see -> number of key tiles
+  long long last = a.causal_from - 1;
+  const long long diag = static_cast<long long>(q0 + BM - 1) + a.q_offset;
+  if (diag > last) last = diag;
+  if (last > a.Lk - 1) last = a.Lk - 1;
+  const int n_tiles = static_cast<int>((last + BN) / BN);
+
+  auto load_kv = [&](int tile, int buf) {
+    const int j0 = tile * BN;
+    for (int c = tid; c < BN * CHUNKS; c += 128) {
+      const int r = c / CHUNKS, cc = c % CHUNKS;
+      const int j = j0 + r;
+      const bool ok = j < a.Lk;
+      const long long jj = ok ? j : 0;
+      cp_async16(smem_u32(sK + buf * BN * LDS + r * LDS + cc * 8), K + jj * a.ldk + cc * 8, ok ? 16 : 0);
+      cp_async16(smem_u32(sV + buf * BN * LDS + r * LDS + cc * 8), V + jj * a.ldv + cc * 8, ok ? 16 : 0);
+    }
+    cp_async_commit();
+  };
+
+  load_kv(0, 0);
+
+  // stage Q (rotated) into shared memory
+  for (int idx = tid; idx < BM * HALF; idx += 128) {
+    const int r = idx / HALF, d = idx % HALF;
+    const int i = q0 + r;
+    float y1 = 0.f, y2 = 0.f;
+    if (i < a.Lq) {
+      const float x1 = __bfloat162float(Q[static_cast<long long>(i) * a.ldq + d]);
+      const float x2 = __bfloat162float(Q[static_cast<long long>(i) * a.ldq + d + HALF]);
+      if (a.cos) {
+        const float c = a.cos[static_cast<long long>(i) * HALF + d];
+        const float s = a.sin[static_cast<long long>(i) * HALF + d];
+        y1 = __fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, s));
+        y2 = __fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, s));
+      } else {
+        y1 = x1;
+        y2 = x2;
+      }
+    }
+    sQ[r * LDS + d] = __float2bfloat16_rn(y1);
+    sQ[r * LDS + d + HALF] = __float2bfloat16_rn(y2);
+  }
+  __syncthreads();
+
+  uint32_t qf[HD / 16][4];
+#pragma unroll
+  for (int kk = 0; kk < HD / 16; ++kk) {
+    const int row = warp * 16 + (lane & 15);
+    const int col = kk * 16 + (lane >> 4) * 8;
+    ldsm_x4(smem_u32(sQ + row * LDS + col), qf[kk][0], qf[kk][1], qf[kk][2], qf[kk][3]);
+  }
+
+  float o[HD / 8][4];
+#pragma unroll
+  for (int t = 0; t < HD / 8; ++t) o[t][0] = o[t][1] = o[t][2] = o[t][3] = 0.f;
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+  const int r0 = q0 + warp * 16 + (lane >> 2);  // this thread's two query rows
+  const int r1 = r0 + 8;
+
+  for (int tile = 0; tile < n_tiles; ++tile) {
+    const int buf = tile & 1;
+    if (tile + 1 < n_tiles) {
+      load_kv(tile + 1, buf ^ 1);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();
+    const __nv_bfloat16* k_s = sK + buf * BN * LDS;
+    const __nv_bfloat16* v_s = sV + buf * BN * LDS;
+
+    float s[BN / 8][4];
+#pragma unroll
+    for (int t = 0; t < BN / 8; ++t) s[t][0] = s[t][1] = s[t][2] = s[t][3] = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < HD / 16; ++kk) {
+#pragma unroll
+      for (int t2 = 0; t2 < BN / 16; ++t2) {
+        const int key = t2 * 16 + (lane & 7) + (lane >> 4) * 8;
+        const int col = kk * 16 + ((lane >> 3) & 1) * 8;
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4(smem_u32(k_s + key * LDS + col), b0, b1, b2, b3);
+        mma_bf16_16816(s[2 * t2], qf[kk], b0, b1);
+        mma_bf16_16816(s[2 * t2 + 1], qf[kk], b2, b3);
+      }
+    }
+    // scale, mask, row max
+    const int j0 = tile * BN;
+    float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+    for (int t = 0; t < BN / 8; ++t) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const long long j = j0 + t * 8 + (lane & 3) * 2 + (e & 1);
+        const long long i = e < 2 ? r0 : r1;
+        const bool vis = j < a.Lk && (j < a.causal_from || j <= i + a.q_offset);
+        const float x = vis ? s[t][e] * a.scale_log2 : -INFINITY;
+        s[t][e] = x;
+        if (e < 2)
+          mx0 = fmaxf(mx0, x);
+        else
+          mx1 = fmaxf(mx1, x);
+      }
+    }
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+    const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+    const float base0 = mn0 == -INFINITY ? 0.f : mn0;
+    const float base1 = mn1 == -INFINITY ? 0.f : mn1;
+    const float al0 = exp2f(m0 - base0), al1 = exp2f(m1 - base1);
+    m0 = mn0;
+    m1 = mn1;
+    float ps0 = 0.f, ps1 = 0.f;
+    uint32_t pf[BN / 16][4];
+#pragma unroll
+    for (int t = 0; t < BN / 8; ++t) {
+      const float p0 = exp2f(s[t][0] - base0), p1 = exp2f(s[t][1] - base0);
+      const float p2 = exp2f(s[t][2] - base1), p3 = exp2f(s[t][3] - base1);
+      ps0 += p0 + p1;
+      ps1 += p2 + p3;
+      pf[t / 2][(t & 1) * 2 + 0] = pack_bf16(p0, p1);
+      pf[t / 2][(t & 1) * 2 + 1] = pack_bf16(p2, p3);
+    }
+    l0 = l0 * al0 + ps0;
+    l1 = l1 * al1 + ps1;
+#pragma unroll
+    for (int t = 0; t < HD / 8; ++t) {
+      o[t][0] *= al0;
+      o[t][1] *= al0;
+      o[t][2] *= al1;
+      o[t][3] *= al1;
+    }
+    // O += P V
+#pragma unroll
+    for (int j = 0; j < BN / 16; ++j) {
+#pragma unroll
+      for (int t2 = 0; t2 < HD / 16; ++t2) {
+        const int key = j * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+        const int col = t2 * 16 + (lane >> 4) * 8;
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4_t(smem_u32(v_s + key * LDS + col), b0, b1, b2, b3);
+        mma_bf16_16816(o[2 * t2], pf[j], b0, b1);
+        mma_bf16_16816(o[2 * t2 + 1], pf[j], b2, b3);
+      }
+    }
+    __syncthreads();  // this buffer is refilled two tiles from now
+  }
+
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+  const float inv0 = 1.f / l0, inv1 = 1.f / l1;
+  const long long obase = bi * a.bo + static_cast<long long>(h) * HD;
+#pragma unroll
+  for (int t = 0; t < HD / 8; ++t) {
+    const int col = t * 8 + (lane & 3) * 2;
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      const int row = half ? r1 : r0;
+      if (row >= a.Lq) continue;
+      const float x0 = o[t][half * 2] * (half ? inv1 : inv0);
+      const float x1 = o[t][half * 2 + 1] * (half ? inv1 : inv0);
+      const long long off = obase + static_cast<long long>(row) * a.ldo + col;
+      if (a.o_type == SO101_BF16) {
+        *reinterpret_cast<__nv_bfloat162*>(static_cast<__nv_bfloat16*>(a.o) + off) = __floats2bfloat162_rn(x0, x1);
+      } else {
+        int8_t* p = static_cast<int8_t*>(a.o) + off;
+        p[0] = quant_i8(x0, a.o_qscale);
+        p[1] = quant_i8(x1, a.o_qscale);
+      }
+    }
+  }
+  grid_dep_launch();
+}
+
+template <int HD>
+int launch_attention(const AttnArgs& a, int batch, cudaStream_t stream) {
+  constexpr int smem = (64 * (HD + 8) + 4 * 64 * (HD + 8)) * 2;
+  static bool configured = false;
+  if (!configured) {
+    if (cudaFuncSetAttribute(attention_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+      return SO101_ERR_LAUNCH;
+    configured = true;
+  }
+  dim3 grid((a.Lq + 63) / 64, a.nq, batch);
+  attention_kernel<HD><<<grid, 128, smem, stream>>>(a);
+  return cudaGetLastError() == cudaSuccess ? SO101_OK : SO101_ERR_LAUNCH;
+}
+
+}  // namespace so101
+
+using namespace so101;
+
+extern "C" int so101_attention(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v, int64_t ldv,
+                               void* o, int64_t ldo, int o_type, float o_qscale, int64_t Lq, int64_t Lk, int nq,
+                               int nkv, int hd, int64_t causal_from, int64_t q_offset, const float* cos,
+                               const float* sin, int batch, int64_t bq, int64_t bk, int64_t bv, int64_t bo,
+                               cudaStream_t stream) {
+  if (!q || !k || !v || !o || Lq <= 0 || Lk <= 0 || nq <= 0 || nkv <= 0 || nq % nkv || batch <= 0) return SO101_ERR_ARG;
+  if (hd != 32 && hd != 64 && hd != 128) return SO101_ERR_ARG;
+  if ((cos == nullptr) != (sin == nullptr)) return SO101_ERR_ARG;
+  if (o_type != SO101_BF16 && o_type != SO101_I8) return SO101_ERR_ARG;
+  if (o_type == SO101_I8 && !(o_qscale > 0.f)) return SO101_ERR_ARG;
+  if (Lq > (1 << 30) || Lk > (1 << 30) || nq > 65535 || batch > 65535) return SO101_ERR_ARG;
+  // 16-byte cp.async rows: K/V bases (with the head offset) and row strides
+  if (reinterpret_cast<uintptr_t>(k) % 16 || reinterpret_cast<uintptr_t>(v) % 16 || (ldk * 2) % 16 ||
+      (ldv * 2) % 16 || (bk * 2) % 16 || (bv * 2) % 16)
+    return SO101_ERR_ARG;
+  if (reinterpret_cast<uintptr_t>(o) % 4 || ldo % 2 || bo % 2) return SO101_ERR_ARG;
+  AttnArgs a;
+  a.q = static_cast<const __nv_bfloat16*>(q);
+  a.k = static_cast<const __nv_bfloat16*>(k);
+  a.v = static_cast<const __nv_bfloat16*>(v);
+  a.o = o;
+  a.ldq = ldq;
+  a.ldk = ldk;
+  a.ldv = ldv;
+  a.ldo = ldo;
+  a.bq = bq;
+  a.bk = bk;
+  a.bv = bv;
+  a.bo = bo;
+  a.o_type = o_type;
+  a.o_qscale = o_qscale;
+  a.Lq = static_cast<int>(Lq);
+  a.Lk = static_cast<int>(Lk);
+  a.nq = nq;
+  a.nkv = nkv;
+  a.causal_from = causal_from;
+  a.q_offset = q_offset;
+  a.cos = cos;
+  a.sin = sin;
+  a.scale_log2 = static_cast<float>(1.4426950408889634 / sqrt(static_cast<double>(hd)));
+  switch (hd) {
+    case 32: return launch_attention<32>(a, batch, stream);
+    case 64: return launch_attention<64>(a, batch, stream);
+    default: return launch_attention<128>(a, batch, stream);
+  }
+}

@@ -1,0 +1,649 @@
+// tcgen05 GEMM for sm_100a: y = epilogue(x @ w^T), TMA-fed shared-memory ring, TMEM accumulator.
+//
+// One template serves every linear of the chunk:
+//   normal  (SWAP = false)  token rows on the 128-row MMA M side, features on MMA N (BN). For the
+//                           vision tower (M = 3072 per chunk) and batched prefix/expert.
+//   swap    (SWAP = true)   weight rows on the 128-row MMA M side, the few token rows (<= 64, the
+//                           action expert's 50) on MMA N. Weight streaming: each CTA streams a
+//                           128 x K slab of W once; the 50 rows never pad to 128.
+//   DUAL                    two weight tiles per stage (gate rows n and up rows N + n of the fused
+//                           [gate; up] matrix) into two accumulators; the epilogue multiplies
+//                           silu(gate) * up, so the SwiGLU never leaves the kernel.
+//   split-K                 grid.z splits K. Each split stores its fp32 (int32 for int8) partial
+//                           and takes a ticket; the last split to arrive sums all partials in
+//                           split order and runs the epilogue, then zeroes the ticket. Wait-free
+//                           and deterministic: a CUDA graph replay gives the same bits.
+//
+// Warp roles (128 threads): warp 0 lane 0 issues TMA, warp 1 lane 0 issues tcgen05.mma and owns
+// the TMEM allocation; all four warps run the epilogue, warp w reading TMEM lanes [32w, 32w+32).
+// Shared memory per stage: P tile(s) 128 x 128 B and Q tile(s) BN x 128 B, SWIZZLE_128B as TMA
+// writes them, which is the canonical K-major layout the MMA descriptors name.
+#include <cstdio>
+#include <mutex>
+
+#include "common.cuh"
+
+namespace so101 {
+
+struct GemmArgs {
+  int M, N, K;  // N: output features (half of w's rows for SILU_GATE)
+  int kb_total, kb_per_split, splits, tiles_q;
+  void* y;
+  long long ldy;
+  int y_type;
+  int epilogue;
+  const float* bias;
+  const void* res;
+  long long ldr;
+  int r_type;
+  long long r_period;
+  float out_scale;
+  const float* w_scale;
+  float x_scale;
+  float y_qscale;
+  long long row_group, row_stride;
+  void* ws;
+  int* tickets;
+  int vec_ok;
+  int* status;
+};
+
+__device__ __forceinline__ float load_elem(const void* p, long long i, int type) {
+  if (type == SO101_F32) return static_cast<const float*>(p)[i];
+  return __bfloat162float(static_cast<const __nv_bfloat16*>(p)[i]);
+}
+
+__device__ __forceinline__ void store_elem(void* p, long long i, int type, float v, float qs) {
+  if (type == SO101_F32)
+    static_cast<float*>(p)[i] = v;
+  else if (type == SO101_BF16)
+    static_cast<__nv_bfloat16*>(p)[i] = __float2bfloat16_rn(v);
+  else
+    static_cast<int8_t*>(p)[i] = quant_i8(v, qs);
+}
+
+// Epilogue of 16 accumulator values that share P index p and have Q indices [qb, qb + 16).
+template <bool SWAP, bool DUAL, bool I8>
+__device__ __forceinline__ void epilogue16(const GemmArgs& a, int p, int qb, float (&v)[16],
+                                           float (&u)[16]) {
+  if (!SWAP) {
+    // one output row m = p, 16 consecutive columns: vector path when fully inside and aligned
+    const int m = p;
+    if (m >= a.M) return;
+    const long long row = a.row_group > 0 ? (m / a.row_group) * a.row_stride + m % a.row_group : m;
+    const long long rrow = a.r_period > 0 ? m % a.r_period : row;
+    if (a.vec_ok && qb + 16 <= a.N) {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const int n = qb + j;
+        float x = v[j];
+        if (I8) x *= a.x_scale * __ldg(a.w_scale + n);
+        if (a.bias) x += __ldg(a.bias + n);
+        if (a.epilogue == SO101_EPI_GELU) {
+          x = gelu_tanh(x);
+        } else if (DUAL) {
+          float up = u[j];
+          if (I8) up *= a.x_scale * __ldg(a.w_scale + a.N + n);
+          x = silu(x) * up;
+        }
+        v[j] = x * a.out_scale;
+      }
+      if (a.res) {
+        if (a.r_type == SO101_F32) {
+          const float4* r4 = reinterpret_cast<const float4*>(static_cast<const float*>(a.res) +
+                                                             rrow * a.ldr + qb);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            float4 r = r4[j];
+            v[4 * j] += r.x;
+            v[4 * j + 1] += r.y;
+            v[4 * j + 2] += r.z;
+            v[4 * j + 3] += r.w;
+          }
+        } else {
+          const uint4* r4 = reinterpret_cast<const uint4*>(
+              static_cast<const __nv_bfloat16*>(a.res) + rrow * a.ldr + qb);
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            uint4 r = r4[j];
+            const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&r);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              float2 f = __bfloat1622float2(h[e]);
+              v[8 * j + 2 * e] += f.x;
+              v[8 * j + 2 * e + 1] += f.y;
+            }
+          }
+        }
+      }
+      if (a.y_type == SO101_F32) {
+        float4* y4 = reinterpret_cast<float4*>(static_cast<float*>(a.y) + row * a.ldy + qb);
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          y4[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+      } else if (a.y_type == SO101_BF16) {
+        uint4 o[2];
+        __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(o);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) h[e] = __floats2bfloat162_rn(v[2 * e], v[2 * e + 1]);
+        uint4* y4 = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.y) + row * a.ldy + qb);
+        y4[0] = o[0];
+        y4[1] = o[1];
+      } else {
+        uint4 o;
+        int8_t* b = reinterpret_cast<int8_t*>(&o);
+#pragma unroll
+        for (int e = 0; e < 16; ++e) b[e] = quant_i8(v[e], a.y_qscale);
+        *reinterpret_cast<uint4*>(static_cast<int8_t*>(a.y) + row * a.ldy + qb) = o;
+      }
+      return;
+    }
+  }
+#pragma unroll 4
+  for (int j = 0; j < 16; ++j) {
+    const int q = qb + j;
+    const int m = SWAP ? q : p;
+    const int n = SWAP ? p : q;
+    if (m >= a.M || n >= a.N) continue;
+    float x = v[j];
+    if (I8) x *= a.x_scale * __ldg(a.w_scale + n);
+    if (a.bias) x += __ldg(a.bias + n);
+    if (a.epilogue == SO101_EPI_GELU) {
+      x = gelu_tanh(x);
+    } else if (DUAL) {
+      float up = u[j];
+      if (I8) up *= a.x_scale * __ldg(a.w_scale + a.N + n);
+      x = silu(x) * up;
+    }
+    x *= a.out_scale;
+    const long long row = a.row_group > 0 ? (m / a.row_group) * a.row_stride + m % a.row_group : m;
+    if (a.res) {
+      const long long rrow = a.r_period > 0 ? m % a.r_period : row;
+      x += load_elem(a.res, rrow * a.ldr + n, a.r_type);
+    }
+    store_elem(a.y, row * a.ldy + n, a.y_type, x, a.y_qscale);
+  }
+}
+
+template <int BN, bool SWAP, bool DUAL, bool I8>
+__global__ void __launch_bounds__(128, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
+                   const GemmArgs a, const int stages) {
+  constexpr int NA = (SWAP && DUAL) ? 2 : 1;  // tiles on the MMA M side per stage
+  constexpr int NB = (!SWAP && DUAL) ? 2 : 1; // tiles on the MMA N side per stage
+  constexpr int A_BYTES = 128 * 128;
+  constexpr int B_BYTES = BN * 128;
+  constexpr int STAGE_BYTES = NA * A_BYTES + NB * B_BYTES;
+  constexpr int NACC = BN * (DUAL ? 2 : 1);
+  constexpr uint32_t TMEM_COLS = NACC <= 32 ? 32 : NACC <= 64 ? 64 : NACC <= 128 ? 128 : NACC <= 256 ? 256 : 512;
+  constexpr uint32_t IDESC = I8 ? idesc_i8(128, BN) : idesc_bf16(128, BN);
+  constexpr int KB_ELEMS = I8 ? 128 : 64;  // 128 bytes of K per stage
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + stages * STAGE_BYTES);
+  uint64_t* empty = full + stages;
+  uint64_t* accum = empty + stages;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
+  int* last_flag = reinterpret_cast<int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int q_tile = blockIdx.x, p_tile = blockIdx.y, split = blockIdx.z;
+  const int p0 = p_tile * 128, q0 = q_tile * BN;
+  const int kb0 = split * a.kb_per_split;
+  const int kb1 = min(kb0 + a.kb_per_split, a.kb_total);
+  const int nkb = kb1 - kb0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < stages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(accum, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0 && lane == 0) {
+    // ---------------- TMA producer: weights first (independent of the previous kernel), then
+    // wait for the previous grid before the first activation load.
+    tma_prefetch_desc(&tm_x);
+    tma_prefetch_desc(&tm_w);
+    const uint64_t pol_w = policy_evict_first();
+    const uint64_t pol_x = policy_evict_last();
+    bool waited = false;
+    for (int i = 0; i < nkb; ++i) {
+      const int s = i % stages;
+      const uint32_t round = static_cast<uint32_t>(i / stages);
+      if (i >= stages && !mbar_wait(&empty[s], (round - 1) & 1u, a.status)) break;
+      uint8_t* st = smem + s * STAGE_BYTES;
+      mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
+      const int kx = (kb0 + i) * KB_ELEMS;
+      // weight tiles
+      if (SWAP) {
+#pragma unroll
+        for (int t = 0; t < NA; ++t) tma_load_2d(st + t * A_BYTES, &tm_w, &full[s], kx, p0 + t * a.N, pol_w);
+      } else {
+#pragma unroll
+        for (int t = 0; t < NB; ++t)
+          tma_load_2d(st + NA * A_BYTES + t * B_BYTES, &tm_w, &full[s], kx, q0 + t * a.N, pol_w);
+      }
+      if (!waited) {
+        grid_dep_wait();
+        waited = true;
+      }
+      // activation tile
+      if (SWAP)
+        tma_load_2d(st + NA * A_BYTES, &tm_x, &full[s], kx, q0, pol_x);
+      else
+        tma_load_2d(st, &tm_x, &full[s], kx, p0, pol_x);
+    }
+    if (!waited) grid_dep_wait();
+  } else if (warp == 1 && lane == 0) {
+    // ---------------- MMA issuer
+    for (int i = 0; i < nkb; ++i) {
+      const int s = i % stages;
+      const uint32_t round = static_cast<uint32_t>(i / stages);
+      if (!mbar_wait(&full[s], round & 1u, a.status)) break;
+      tc_fence_after();
+      const uint32_t base = smem_u32(smem + s * STAGE_BYTES);
+      const uint64_t a0 = sw128_desc(base);
+      const uint64_t b0 = sw128_desc(base + NA * A_BYTES);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const uint32_t acc = (i > 0 || k > 0) ? 1u : 0u;
+        if (I8)
+          mma_i8(tmem, a0 + 2 * k, b0 + 2 * k, IDESC, acc);
+        else
+          mma_f16(tmem, a0 + 2 * k, b0 + 2 * k, IDESC, acc);
+        if (DUAL) {
+          const uint64_t a1 = SWAP ? sw128_desc(base + A_BYTES) : a0;
+          const uint64_t b1 = SWAP ? b0 : sw128_desc(base + NA * A_BYTES + B_BYTES);
+          if (I8)
+            mma_i8(tmem + BN, a1 + 2 * k, b1 + 2 * k, IDESC, acc);
+          else
+            mma_f16(tmem + BN, a1 + 2 * k, b1 + 2 * k, IDESC, acc);
+        }
+      }
+      mma_commit(&empty[s]);
+    }
+    mma_commit(accum);
+    grid_dep_wait();
+  } else {
+    grid_dep_wait();
+  }
+  __syncwarp();
+
+  // ---------------- epilogue: all 128 threads, thread t owns TMEM lane t (P index p0 + t)
+  mbar_wait(accum, 0, a.status);
+  tc_fence_after();
+  grid_dep_launch();
+  const int t = threadIdx.x;
+  const uint32_t lane_addr = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+  const int p = p0 + t;
+  float v[16], u[16];
+  if (a.splits == 1) {
+#pragma unroll 1
+    for (int c = 0; c < BN; c += 16) {
+      uint32_t r0[16], r1[16];
+      tmem_ld16(lane_addr + c, r0);
+      if (DUAL) tmem_ld16(lane_addr + BN + c, r1);
+      tmem_ld_wait();
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        v[j] = I8 ? static_cast<float>(static_cast<int>(r0[j])) : __uint_as_float(r0[j]);
+        u[j] = DUAL ? (I8 ? static_cast<float>(static_cast<int>(r1[j])) : __uint_as_float(r1[j])) : 0.f;
+      }
+      epilogue16<SWAP, DUAL, I8>(a, p, q0 + c, v, u);
+    }
+  } else {
+    const int tile = p_tile * a.tiles_q + q_tile;
+    uint32_t* ws = static_cast<uint32_t*>(a.ws);
+    uint32_t* part = ws + (static_cast<size_t>(tile) * a.splits + split) * NACC * 128;
+#pragma unroll 1
+    for (int c = 0; c < NACC; c += 16) {
+      uint32_t r[16];
+      tmem_ld16(lane_addr + c, r);
+      tmem_ld_wait();
+#pragma unroll
+      for (int j = 0; j < 16; ++j) __stcg(part + (c + j) * 128 + t, r[j]);
+    }
+    __threadfence();
+    __syncthreads();
+    if (t == 0) {
+      const int prev = atomicAdd(a.tickets + tile, 1);
+      *last_flag = (prev == a.splits - 1);
+    }
+    __syncthreads();
+    if (*last_flag) {
+      __threadfence();
+      const uint32_t* base = ws + static_cast<size_t>(tile) * a.splits * NACC * 128;
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 16) {
+        if (I8) {
+          int iv[16], iu[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) iv[j] = iu[j] = 0;
+          for (int s = 0; s < a.splits; ++s) {
+            const uint32_t* ps = base + static_cast<size_t>(s) * NACC * 128;
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              iv[j] += static_cast<int>(__ldcg(ps + (c + j) * 128 + t));
+              if (DUAL) iu[j] += static_cast<int>(__ldcg(ps + (BN + c + j) * 128 + t));
+            }
+          }
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            v[j] = static_cast<float>(iv[j]);
+            u[j] = static_cast<float>(iu[j]);
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) v[j] = u[j] = 0.f;
+          for (int s = 0; s < a.splits; ++s) {
+            const uint32_t* ps = base + static_cast<size_t>(s) * NACC * 128;
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              v[j] += __uint_as_float(__ldcg(ps + (c + j) * 128 + t));
+              if (DUAL) u[j] += __uint_as_float(__ldcg(ps + (BN + c + j) * 128 + t));
+            }
+          }
+        }
+        epilogue16<SWAP, DUAL, I8>(a, p, q0 + c, v, u);
+      }
+      if (t == 0) a.tickets[tile] = 0;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) tmem_dealloc(tmem, TMEM_COLS);
+}
+
+// ============================================================================ host side
+namespace {
+
+using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                              const cuuint64_t*, const cuuint32_t*, const cuuint32_t*,
+                              CUtensorMapInterleave, CUtensorMapSwizzle, CUtensorMapL2promotion,
+                              CUtensorMapFloatOOBfill);
+
+EncodeFn encode_fn() {
+  static EncodeFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeFn>(p);
+  });
+  return fn;
+}
+
+// 2-D K-major tensor map over rows x inner (elements), row stride ld elements, 128-byte boxes.
+int make_map(CUtensorMap* m, const void* ptr, bool i8, long long inner, long long rows, long long ld,
+             int box_rows) {
+  EncodeFn enc = encode_fn();
+  if (!enc) return SO101_ERR_DRIVER;
+  const int esize = i8 ? 1 : 2;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * esize};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(128 / esize), static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(m, i8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                   const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? SO101_OK : SO101_ERR_ARG;
+}
+
+int sm_count() {
+  int dev = 0, n = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n;
+}
+
+int stage_bytes(int bn, bool swap, bool dual) {
+  const int na = (swap && dual) ? 2 : 1, nb = (!swap && dual) ? 2 : 1;
+  return na * 128 * 128 + nb * bn * 128;
+}
+
+constexpr int kSmemBudget = 220 * 1024;
+
+struct Plan {
+  so101_gemm_config cfg;
+  int kb_total, kb_per_split, splits, tiles_p, tiles_q, nacc;
+};
+
+int ceil_div(long long a, long long b) { return static_cast<int>((a + b - 1) / b); }
+
+int plan_gemm(int a_type, long long M, long long N, long long K, int epi, const so101_gemm_config* in,
+              Plan* pl) {
+  const bool dual = epi == SO101_EPI_SILU_GATE;
+  const int kb_elems = a_type == SO101_I8 ? 128 : 64;
+  so101_gemm_config c = in ? *in : so101_gemm_config{0, 0, 0, 0};
+  so101_gemm_config pick;
+  so101_gemm_pick(a_type, M, N, K, epi, &pick);
+  if (!in || (c.bn == 0 && c.swap == 0 && c.splits == 0 && c.stages == 0)) c = pick;
+  if (c.bn == 0) c.bn = pick.bn;
+  if (c.splits <= 0) c.splits = 1;
+  if (c.swap) {
+    if (c.bn != 16 && c.bn != 32 && c.bn != 48 && c.bn != 64) return SO101_ERR_ARG;
+    if (a_type == SO101_I8) return SO101_ERR_ARG;
+  } else {
+    if (c.bn != 64 && c.bn != 128 && c.bn != 256) return SO101_ERR_ARG;
+    if (dual && c.bn == 256) return SO101_ERR_ARG;
+  }
+  const int sb = stage_bytes(c.bn, c.swap, dual);
+  const int max_st = (kSmemBudget - 1024 - 256) / sb;
+  if (c.stages <= 0) c.stages = max_st < 8 ? max_st : 8;
+  if (c.stages < 2 || c.stages > max_st) return SO101_ERR_ARG;
+  pl->kb_total = ceil_div(K, kb_elems);
+  int splits = c.splits > pl->kb_total ? pl->kb_total : c.splits;
+  pl->kb_per_split = ceil_div(pl->kb_total, splits);
+  pl->splits = ceil_div(pl->kb_total, pl->kb_per_split);  // no empty split
+  c.splits = pl->splits;
+  pl->tiles_p = c.swap ? ceil_div(N, 128) : ceil_div(M, 128);
+  pl->tiles_q = c.swap ? ceil_div(M, c.bn) : ceil_div(N, c.bn);
+  pl->nacc = c.bn * (dual ? 2 : 1);
+  pl->cfg = c;
+  return SO101_OK;
+}
+
+template <int BN, bool SWAP, bool DUAL, bool I8>
+int launch_inst(const CUtensorMap& tx, const CUtensorMap& tw, const GemmArgs& a, const Plan& pl,
+                cudaStream_t stream, bool pdl) {
+  auto kern = gemm_tc_kernel<BN, SWAP, DUAL, I8>;
+  const int smem = pl.cfg.stages * stage_bytes(BN, SWAP, DUAL) + 1024 + 256;
+  static int configured = 0;
+  if (configured < smem) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBudget) != cudaSuccess)
+      return SO101_ERR_LAUNCH;
+    configured = kSmemBudget;
+  }
+  cudaLaunchConfig_t lc = {};
+  lc.gridDim = dim3(pl.tiles_q, pl.tiles_p, pl.splits);
+  lc.blockDim = dim3(128, 1, 1);
+  lc.dynamicSmemBytes = smem;
+  lc.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  lc.attrs = attr;
+  lc.numAttrs = pdl ? 1 : 0;
+  cudaError_t e = cudaLaunchKernelEx(&lc, kern, tx, tw, a, pl.cfg.stages);
+  return e == cudaSuccess ? SO101_OK : SO101_ERR_LAUNCH;
+}
+
+template <bool SWAP, bool DUAL, bool I8>
+int launch_bn(const CUtensorMap& tx, const CUtensorMap& tw, const GemmArgs& a, const Plan& pl,
+              cudaStream_t stream, bool pdl) {
+  if constexpr (SWAP) {
+    switch (pl.cfg.bn) {
+      case 16: return launch_inst<16, SWAP, DUAL, I8>(tx, tw, a, pl, stream, pdl);
+      case 32: return launch_inst<32, SWAP, DUAL, I8>(tx, tw, a, pl, stream, pdl);
+      case 48: return launch_inst<48, SWAP, DUAL, I8>(tx, tw, a, pl, stream, pdl);
+      case 64: return launch_inst<64, SWAP, DUAL, I8>(tx, tw, a, pl, stream, pdl);
+    }
+  } else {
+    switch (pl.cfg.bn) {
+      case 64: return launch_inst<64, SWAP, DUAL, I8>(tx, tw, a, pl, stream, pdl);
+      case 128: return launch_inst<128, SWAP, DUAL, I8>(tx, tw, a, pl, stream, pdl);
+      case 256:
+        if constexpr (!DUAL) return launch_inst<256, SWAP, DUAL, I8>(tx, tw, a, pl, stream, pdl);
+        break;
+    }
+  }
+  return SO101_ERR_ARG;
+}
+
+bool g_pdl = false;
+
+}  // namespace
+}  // namespace so101
+
+using namespace so101;
+
+extern "C" int so101_set_pdl(int enable) {
+  g_pdl = enable != 0;
+  return SO101_OK;
+}
+
+extern "C" int so101_gemm_pick(int a_type, int64_t M, int64_t N, int64_t K, int epilogue,
+                               so101_gemm_config* cfg) {
+  if (!cfg) return SO101_ERR_ARG;
+  const bool dual = epilogue == SO101_EPI_SILU_GATE;
+  const int kb_elems = a_type == SO101_I8 ? 128 : 64;
+  const int kb = static_cast<int>((K + kb_elems - 1) / kb_elems);
+  const int sms = sm_count();
+  so101_gemm_config c = {0, 0, 1, 0};
+  if (M <= 64 && a_type == SO101_BF16) {
+    c.swap = 1;
+    c.bn = M <= 16 ? 16 : M <= 32 ? 32 : M <= 48 ? 48 : 64;
+    const int tiles = static_cast<int>((N + 127) / 128);
+    int s = sms / tiles;
+    const int max_s = kb / 2 > 0 ? kb / 2 : 1;  // at least two K blocks per split
+    c.splits = s < 1 ? 1 : (s > max_s ? max_s : s);
+  } else {
+    c.swap = 0;
+    c.bn = (N >= 1024 && !dual) ? 256 : 128;
+    if (N <= 128) c.bn = 64;
+    const long long tiles = ((M + 127) / 128) * ((N + c.bn - 1) / c.bn);
+    c.splits = 1;
+    if (tiles < sms / 2) {
+      int s = static_cast<int>(sms / tiles);
+      const int max_s = kb / 4 > 0 ? kb / 4 : 1;
+      c.splits = s > max_s ? max_s : s;
+    }
+  }
+  const int sb = stage_bytes(c.bn, c.swap, dual);
+  const int max_st = (kSmemBudget - 1024 - 256) / sb;
+  c.stages = max_st < 8 ? max_st : 8;
+  *cfg = c;
+  return SO101_OK;
+}
+
+extern "C" int so101_gemm_workspace(int a_type, int64_t M, int64_t N, int64_t K, int epilogue,
+                                    const so101_gemm_config* cfg, int64_t* workspace_bytes,
+                                    int64_t* n_tickets) {
+  Plan pl;
+  int rc = plan_gemm(a_type, M, N, K, epilogue, cfg, &pl);
+  if (rc) return rc;
+  const long long tiles = static_cast<long long>(pl.tiles_p) * pl.tiles_q;
+  if (workspace_bytes) *workspace_bytes = pl.splits > 1 ? tiles * pl.splits * pl.nacc * 128 * 4 : 0;
+  if (n_tickets) *n_tickets = pl.splits > 1 ? tiles : 0;
+  return SO101_OK;
+}
+
+extern "C" int so101_gemm(int a_type, const void* x, int64_t ldx, const void* w, int64_t ldw, void* y,
+                          int64_t ldy, int y_type, int64_t M, int64_t N, int64_t K,
+                          const so101_epilogue* epi, const so101_gemm_config* cfg, void* workspace,
+                          int64_t workspace_bytes, int* tickets, int64_t n_tickets, cudaStream_t stream) {
+  if (!x || !w || !y || !epi) return SO101_ERR_ARG;
+  if (a_type != SO101_BF16 && a_type != SO101_I8) return SO101_ERR_ARG;
+  if (M <= 0 || N <= 0 || K <= 0) return SO101_ERR_ARG;
+  if (M > (1LL << 30) || N > (1LL << 24) || K > (1LL << 24)) return SO101_ERR_ARG;
+  const int esize = a_type == SO101_I8 ? 1 : 2;
+  if ((K * esize) % 16 || (ldx * esize) % 16 || (ldw * esize) % 16) return SO101_ERR_ARG;
+  if (reinterpret_cast<uintptr_t>(x) % 16 || reinterpret_cast<uintptr_t>(w) % 16) return SO101_ERR_ARG;
+  if (ldx < K || ldw < K) return SO101_ERR_ARG;
+  if (y_type != SO101_BF16 && y_type != SO101_F32 && y_type != SO101_I8) return SO101_ERR_ARG;
+  const bool dual = epi->epilogue == SO101_EPI_SILU_GATE;
+  if (epi->epilogue < 0 || epi->epilogue > 2) return SO101_ERR_ARG;
+  if (a_type == SO101_I8 && !epi->w_scale) return SO101_ERR_ARG;
+  if (ldy < N && epi->row_group <= 0) return SO101_ERR_ARG;
+  Plan pl;
+  int rc = plan_gemm(a_type, M, N, K, epi->epilogue, cfg, &pl);
+  if (rc) return rc;
+  const long long tiles = static_cast<long long>(pl.tiles_p) * pl.tiles_q;
+  if (pl.splits > 1) {
+    if (!workspace || !tickets || n_tickets < tiles ||
+        workspace_bytes < tiles * pl.splits * pl.nacc * 128 * 4)
+      return SO101_ERR_WORKSPACE;
+  }
+  if (pl.tiles_q > 65535 || pl.tiles_p > 65535) return SO101_ERR_ARG;
+  GemmArgs a = {};
+  a.M = static_cast<int>(M);
+  a.N = static_cast<int>(N);
+  a.K = static_cast<int>(K);
+  a.kb_total = pl.kb_total;
+  a.kb_per_split = pl.kb_per_split;
+  a.splits = pl.splits;
+  a.tiles_q = pl.tiles_q;
+  a.y = y;
+  a.ldy = ldy;
+  a.y_type = y_type;
+  a.epilogue = epi->epilogue;
+  a.bias = epi->bias;
+  a.res = epi->residual;
+  a.ldr = epi->ldr;
+  a.r_type = epi->r_type;
+  a.r_period = epi->r_period;
+  a.out_scale = epi->out_scale == 0.f ? 1.f : epi->out_scale;
+  a.w_scale = epi->w_scale;
+  a.x_scale = epi->x_scale;
+  a.y_qscale = epi->y_qscale;
+  a.row_group = epi->row_group;
+  a.row_stride = epi->row_stride;
+  a.ws = workspace;
+  a.tickets = tickets;
+  a.status = status_ptr();
+  const int ysz = y_type == SO101_F32 ? 4 : y_type == SO101_BF16 ? 2 : 1;
+  bool vec = reinterpret_cast<uintptr_t>(y) % 16 == 0 && (ldy * ysz) % 16 == 0;
+  if (a.row_group > 0) vec = vec && (a.row_stride * ldy * ysz) % 16 == 0;
+  if (a.res) {
+    const int rsz = a.r_type == SO101_F32 ? 4 : 2;
+    vec = vec && reinterpret_cast<uintptr_t>(a.res) % 16 == 0 && (a.ldr * rsz) % 16 == 0;
+  }
+  a.vec_ok = vec ? 1 : 0;
+
+  const bool i8 = a_type == SO101_I8;
+  const long long w_rows = dual ? 2 * N : N;
+  CUtensorMap tx, tw;
+  const int x_box = pl.cfg.swap ? pl.cfg.bn : 128;
+  const int w_box = pl.cfg.swap ? 128 : pl.cfg.bn;
+  rc = make_map(&tx, x, i8, K, M, ldx, x_box);
+  if (rc) return rc;
+  rc = make_map(&tw, w, i8, K, w_rows, ldw, w_box);
+  if (rc) return rc;
+  const bool pdl = g_pdl;
+  if (pl.cfg.swap) {
+    if (dual) return launch_bn<true, true, false>(tx, tw, a, pl, stream, pdl);
+    return launch_bn<true, false, false>(tx, tw, a, pl, stream, pdl);
+  }
+  if (i8) {
+    if (dual) return SO101_ERR_ARG;
+    return launch_bn<false, false, true>(tx, tw, a, pl, stream, pdl);
+  }
+  if (dual) return launch_bn<false, true, false>(tx, tw, a, pl, stream, pdl);
+  return launch_bn<false, false, false>(tx, tw, a, pl, stream, pdl);
+}

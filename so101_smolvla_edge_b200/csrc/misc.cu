@@ -1,0 +1,292 @@
+// Small kernels around the GEMMs: frame preprocessing into patch rows, fp32 CUDA-core linears
+// (the reference keeps the action/time/state MLPs in fp32), the expert's output head fused with
+// the Euler step, the prefix tail rows (task tokens + state) and the unnormalisation.
+#include "common.cuh"
+
+namespace so101 {
+
+// ------------------------------------------------------------------ preprocess + patch unfold
+// One thread per output pair (2 features). Output row = img * G^2 + gy * G + gx, feature =
+// c * P * P + py * P + px; pixel (Y, X) = (gy * P + py, gx * P + px) of the padded S x S image.
+// Pixels left of S - rw or above S - rh are padding (0 -> -1 after *2-1); the rest are bilinear
+// samples (align_corners = False, source index clamped at 0) of the h x w frame scaled to
+// rh x rw.
+__device__ __forceinline__ float pixel(const uint8_t* __restrict__ img, int h, int w, int c, int yr, int xr,
+                                       float sh, float sw) {
+  float sy = sh * (static_cast<float>(yr) + 0.5f) - 0.5f;
+  float sx = sw * (static_cast<float>(xr) + 0.5f) - 0.5f;
+  sy = sy < 0.f ? 0.f : sy;
+  sx = sx < 0.f ? 0.f : sx;
+  const int y0 = static_cast<int>(sy), x0 = static_cast<int>(sx);
+  const int y1 = y0 < h - 1 ? y0 + 1 : y0, x1 = x0 < w - 1 ? x0 + 1 : x0;
+  const float ly = sy - static_cast<float>(y0), lx = sx - static_cast<float>(x0);
+  const float hy = 1.f - ly, hx = 1.f - lx;
+  const float v00 = static_cast<float>(img[(static_cast<long long>(y0) * w + x0) * 3 + c]) / 255.0f;
+  const float v01 = static_cast<float>(img[(static_cast<long long>(y0) * w + x1) * 3 + c]) / 255.0f;
+  const float v10 = static_cast<float>(img[(static_cast<long long>(y1) * w + x0) * 3 + c]) / 255.0f;
+  const float v11 = static_cast<float>(img[(static_cast<long long>(y1) * w + x1) * 3 + c]) / 255.0f;
+  return hy * (hx * v00 + lx * v01) + ly * (hx * v10 + lx * v11);
+}
+
+__global__ void preprocess_kernel(const uint8_t* __restrict__ img, int n_img, int h, int w, int rh, int rw,
+                                  int S, int P, void* __restrict__ out, int y_type, float qs) {
+  const int G = S / P, F = 3 * P * P;
+  const long long pairs = static_cast<long long>(n_img) * G * G * (F / 2);
+  const long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
+  if (i >= pairs) return;
+  const long long e = i * 2;
+  const long long row = e / F;
+  const int f0 = static_cast<int>(e % F);
+  const int im = static_cast<int>(row / (G * G));
+  const int pr = static_cast<int>(row % (G * G));
+  const int gy = pr / G, gx = pr % G;
+  const uint8_t* src = img + static_cast<long long>(im) * h * w * 3;
+  const float sh = static_cast<float>(h) / static_cast<float>(rh);
+  const float sw = static_cast<float>(w) / static_cast<float>(rw);
+  float v[2];
+#pragma unroll
+  for (int t = 0; t < 2; ++t) {
+    const int f = f0 + t;
+    const int c = f / (P * P), py = (f / P) % P, px = f % P;
+    const int Y = gy * P + py, X = gx * P + px;
+    const int yr = Y - (S - rh), xr = X - (S - rw);
+    float val = 0.f;
+    if (yr >= 0 && xr >= 0) {
+      if (rh == h && rw == w)
+        val = static_cast<float>(src[(static_cast<long long>(yr) * w + xr) * 3 + c]) / 255.0f;
+      else
+        val = pixel(src, h, w, c, yr, xr, sh, sw);
+    }
+    v[t] = val * 2.0f - 1.0f;
+  }
+  if (y_type == SO101_BF16) {
+    reinterpret_cast<__nv_bfloat162*>(out)[i] = __floats2bfloat162_rn(v[0], v[1]);
+  } else if (y_type == SO101_I8) {
+    int8_t* o = static_cast<int8_t*>(out) + e;
+    o[0] = quant_i8(v[0], qs);
+    o[1] = quant_i8(v[1], qs);
+  } else {
+    float* o = static_cast<float*>(out) + e;
+    o[0] = v[0];
+    o[1] = v[1];
+  }
+}
+
+// ------------------------------------------------------------------ fp32 linear (CUDA cores)
+// 32 x 32 output tile per 128-thread block, each thread 2 rows x 4 columns, K in chunks of 32.
+constexpr int LF_BM = 32, LF_BN = 32, LF_BK = 32;
+
+__global__ void __launch_bounds__(128) linear_f32_kernel(const float* __restrict__ x, long long ldx,
+                                                         const float* __restrict__ w, long long ldw,
+                                                         const float* __restrict__ bias,
+                                                         const float* __restrict__ bias2, float* __restrict__ y,
+                                                         long long ldy, int M, int N, int K, int silu_in) {
+  grid_dep_wait();
+  __shared__ float xs[LF_BK][LF_BM + 1];
+  __shared__ float ws[LF_BK][LF_BN + 1];
+  const int m0 = blockIdx.y * LF_BM, n0 = blockIdx.x * LF_BN;
+  const int tx = threadIdx.x % 8, ty = threadIdx.x / 8;  // 8 column groups x 16 row groups
+  float acc[2][4] = {};
+  for (int k0 = 0; k0 < K; k0 += LF_BK) {
+    for (int i = threadIdx.x; i < LF_BM * LF_BK; i += 128) {
+      const int r = i / LF_BK, kk = i % LF_BK;
+      float v = 0.f;
+      if (m0 + r < M && k0 + kk < K) {
+        v = x[static_cast<long long>(m0 + r) * ldx + k0 + kk];
+        if (silu_in) v = silu(v);
+      }
+      xs[kk][r] = v;
+      const int c = i / LF_BK;
+      ws[kk][c] = (n0 + c < N && k0 + kk < K) ? w[static_cast<long long>(n0 + c) * ldw + k0 + kk] : 0.f;
+    }
+    __syncthreads();
+#pragma unroll 8
+    for (int kk = 0; kk < LF_BK; ++kk) {
+      const float a0 = xs[kk][ty * 2], a1 = xs[kk][ty * 2 + 1];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float b = ws[kk][tx * 4 + j];
+        acc[0][j] = fmaf(a0, b, acc[0][j]);
+        acc[1][j] = fmaf(a1, b, acc[1][j]);
+      }
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const int m = m0 + ty * 2 + i;
+    if (m >= M) continue;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int n = n0 + tx * 4 + j;
+      if (n >= N) continue;
+      float v = acc[i][j];
+      if (bias) v += bias[n];
+      if (bias2) v += bias2[n];
+      y[static_cast<long long>(m) * ldy + n] = v;
+    }
+  }
+  grid_dep_launch();
+}
+
+// ------------------------------------------------------------------ expert head + Euler step
+// One block per row m: h = rms_norm(e[m]) in shared memory, then each warp computes output
+// columns n = warp, warp + 8, ... as warp-reduced dot products; x_t[m, n] += dt * (h . w_n + b_n).
+__global__ void expert_out_kernel(const float* __restrict__ e, long long lde, const float* __restrict__ norm_w,
+                                  float eps, const float* __restrict__ w_out, const float* __restrict__ b_out,
+                                  float* __restrict__ x_t, long long ldx, int N, int K, float dt) {
+  grid_dep_wait();
+  extern __shared__ float h[];
+  __shared__ float red[32];
+  const long long m = blockIdx.x;
+  const float* row = e + m * lde;
+  float ss = 0.f;
+  for (int k = threadIdx.x; k < K; k += blockDim.x) {
+    const float v = row[k];
+    h[k] = v;
+    ss += v * v;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float t = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+    if (threadIdx.x == 0) red[0] = rsqrtf(t / static_cast<float>(K) + eps);
+  }
+  __syncthreads();
+  const float rstd = red[0];
+  for (int k = threadIdx.x; k < K; k += blockDim.x) h[k] = (h[k] * rstd) * norm_w[k];
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  for (int n = warp; n < N; n += nw) {
+    const float* wr = w_out + static_cast<long long>(n) * K;
+    float acc = 0.f;
+    for (int k = lane; k < K; k += 32) acc = fmaf(h[k], wr[k], acc);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (lane == 0) x_t[m * ldx + n] += dt * (acc + b_out[n]);
+  }
+  grid_dep_launch();
+}
+
+// ------------------------------------------------------------------ prefix tail rows
+// block b: lang rows copied, then the state row from the normalised, zero-padded state.
+__global__ void prefix_tail_kernel(const float* __restrict__ state, int state_dim, const float* __restrict__ s_mean,
+                                   const float* __restrict__ s_std, const float* __restrict__ state_w, int max_state,
+                                   const float* __restrict__ state_b, const float* __restrict__ lang, int lang_len,
+                                   int d, float* __restrict__ prefix, long long ldp, long long prefix_rows,
+                                   long long tail_row) {
+  extern __shared__ float st[];
+  const int b = blockIdx.x;
+  float* base = prefix + (static_cast<long long>(b) * prefix_rows + tail_row) * ldp;
+  for (int i = threadIdx.x; i < lang_len * d; i += blockDim.x) base[(i / d) * ldp + i % d] = lang[i];
+  for (int j = threadIdx.x; j < max_state; j += blockDim.x)
+    st[j] = j < state_dim ? (state[b * state_dim + j] - s_mean[j]) / (s_std[j] + 1e-8f) : 0.f;
+  __syncthreads();
+  float* srow = base + static_cast<long long>(lang_len) * ldp;
+  for (int n = threadIdx.x; n < d; n += blockDim.x) {
+    float acc = 0.f;
+    for (int j = 0; j < max_state; ++j) acc = fmaf(st[j], state_w[static_cast<long long>(n) * max_state + j], acc);
+    srow[n] = acc + state_b[n];
+  }
+}
+
+// ------------------------------------------------------------------ unnormalisation
+__global__ void finish_kernel(const float* __restrict__ x_t, int max_action, const float* __restrict__ state,
+                              int state_dim, const float* __restrict__ s_mean, const float* __restrict__ s_std,
+                              const float* __restrict__ r_mean, const float* __restrict__ r_std,
+                              const float* __restrict__ a_mean, const float* __restrict__ a_std,
+                              float* __restrict__ out, int action_dim, int H, int repr) {
+  grid_dep_wait();
+  const int b = blockIdx.x, col = threadIdx.x;
+  if (col >= action_dim) return;
+  const float* x = x_t + static_cast<long long>(b) * H * max_action;
+  float st = 0.f;
+  if (repr != 0 && col < state_dim) st = (state[b * state_dim + col] - s_mean[col]) / (s_std[col] + 1e-8f);
+  float run = 0.f;
+  for (int i = 0; i < H; ++i) {
+    float a = x[i * max_action + col];
+    if (repr != 0) {
+      a = a * r_std[col] + r_mean[col];
+      if (repr == 1) {
+        a = a + st;
+      } else {
+        run += a;
+        a = st + run;
+      }
+    }
+    out[(static_cast<long long>(b) * H + i) * action_dim + col] = a * a_std[col] + a_mean[col];
+  }
+}
+
+}  // namespace so101
+
+using namespace so101;
+
+namespace {
+int launched() { return cudaGetLastError() == cudaSuccess ? SO101_OK : SO101_ERR_LAUNCH; }
+}  // namespace
+
+extern "C" int so101_preprocess(const uint8_t* img, int n_img, int h, int w, int rh, int rw, int S, int P,
+                                void* patches, int y_type, float y_qscale, cudaStream_t stream) {
+  if (!img || !patches || n_img <= 0 || h <= 0 || w <= 0 || P <= 0 || S % P) return SO101_ERR_ARG;
+  if (rh <= 0 || rw <= 0 || rh > S || rw > S || (3 * P * P) % 2) return SO101_ERR_ARG;
+  if (y_type == SO101_I8 && !(y_qscale > 0.f)) return SO101_ERR_ARG;
+  const long long G = S / P;
+  const long long pairs = n_img * G * G * (3 * P * P / 2);
+  const long long blocks = (pairs + 255) / 256;
+  if (blocks > 0x7fffffffLL) return SO101_ERR_ARG;
+  preprocess_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(img, n_img, h, w, rh, rw, S, P, patches,
+                                                                        y_type, y_qscale);
+  return launched();
+}
+
+extern "C" int so101_linear_f32(const float* x, int64_t ldx, const float* w, int64_t ldw, const float* bias,
+                                const float* bias2, float* y, int64_t ldy, int64_t M, int64_t N, int64_t K,
+                                int silu_in, cudaStream_t stream) {
+  if (!x || !w || !y || M <= 0 || N <= 0 || K <= 0 || ldx < K || ldw < K || ldy < N) return SO101_ERR_ARG;
+  const long long gy = (M + LF_BM - 1) / LF_BM, gx = (N + LF_BN - 1) / LF_BN;
+  if (gy > 65535 || gx > 0x7fffffffLL) return SO101_ERR_ARG;
+  linear_f32_kernel<<<dim3(static_cast<unsigned>(gx), static_cast<unsigned>(gy)), 128, 0, stream>>>(
+      x, ldx, w, ldw, bias, bias2, y, ldy, static_cast<int>(M), static_cast<int>(N), static_cast<int>(K), silu_in);
+  return launched();
+}
+
+extern "C" int so101_expert_out(const float* e, int64_t lde, const float* norm_w, float eps, const float* w_out,
+                                const float* b_out, float* x_t, int64_t ldx, int64_t M, int64_t N, int64_t K,
+                                float dt, cudaStream_t stream) {
+  if (!e || !norm_w || !w_out || !b_out || !x_t || M <= 0 || N <= 0 || K <= 0 || K > 8192) return SO101_ERR_ARG;
+  if (M > 0x7fffffffLL) return SO101_ERR_ARG;
+  expert_out_kernel<<<static_cast<unsigned>(M), 256, K * sizeof(float), stream>>>(
+      e, lde, norm_w, eps, w_out, b_out, x_t, ldx, static_cast<int>(N), static_cast<int>(K), dt);
+  return launched();
+}
+
+extern "C" int so101_prefix_tail(const float* state, int state_dim, const float* s_mean, const float* s_std,
+                                 const float* state_w, int max_state, const float* state_b, const float* lang,
+                                 int lang_len, int d, float* prefix, int64_t ldp, int64_t prefix_rows,
+                                 int64_t tail_row, int batch, cudaStream_t stream) {
+  if (!state || !s_mean || !s_std || !state_w || !state_b || !prefix || batch <= 0 || d <= 0) return SO101_ERR_ARG;
+  if (lang_len > 0 && !lang) return SO101_ERR_ARG;
+  if (state_dim > max_state || max_state <= 0 || max_state > 4096) return SO101_ERR_ARG;
+  prefix_tail_kernel<<<batch, 256, max_state * sizeof(float), stream>>>(state, state_dim, s_mean, s_std, state_w,
+                                                                         max_state, state_b, lang, lang_len, d,
+                                                                         prefix, ldp, prefix_rows, tail_row);
+  return launched();
+}
+
+extern "C" int so101_finish(const float* x_t, int max_action, const float* state, int state_dim,
+                            const float* s_mean, const float* s_std, const float* r_mean, const float* r_std,
+                            const float* a_mean, const float* a_std, float* out, int action_dim, int H, int repr,
+                            int batch, cudaStream_t stream) {
+  if (!x_t || !state || !s_mean || !s_std || !r_mean || !r_std || !a_mean || !a_std || !out) return SO101_ERR_ARG;
+  if (batch <= 0 || H <= 0 || action_dim <= 0 || action_dim > max_action || action_dim > 1024) return SO101_ERR_ARG;
+  if (repr < 0 || repr > 2) return SO101_ERR_ARG;
+  finish_kernel<<<batch, ((action_dim + 31) / 32) * 32, 0, stream>>>(x_t, max_action, state, state_dim, s_mean,
+                                                                       s_std, r_mean, r_std, a_mean, a_std, out,
+                                                                       action_dim, H, repr);
+  return launched();
+}

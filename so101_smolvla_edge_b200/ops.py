@@ -1,0 +1,289 @@
+"""The kernels as torch-tensor operators, with the reference's operator API.
+
+    linear     kernels/gemm.py:350-398        y = x @ w.T with fused bias / residual / SiLU gate
+                                              (+ GELU, int8 operands, row remap for the engine)
+    attention  kernels/attention.py:110-153   GQA over the kv heads, RoPE on q, computed mask
+    rope_kv    kernels/rope.py:481-506        RoPE on the keys + K/V cache write
+    rms_norm   kernels/norm.py:423-440        fp32 statistics, one rounding
+
+Every call goes through the C ABI of libso101_b200.so on the tensors' current CUDA stream.
+Preconditions the kernels cannot meet raise ValueError, as the reference's wrappers do.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+
+import torch
+
+from . import _lib as L
+
+DTYPE = {torch.bfloat16: L.BF16, torch.float32: L.F32, torch.int8: L.I8}
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _stream(dev: torch.device) -> int:
+    return torch.cuda.current_stream(dev).cuda_stream
+
+
+def _cuda(*ts: torch.Tensor | None) -> None:
+    for t in ts:
+        if t is not None and t.device.type != "cuda":
+            raise ValueError("the B200 kernels take CUDA tensors only")
+
+
+class Workspace:
+    """Split-K partials and tickets for one device. Every GEMM on the device's stream shares it
+    (they run one after another); it must exist before a CUDA graph is captured, as the
+    reference's split-K counters must (kernels/gemm.py:335-347)."""
+
+    def __init__(self, device: torch.device, nbytes: int = 64 << 20, n_tickets: int = 1 << 16):
+        self.partials = torch.empty(nbytes // 4, dtype=torch.float32, device=device)
+        self.tickets = torch.zeros(n_tickets, dtype=torch.int32, device=device)
+
+    @property
+    def nbytes(self) -> int:
+        return self.partials.numel() * 4
+
+
+_WS: dict[torch.device, Workspace] = {}
+
+
+def workspace(device: torch.device | str) -> Workspace:
+    device = torch.device(device)
+    if device.index is None:
+        device = torch.device("cuda", torch.cuda.current_device())
+    ws = _WS.get(device)
+    if ws is None:
+        ws = _WS[device] = Workspace(device)
+    return ws
+
+
+def gemm_config(m: int, n: int, k: int, *, silu_gate=False, int8=False) -> tuple[int, int, int, int]:
+    """(swap, bn, splits, stages) the library picks for this problem."""
+    cfg = L.GemmConfig()
+    epi = L.EPI_SILU_GATE if silu_gate else L.EPI_NONE
+    L.check(L.lib().so101_gemm_pick(L.I8 if int8 else L.BF16, m, n, k, epi, C.byref(cfg)), "gemm_pick")
+    return cfg.as_tuple()
+
+
+def linear(
+    x: torch.Tensor,
+    w: torch.Tensor,
+    *,
+    bias: torch.Tensor | None = None,
+    residual: torch.Tensor | None = None,
+    silu_gate: bool = False,
+    gelu: bool = False,
+    out_dtype: torch.dtype | None = None,
+    out: torch.Tensor | None = None,
+    config: tuple[int, int, int, int] | None = None,
+    out_scale: float = 1.0,
+    residual_period: int = 0,
+    x_scale: float | None = None,
+    w_scale: torch.Tensor | None = None,
+    y_qscale: float | None = None,
+) -> torch.Tensor:
+    """Compute x (..., K) @ w (N, K).T with a fused epilogue on tcgen05.
+
+    With `silu_gate`, w is (2F, K) = [gate; up] and the result (..., F). `residual` (..., N) is
+    added in float32 and the result takes its dtype unless `out_dtype` says otherwise; `out` may
+    be the residual itself. A float32 x is rounded to bf16 first, as `SmolVLA.lin` casts it.
+    int8 operands: x and w int8 with `x_scale` (per tensor) and `w_scale` (N,) dequantizing the
+    int32 accumulator. out_dtype int8 quantizes the result by `y_qscale`.
+    """
+    _cuda(x, w, bias, residual, out)
+    if silu_gate and (residual is not None or bias is not None or gelu):
+        raise ValueError("silu_gate takes neither a residual, a bias nor gelu")
+    k = x.shape[-1]
+    int8 = w.dtype == torch.int8
+    if int8:
+        if x.dtype != torch.int8 or w_scale is None or x_scale is None:
+            raise ValueError("int8 weights need int8 x, x_scale and w_scale")
+    elif x.dtype != torch.bfloat16:
+        x = x.to(torch.bfloat16)
+    if w.dtype not in (torch.bfloat16, torch.int8):
+        raise ValueError(f"w must be bf16 or int8, not {w.dtype}")
+    x2 = x.reshape(-1, k)
+    if x2.stride(-1) != 1 or w.stride(-1) != 1:
+        raise ValueError("x and w need unit column stride")
+    m = x2.shape[0]
+    n = w.shape[0] // 2 if silu_gate else w.shape[0]
+    if w.shape[1] != k:
+        raise ValueError(f"x has {k} features, w {tuple(w.shape)}")
+    if out_dtype is None:
+        out_dtype = residual.dtype if residual is not None else (
+            torch.bfloat16 if int8 else w.dtype)  # fmt: skip
+    y = out.view(m, n) if out is not None else torch.empty(m, n, dtype=out_dtype, device=x.device)
+    r2 = None
+    if residual is not None:
+        r2 = residual.reshape(-1, n) if residual_period == 0 else residual
+        if r2.stride(-1) != 1:
+            raise ValueError("residual needs unit column stride")
+    epi = L.Epilogue(
+        epilogue=L.EPI_SILU_GATE if silu_gate else (L.EPI_GELU if gelu else L.EPI_NONE),
+        bias=_ptr(bias), residual=_ptr(r2), ldr=r2.stride(0) if r2 is not None else 0,
+        r_type=DTYPE[r2.dtype] if r2 is not None else 0, r_period=residual_period,
+        out_scale=out_scale, w_scale=_ptr(w_scale), x_scale=x_scale or 0.0,
+        y_qscale=y_qscale or 0.0, row_group=0, row_stride=0,
+    )  # fmt: skip
+    cfg = None
+    if config is not None:
+        cfg = L.GemmConfig(*config)
+    ws = workspace(x.device)
+    rc = L.lib().so101_gemm(
+        L.I8 if int8 else L.BF16, x2.data_ptr(), x2.stride(0), w.data_ptr(), w.stride(0),
+        y.data_ptr(), y.stride(0), DTYPE[y.dtype], m, n, k, C.byref(epi),
+        C.byref(cfg) if cfg is not None else None, ws.partials.data_ptr(), ws.nbytes,
+        ws.tickets.data_ptr(), ws.tickets.numel(), _stream(x.device),
+    )  # fmt: skip
+    L.check(rc, "so101_gemm")
+    return y.view(*x.shape[:-1], n)
+
+
+def attention(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    n_heads: int,
+    n_kv: int,
+    *,
+    cos: torch.Tensor | None = None,
+    sin: torch.Tensor | None = None,
+    causal_from: int | None = None,
+    q_offset: int = 0,
+    out: torch.Tensor | None = None,
+    out_dtype: torch.dtype = torch.bfloat16,
+    out_qscale: float | None = None,
+) -> torch.Tensor:
+    """Attention of q's heads over k and v, written as (Lq, n_heads * hd).
+
+    q is (Lq, >= n_heads * hd) with head h in columns [h * hd, (h + 1) * hd) and any row stride,
+    so it can be a slice of the fused qkv output; k and v are (Lk, n_kv * hd). A leading batch
+    dimension on all three runs independent problems. cos and sin (Lq, hd / 2) rotate q; None
+    means no RoPE. Key j is visible to query i iff j < causal_from or j <= i + q_offset; None
+    means every key is visible.
+    """
+    _cuda(q, k, v, out)
+    batched = q.dim() == 3
+    qb, kb, vb = (q, k, v) if batched else (q[None], k[None], v[None])
+    bsz, lq, lk = qb.shape[0], qb.shape[1], kb.shape[1]
+    hd = kb.shape[2] // n_kv
+    for name, t in (("q", qb), ("k", kb), ("v", vb)):
+        if t.stride(-1) != 1:
+            raise ValueError(f"{name} needs unit column stride, has {t.stride()}")
+        if t.dtype != torch.bfloat16:
+            raise ValueError(f"{name} must be bf16")
+    if out is None:
+        out = torch.empty(bsz, lq, n_heads * hd, dtype=out_dtype, device=q.device)
+    ob = out if out.dim() == 3 else out[None]
+    if cos is not None:
+        cos = cos.reshape(lq, hd // 2).float().contiguous()
+        sin = sin.reshape(lq, hd // 2).float().contiguous()
+    ck = lk if causal_from is None else causal_from
+    rc = L.lib().so101_attention(
+        qb.data_ptr(), qb.stride(1), kb.data_ptr(), kb.stride(1), vb.data_ptr(), vb.stride(1),
+        ob.data_ptr(), ob.stride(1), DTYPE[ob.dtype], out_qscale or 0.0, lq, lk, n_heads, n_kv, hd,
+        ck, q_offset, _ptr(cos), _ptr(sin), bsz, qb.stride(0), kb.stride(0), vb.stride(0),
+        ob.stride(0), _stream(q.device),
+    )  # fmt: skip
+    L.check(rc, "so101_attention")
+    return out
+
+
+def rope_kv(
+    qkv: torch.Tensor,
+    n_heads: int,
+    n_kv: int,
+    cos: torch.Tensor,
+    sin: torch.Tensor,
+    k_out: torch.Tensor,
+    v_out: torch.Tensor | None = None,
+) -> None:
+    """Rotate the key columns of qkv into k_out and copy its value columns into v_out.
+
+    qkv is (R, (n_heads + 2 * n_kv) * hd), k_out and v_out (R, n_kv * hd) and may be row slices
+    of a larger cache, cos and sin (R, hd / 2).
+    """
+    _cuda(qkv, k_out, v_out)
+    r = qkv.shape[0]
+    hd = qkv.shape[1] // (n_heads + 2 * n_kv)
+    for name, t in (("qkv", qkv), ("k_out", k_out), ("v_out", v_out)):
+        if t is not None and t.stride(-1) != 1:
+            raise ValueError(f"{name} needs unit column stride")
+    cos = cos.reshape(r, hd // 2).float().contiguous()
+    sin = sin.reshape(r, hd // 2).float().contiguous()
+    rc = L.lib().so101_rope_kv(
+        qkv.data_ptr(), qkv.stride(0), n_heads, n_kv, hd, cos.data_ptr(), sin.data_ptr(),
+        k_out.data_ptr(), k_out.stride(0), _ptr(v_out), v_out.stride(0) if v_out is not None else 0,
+        r, 1, 0, 0, 0, _stream(qkv.device),
+    )  # fmt: skip
+    L.check(rc, "so101_rope_kv")
+
+
+def rms_norm(
+    x: torch.Tensor,
+    w: torch.Tensor,
+    eps: float,
+    out_dtype: torch.dtype = torch.bfloat16,
+    out: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """Normalize x (..., N), float32 or bf16, by w (N,) into `out_dtype`."""
+    _cuda(x, w, out)
+    n = x.shape[-1]
+    x2 = x.reshape(-1, n)
+    if x2.stride(-1) != 1:
+        x2 = x2.contiguous()
+    y = out if out is not None else torch.empty(x2.shape, dtype=out_dtype, device=x.device)
+    w = w.float().contiguous()
+    rc = L.lib().so101_rms_norm(
+        x2.data_ptr(), x2.stride(0), DTYPE[x2.dtype], w.data_ptr(), y.data_ptr(), y.stride(0),
+        DTYPE[y.dtype], x2.shape[0], n, eps, _stream(x.device),
+    )  # fmt: skip
+    L.check(rc, "so101_rms_norm")
+    return y.view(*x.shape[:-1], n)
+
+
+def layer_norm(x, w, b, eps, out_dtype=torch.bfloat16, out_qscale=None, shuffle=1,
+               tokens_per_image=0, out=None):  # fmt: skip
+    """LayerNorm of float32 rows (+ the SmolVLM pixel shuffle of each image's tokens)."""
+    _cuda(x, w, b, out)
+    n = x.shape[-1]
+    x2 = x.reshape(-1, n)
+    rows = x2.shape[0]
+    if out is None:
+        shape = (rows // shuffle**2, n * shuffle**2) if shuffle > 1 else (rows, n)
+        out = torch.empty(shape, dtype=out_dtype, device=x.device)
+    rc = L.lib().so101_layer_norm(
+        x2.data_ptr(), x2.stride(0), w.data_ptr(), b.data_ptr(), out.data_ptr(), out.stride(0),
+        DTYPE[out.dtype], out_qscale or 0.0, rows, n, eps, shuffle, tokens_per_image,
+        _stream(x.device),
+    )  # fmt: skip
+    L.check(rc, "so101_layer_norm")
+    return out
+
+
+def quantize_weight(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """Per-output-channel symmetric int8 (w_q, scale) of a float32 or bf16 (N, K) matrix."""
+    _cuda(w)
+    w = w.contiguous()
+    n, k = w.shape
+    wq = torch.empty(n, k, dtype=torch.int8, device=w.device)
+    s = torch.empty(n, dtype=torch.float32, device=w.device)
+    rc = L.lib().so101_quantize_weight(w.data_ptr(), DTYPE[w.dtype], n, k, wq.data_ptr(),
+                                       s.data_ptr(), _stream(w.device))  # fmt: skip
+    L.check(rc, "so101_quantize_weight")
+    return wq, s
+
+
+def device_status() -> int:
+    return L.lib().so101_device_status()
+
+
+def set_pdl(enable: bool) -> None:
+    """Launch GEMMs with programmatic dependent launch (they start streaming weights while the
+    previous kernel on the stream drains)."""
+    L.check(L.lib().so101_set_pdl(1 if enable else 0), "so101_set_pdl")

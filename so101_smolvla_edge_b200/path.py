@@ -1,0 +1,475 @@
+"""The chunk on the B200 kernels: vision tower, prefix pass and denoising loop as fixed launch lists.
+
+`B200Path` replaces the reference's two backend seams with one object:
+
+    TritonPath (pkg/model/smolvla_triton.py:46-130)   prefix pass + velocity on custom kernels
+    TrtVision  (pkg/model/trt_vision.py:212-252)      vision stage in fixed buffers, bf16 or int8
+
+It owns every buffer the chunk touches (weights, activations, the expert's K/V caches at the kv
+heads in token-major (len, n_kv * hd) layout, split-K workspace) and builds three `Program`s —
+vision, prefix, denoise — each a list of C-ABI launches with their arguments fixed once. Running a
+program issues the launches on the current stream; capturing the three into one CUDA graph is the
+engine's chunk. Batch B runs B independent observations through the same launches (GEMMs over
+all B's rows at once, attention per observation).
+
+Layout (B observations, C cameras, Np patches per camera, L prefix rows, H action rows):
+    img      (B*C, h, w, 3) u8       patches (B*C*Np, 3 P^2)     xv  (B*C*Np, vis_dim) fp32
+    prefix   (B*L, text_dim) fp32 residual stream of the prefix pass
+    ck/cv[i] (B, L+H, kv) bf16 self layers: rows [:L] VLM keys/values, rows [L:] this step's own
+    kx/vx[i] (B, L, kv) bf16 cross layers: the expert's projections of the VLM keys/values
+    x_t      (B*H, max_action) fp32, e (B*H, exp_dim) fp32 expert residual stream
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+import math
+
+import numpy as np
+import torch
+
+from . import _lib as L
+from .bundle import Bundle
+from .ops import DTYPE, workspace
+from .spec import ModelSpec, vision_linear_names
+
+REPRS = {"absolute": 0, "delta": 1, "velocity": 2}
+
+
+def unsupported(spec: ModelSpec) -> str | None:
+    """Why the B200 kernels cannot run this model, or None."""
+    hd_v = spec.vis_dim // max(spec.vis_heads, 1)
+    if spec.head_dim not in (32, 64, 128):
+        return f"head_dim {spec.head_dim} is not 32, 64 or 128"
+    if spec.vis_dim % spec.vis_heads or hd_v not in (32, 64, 128):
+        return f"vision head size {hd_v} is not 32, 64 or 128"
+    if spec.n_heads % spec.n_kv:
+        return "n_heads is not a multiple of n_kv"
+    ks = {"vis_dim": spec.vis_dim, "patch features": 3 * spec.patch**2, "vis_mlp": spec.vis_mlp,
+          "connector": spec.vis_dim * spec.shuffle**2, "text_dim": spec.text_dim,
+          "q heads": spec.q_dim, "text_mlp": spec.text_mlp, "kv": spec.kv_dim,
+          "exp_dim": spec.exp_dim, "exp_mlp": spec.exp_mlp}  # fmt: skip
+    for name, k in ks.items():
+        if k % 16:
+            return f"{name} width {k} is not a multiple of 16 (TMA rows of 16-byte multiples)"
+    for name, n in (("vis_dim", spec.vis_dim), ("text_dim", spec.text_dim), ("exp_dim", spec.exp_dim)):
+        if n > 1024:
+            return f"{name} {n} is wider than the row kernels' 1024"
+    g = spec.grid
+    if spec.image_size % spec.patch or g % spec.shuffle:
+        return "the patch grid does not divide by the shuffle factor"
+    return None
+
+
+class Program:
+    """A fixed list of C-ABI launches; `run` issues them on a stream."""
+
+    def __init__(self, name: str):
+        self.name = name
+        self.calls: list[tuple[str, object, tuple]] = []
+        self._keep: list[object] = []
+
+    def add(self, what: str, fn, *args, keep=()) -> None:
+        self.calls.append((what, fn, args))
+        self._keep.extend(keep)
+
+    def run(self, stream: int) -> None:
+        for what, fn, args in self.calls:
+            rc = fn(*args, stream)
+            if rc:
+                L.check(rc, f"{self.name}/{what}")
+
+    def __len__(self) -> int:
+        return len(self.calls)
+
+
+def _rope(pos: torch.Tensor, hd: int, base: float) -> tuple[torch.Tensor, torch.Tensor]:
+    """cos/sin (len, hd/2) in float32 exactly as the reference builds them
+    (pkg/model/smolvla.py:77-85), on the host."""
+    half = hd // 2
+    exps = (2.0 / hd) * torch.arange(half, dtype=torch.float32)
+    ang = pos.float()[:, None] / (base**exps)[None, :]
+    return torch.cos(ang), torch.sin(ang)
+
+
+def _time_proj(s: ModelSpec, w_time: np.ndarray, b: np.ndarray) -> torch.Tensor:
+    """Time half of action_time_mlp_in for every step, bias included (pkg/model/engine.py:137-141)."""
+    dt = -1.0 / s.n_steps
+    t = torch.tensor([1.0 + k * dt for k in range(s.n_steps)], dtype=torch.float32).double()
+    frac = torch.linspace(0.0, 1.0, s.exp_dim // 2, dtype=torch.float64)
+    period = s.min_period * (s.max_period / s.min_period) ** frac
+    ang = t[:, None] * (2 * math.pi / period)[None, :]
+    temb = torch.cat([torch.sin(ang), torch.cos(ang)], dim=-1).float()
+    return temb @ torch.from_numpy(w_time).T + torch.from_numpy(b)
+
+
+class B200Path:
+    """Weights, buffers and launch programs of one chunk (or B chunks) on one GPU."""
+
+    def __init__(self, bundle: Bundle, device: torch.device, batch: int = 1,
+                 vision_precision: str = "bf16", act_clip: dict[str, float] | None = None):  # fmt: skip
+        s = self.spec = bundle.spec
+        why = unsupported(s)
+        if why:
+            raise ValueError(f"the B200 kernels cannot run this model: {why}")
+        if vision_precision not in ("bf16", "int8"):
+            raise ValueError(f"vision precision must be 'bf16' or 'int8', not {vision_precision!r}")
+        if vision_precision == "int8" and not act_clip:
+            raise ValueError("int8 vision needs activation clips (act_clip)")
+        self.bundle, self.meta = bundle, bundle.meta
+        self.dev = device
+        self.B = B = int(batch)
+        self.lib = L.lib()
+        self.int8 = vision_precision == "int8"
+        self.clip = dict(act_clip or {})
+        if self.int8:
+            bad = set(self.clip) - set(vision_linear_names(s))
+            if bad:
+                raise ValueError(f"act_clip names no vision linear: {sorted(bad)[:4]}")
+        self.C, self.Np, self.L, self.H = s.n_cams, s.n_patches, s.prefix_len, s.chunk
+        self.h_img, self.w_img = bundle.meta["image_hw"]
+        self.state_dim, self.action_dim = bundle.meta["state_dim"], bundle.meta["action_dim"]
+        self.repr = REPRS[bundle.meta["action_repr"]]
+        self.ws = workspace(device)  # split-K partials and tickets exist before any capture
+        self._amax: tuple[torch.Tensor, dict[str, int]] | None = None  # calibration hooks
+        self._upload(bundle)
+        self._alloc()
+        self.progs = {"vision": Program("vision"), "prefix": Program("prefix"),
+                      "denoise": Program("denoise")}  # fmt: skip
+        self._build_vision(self.progs["vision"])
+        self._build_prefix(self.progs["prefix"])
+        self._build_denoise(self.progs["denoise"])
+
+    # ------------------------------------------------------------------ weights and buffers
+    def _upload(self, b: Bundle) -> None:
+        s, dev = self.spec, self.dev
+        t = b.tensors
+        from .spec import param_shapes
+
+        self.w: dict[str, torch.Tensor] = {}
+        for name, (_, kind) in param_shapes(s).items():
+            arr = torch.from_numpy(np.ascontiguousarray(t[name]))
+            self.w[name] = arr.to(dev, torch.bfloat16 if kind == "w" else torch.float32).contiguous()
+        for name in ("lang.emb", "norm.state.mean", "norm.state.std", "norm.action.mean",
+                     "norm.action.std"):  # fmt: skip
+            self.w[name] = torch.from_numpy(np.ascontiguousarray(t[name])).to(dev).float()
+        for name, n in (("repr.mean", 0.0), ("repr.std", 1.0)):
+            v = t.get(name)
+            v = np.full(s.max_action, n, np.float32) if v is None else v
+            self.w[name] = torch.from_numpy(np.ascontiguousarray(v)).to(dev).float()
+        # act.in and time_in's action half are consecutive linear maps of x_t: fold them once
+        w_a = t["act.time_in.w_action"].astype(np.float64)
+        self.w["act.ain.w"] = torch.from_numpy((w_a @ t["act.in.w"].astype(np.float64)).astype(np.float32)).to(dev)
+        self.w["act.ain.b"] = torch.from_numpy((w_a @ t["act.in.b"].astype(np.float64)).astype(np.float32)).to(dev)
+        self.w["time_proj"] = _time_proj(s, t["act.time_in.w_time"], t["act.time_in.b"]).to(dev).contiguous()
+        L_, H, hd = s.prefix_len, s.chunk, s.head_dim
+        for key, pos in (("p", torch.arange(L_)), ("s", torch.arange(L_, L_ + H)), ("c", torch.arange(H))):
+            c, sn = _rope(pos, hd, s.rope_wavelength)
+            self.w[f"cos_{key}"], self.w[f"sin_{key}"] = c.to(dev), sn.to(dev)
+        self.wq: dict[str, tuple[torch.Tensor, torch.Tensor]] = {}
+        if self.int8:
+            stream = torch.cuda.current_stream(dev).cuda_stream
+            for q in self.clip:
+                wname = "vis.patch.w" if q == "patch" else ("conn.w" if q == "conn" else q + ".w")
+                wf = torch.from_numpy(np.ascontiguousarray(t[wname])).to(dev).float().contiguous()
+                n, k = wf.shape
+                wq = torch.empty(n, k, dtype=torch.int8, device=dev)
+                sc = torch.empty(n, dtype=torch.float32, device=dev)
+                L.check(self.lib.so101_quantize_weight(wf.data_ptr(), L.F32, n, k, wq.data_ptr(),
+                                                       sc.data_ptr(), stream), "quantize_weight")  # fmt: skip
+                self.wq[q] = (wq, sc)
+            torch.cuda.synchronize(dev)
+
+    def _alloc(self) -> None:
+        s, dev, B = self.spec, self.dev, self.B
+        C_, Np, L_, H = self.C, self.Np, self.L, self.H
+        bf, f32, i8 = torch.bfloat16, torch.float32, torch.int8
+        rows_v = B * C_ * Np
+        vd, sh = s.vis_dim, s.shuffle
+        qdt = lambda name: i8 if (self.int8 and name in self.clip) else bf  # noqa: E731
+
+        def z(*shape, dtype=f32):
+            return torch.zeros(*shape, dtype=dtype, device=dev)
+
+        self.img = z(B * C_, self.h_img, self.w_img, 3, dtype=torch.uint8)
+        self.state = z(B, self.state_dim)
+        self.noise = z(B, H, s.max_action)  # x_t: the noise, denoised in place
+        self.out = z(B, H, self.action_dim)
+        # vision
+        self.patches = z(rows_v, 3 * s.patch**2, dtype=qdt("patch"))
+        self.xv = z(rows_v, vd)
+        self.hv_bf = z(rows_v, vd, dtype=bf)
+        self.hv_i8 = z(rows_v, vd, dtype=i8) if self.int8 else None
+        self.qkv_v = z(rows_v, 3 * vd, dtype=bf)
+        self.attn_v_bf = z(rows_v, vd, dtype=bf)
+        self.attn_v_i8 = z(rows_v, vd, dtype=i8) if self.int8 else None
+        self.mlp_v_bf = z(rows_v, s.vis_mlp, dtype=bf)
+        self.mlp_v_i8 = z(rows_v, s.vis_mlp, dtype=i8) if self.int8 else None
+        self.shuf = z(rows_v // sh**2, vd * sh**2, dtype=qdt("conn"))
+        # prefix
+        self.prefix = z(B * L_, s.text_dim)
+        self.h_t = z(B * L_, s.text_dim, dtype=bf)
+        self.qkv_t = z(B * L_, s.qkv_dim, dtype=bf)
+        self.attn_t = z(B * L_, s.q_dim, dtype=bf)
+        self.mlp_t = z(B * L_, s.text_mlp, dtype=bf)
+        kv = s.kv_dim
+        layers = range(s.n_layers)
+        self.ck = [z(B, L_ + H, kv, dtype=bf) if s.is_self_attn(i) else None for i in layers]
+        self.cv = [z(B, L_ + H, kv, dtype=bf) if s.is_self_attn(i) else None for i in layers]
+        self.kx = [None if s.is_self_attn(i) else z(B, L_, kv, dtype=bf) for i in layers]
+        self.vx = [None if s.is_self_attn(i) else z(B, L_, kv, dtype=bf) for i in layers]
+        self.k_scratch = z(B * L_, kv, dtype=bf)
+        # expert
+        self.h0 = z(B * H, s.exp_dim)
+        self.e = z(B * H, s.exp_dim)
+        self.h_e = z(B * H, s.exp_dim, dtype=bf)
+        self.qkv_e = z(B * H, s.qkv_dim, dtype=bf)
+        self.attn_e = z(B * H, s.q_dim, dtype=bf)
+        self.mlp_e = z(B * H, s.exp_mlp, dtype=bf)
+        self.v_buf = z(B * H, s.max_action)
+
+    # ------------------------------------------------------------------ launch helpers
+    def _gemm(self, prog: Program, what: str, x: torch.Tensor, w: torch.Tensor, y: torch.Tensor, *,
+              bias=None, residual=None, r_period=0, gate=False, gelu=False, out_scale=1.0,
+              row_map=(0, 0), x_scale=0.0, w_scale=None, y_qscale=0.0, M=None) -> None:  # fmt: skip
+        m = x.shape[0] if M is None else M
+        k = x.shape[1]
+        n = w.shape[0] // 2 if gate else w.shape[0]
+        a_type = L.I8 if w.dtype == torch.int8 else L.BF16
+        epi = L.Epilogue(
+            epilogue=L.EPI_SILU_GATE if gate else (L.EPI_GELU if gelu else L.EPI_NONE),
+            bias=None if bias is None else bias.data_ptr(),
+            residual=None if residual is None else residual.data_ptr(),
+            ldr=0 if residual is None else residual.stride(0),
+            r_type=0 if residual is None else DTYPE[residual.dtype], r_period=r_period,
+            out_scale=out_scale, w_scale=None if w_scale is None else w_scale.data_ptr(),
+            x_scale=x_scale, y_qscale=y_qscale, row_group=row_map[0], row_stride=row_map[1],
+        )  # fmt: skip
+        need, tick = C.c_int64(), C.c_int64()
+        L.check(self.lib.so101_gemm_workspace(a_type, m, n, k, epi.epilogue, None, C.byref(need),
+                                              C.byref(tick)), what)  # fmt: skip
+        if need.value > self.ws.nbytes or tick.value > self.ws.tickets.numel():
+            raise RuntimeError(f"{what}: split-K workspace too small ({need.value} bytes)")
+        prog.add(what, self.lib.so101_gemm, a_type, x.data_ptr(), x.stride(0), w.data_ptr(),
+                 w.stride(0), y.data_ptr(), y.stride(0), DTYPE[y.dtype], m, n, k, C.byref(epi),
+                 None, self.ws.partials.data_ptr(), self.ws.nbytes, self.ws.tickets.data_ptr(),
+                 self.ws.tickets.numel(), keep=(epi,))  # fmt: skip
+
+    def _attn(self, prog, what, q, ldq, bq, k, ldk, bk, v, ldv, bv, o, ldo, bo, *, Lq, Lk, nq, nkv,
+              hd, causal_from, q_offset=0, cos=None, sin=None, batch=1, o_qscale=0.0):  # fmt: skip
+        o_type = L.I8 if o.dtype == torch.int8 else L.BF16
+        prog.add(what, self.lib.so101_attention, q, ldq, k, ldk, v, ldv, o.data_ptr() if
+                 isinstance(o, torch.Tensor) else o, ldo, o_type, o_qscale, Lq, Lk, nq, nkv, hd,
+                 causal_from, q_offset, None if cos is None else cos.data_ptr(),
+                 None if sin is None else sin.data_ptr(), batch, bq, bk, bv, bo)  # fmt: skip
+
+    def _rms(self, prog, what, x, w, y, rows):
+        s = self.spec
+        prog.add(what, self.lib.so101_rms_norm, x.data_ptr(), x.stride(0), DTYPE[x.dtype], w.data_ptr(),
+                 y.data_ptr(), y.stride(0), DTYPE[y.dtype], rows, x.shape[1], s.rms_eps)  # fmt: skip
+
+    def _qs(self, name: str) -> float:
+        """Per-tensor int8 scale of linear `name`'s input (0 when it stays bf16)."""
+        return self.clip[name] / 127.0 if (self.int8 and name in self.clip) else 0.0
+
+    # ------------------------------------------------------------------ vision
+    def _build_vision(self, p: Program) -> None:
+        s, w = self.spec, self.w
+        B, C_, Np = self.B, self.C, self.Np
+        S = s.image_size
+        h, wd = self.h_img, self.w_img
+        ratio = max(wd / S, h / S)
+        rh, rw = int(h / ratio), int(wd / ratio)
+        vd, nh = s.vis_dim, s.vis_heads
+        hd = vd // nh
+        rows_v = B * C_ * Np
+        qs = self._qs("patch")
+        p.add("preprocess", self.lib.so101_preprocess, self.img.data_ptr(), B * C_, h, wd, rh, rw, S,
+              s.patch, self.patches.data_ptr(), DTYPE[self.patches.dtype], qs)  # fmt: skip
+        self._lin(p, "patch", self.patches, "vis.patch.w", self.xv, bias=w["vis.patch.b"],
+                  residual=w["vis.pos"], r_period=Np)  # fmt: skip
+        for i in range(s.vis_layers):
+            pre = f"vis.{i}."
+            hv = self._vis_in(pre + "qkv", self.hv_bf, self.hv_i8)
+            p.add(f"{i}.ln1", self.lib.so101_layer_norm, self.xv.data_ptr(), vd, w[pre + "ln1.w"].data_ptr(),
+                  w[pre + "ln1.b"].data_ptr(), hv.data_ptr(), vd, DTYPE[hv.dtype], self._qs(pre + "qkv"),
+                  rows_v, vd, s.vis_eps, 1, 0)  # fmt: skip
+            self._lin(p, pre + "qkv", hv, pre + "qkv.w", self.qkv_v, bias=w[pre + "qkv.b"])
+            av = self._vis_in(pre + "out", self.attn_v_bf, self.attn_v_i8)
+            base = self.qkv_v.data_ptr()
+            self._attn(p, f"{i}.attn", base, 3 * vd, Np * 3 * vd, base + 2 * vd, 3 * vd, Np * 3 * vd,
+                       base + 4 * vd, 3 * vd, Np * 3 * vd, av, vd, Np * vd, Lq=Np, Lk=Np, nq=nh,
+                       nkv=nh, hd=hd, causal_from=Np, batch=B * C_,
+                       o_qscale=self._qs(pre + "out"))  # fmt: skip
+            self._lin(p, pre + "out", av, pre + "out.w", self.xv, bias=w[pre + "out.b"], residual=self.xv)
+            hv = self._vis_in(pre + "fc1", self.hv_bf, self.hv_i8)
+            p.add(f"{i}.ln2", self.lib.so101_layer_norm, self.xv.data_ptr(), vd, w[pre + "ln2.w"].data_ptr(),
+                  w[pre + "ln2.b"].data_ptr(), hv.data_ptr(), vd, DTYPE[hv.dtype], self._qs(pre + "fc1"),
+                  rows_v, vd, s.vis_eps, 1, 0)  # fmt: skip
+            mv = self._vis_in(pre + "fc2", self.mlp_v_bf, self.mlp_v_i8)
+            self._lin(p, pre + "fc1", hv, pre + "fc1.w", mv, bias=w[pre + "fc1.b"], gelu=True,
+                      y_qscale=self._qs(pre + "fc2"))  # fmt: skip
+            self._lin(p, pre + "fc2", mv, pre + "fc2.w", self.xv, bias=w[pre + "fc2.b"], residual=self.xv)
+        p.add("post_ln+shuffle", self.lib.so101_layer_norm, self.xv.data_ptr(), vd,
+              w["vis.post_ln.w"].data_ptr(), w["vis.post_ln.b"].data_ptr(), self.shuf.data_ptr(),
+              self.shuf.stride(0), DTYPE[self.shuf.dtype], self._qs("conn"), rows_v, vd, s.vis_eps,
+              s.shuffle, Np)  # fmt: skip
+        self._lin(p, "conn", self.shuf, "conn.w", self.prefix, out_scale=math.sqrt(s.text_dim),
+                  row_map=(C_ * s.img_tokens, self.L))  # fmt: skip
+
+    def _vis_in(self, name: str, bf: torch.Tensor, i8: torch.Tensor | None) -> torch.Tensor:
+        return i8 if (self.int8 and name in self.clip) else bf
+
+    def _lin(self, p: Program, q: str, x, wname: str, y, **kw) -> None:
+        """A vision linear: int8 operands when `q` has a clip, else bf16."""
+        if self._amax is not None:  # calibration: fold max |x| of this linear's input
+            amax, idx = self._amax
+            p.add(f"amax {q}", self.lib.so101_absmax, x.data_ptr(), x.stride(0), DTYPE[x.dtype],
+                  x.shape[0], x.shape[1], amax.data_ptr() + 4 * idx[q])  # fmt: skip
+        if self.int8 and q in self.clip:
+            wq, ws = self.wq[q]
+            self._gemm(p, q, x, wq, y, x_scale=self.clip[q] / 127.0, w_scale=ws, **kw)
+        else:
+            self._gemm(p, q, x, self.w[wname], y, **kw)
+
+    # ------------------------------------------------------------------ prefix
+    def _build_prefix(self, p: Program) -> None:
+        s, w = self.spec, self.w
+        B, L_, H = self.B, self.L, self.H
+        nq, nk, hd, kv, qd = s.n_heads, s.n_kv, s.head_dim, s.kv_dim, s.qkv_dim
+        tail = self.C * s.img_tokens
+        p.add("prefix_tail", self.lib.so101_prefix_tail, self.state.data_ptr(), self.state_dim,
+              w["norm.state.mean"].data_ptr(), w["norm.state.std"].data_ptr(), w["state.w"].data_ptr(),
+              s.max_state, w["state.b"].data_ptr(), w["lang.emb"].data_ptr(), s.lang_len, s.text_dim,
+              self.prefix.data_ptr(), s.text_dim, L_, tail, B)  # fmt: skip
+        x = self.prefix
+        esz = 2  # bf16 bytes
+        for i in range(s.n_layers):
+            t = f"txt.{i}."
+            self._rms(p, f"{i}.ln_in", x, w[t + "ln_in"], self.h_t, B * L_)
+            self._gemm(p, f"{i}.qkv", self.h_t, w[t + "qkv"], self.qkv_t)
+            qkv_ptr = self.qkv_t.data_ptr()
+            if s.is_self_attn(i):
+                k_ptr, v_ptr = self.ck[i].data_ptr(), self.cv[i].data_ptr()
+                bk = (L_ + H) * kv
+                p.add(f"{i}.rope_kv", self.lib.so101_rope_kv, qkv_ptr, qd, nq, nk, hd,
+                      w["cos_p"].data_ptr(), w["sin_p"].data_ptr(), k_ptr, kv, v_ptr, kv, L_, B,
+                      L_ * qd, bk, bk)  # fmt: skip
+                ldk = ldv = kv
+                bv = bk
+            else:
+                k_ptr = self.k_scratch.data_ptr()
+                p.add(f"{i}.rope_k", self.lib.so101_rope_kv, qkv_ptr, qd, nq, nk, hd,
+                      w["cos_p"].data_ptr(), w["sin_p"].data_ptr(), k_ptr, kv, None, 0, L_, B,
+                      L_ * qd, L_ * kv, 0)  # fmt: skip
+                self._gemm(p, f"{i}.exp_k", self.k_scratch, w[f"exp.{i}.k"], self.kx[i].view(B * L_, kv))
+                v_view = self.qkv_t[:, (nq + nk) * hd:]
+                self._gemm(p, f"{i}.exp_v", v_view, w[f"exp.{i}.v"], self.vx[i].view(B * L_, kv))
+                v_ptr = qkv_ptr + (nq + nk) * hd * esz
+                ldk, bk, ldv, bv = kv, L_ * kv, qd, L_ * qd
+            if i == s.n_layers - 1:
+                break  # the last layer's output is never read
+            self._attn(p, f"{i}.attn", qkv_ptr, qd, L_ * qd, k_ptr, ldk, bk, v_ptr, ldv, bv, self.attn_t,
+                       s.q_dim, L_ * s.q_dim, Lq=L_, Lk=L_, nq=nq, nkv=nk, hd=hd, causal_from=L_ - 1,
+                       cos=w["cos_p"], sin=w["sin_p"], batch=B)  # fmt: skip
+            self._gemm(p, f"{i}.o", self.attn_t, w[t + "o"], x, residual=x)
+            self._rms(p, f"{i}.ln_post", x, w[t + "ln_post"], self.h_t, B * L_)
+            self._gemm(p, f"{i}.gate_up", self.h_t, w[t + "gate_up"], self.mlp_t, gate=True)
+            self._gemm(p, f"{i}.down", self.mlp_t, w[t + "down"], x, residual=x)
+
+    # ------------------------------------------------------------------ denoising
+    def _build_step(self, p: Program, k: int, x_in: torch.Tensor, x_out: torch.Tensor, dt: float) -> None:
+        """One velocity evaluation at step k, folded into x_out += dt * v."""
+        s, w = self.spec, self.w
+        B, L_, H = self.B, self.L, self.H
+        nq, nk, hd, kv, qd = s.n_heads, s.n_kv, s.head_dim, s.kv_dim, s.qkv_dim
+        M = B * H
+        tp = w["time_proj"][k]
+        p.add(f"s{k}.act_time_in", self.lib.so101_linear_f32, x_in.data_ptr(), s.max_action,
+              w["act.ain.w"].data_ptr(), s.max_action, w["act.ain.b"].data_ptr(), tp.data_ptr(),
+              self.h0.data_ptr(), s.exp_dim, M, s.exp_dim, s.max_action, 0)  # fmt: skip
+        p.add(f"s{k}.time_out", self.lib.so101_linear_f32, self.h0.data_ptr(), s.exp_dim,
+              w["act.time_out.w"].data_ptr(), s.exp_dim, w["act.time_out.b"].data_ptr(), None,
+              self.e.data_ptr(), s.exp_dim, M, s.exp_dim, s.exp_dim, 1)  # fmt: skip
+        e = self.e
+        for i in range(s.n_layers):
+            pre = f"exp.{i}."
+            self._rms(p, f"s{k}.{i}.ln_in", e, w[pre + "ln_in"], self.h_e, M)
+            if s.is_self_attn(i):
+                self._gemm(p, f"s{k}.{i}.qkv", self.h_e, w[pre + "qkv"], self.qkv_e)
+                bk = (L_ + H) * kv
+                own = L_ * kv * 2  # bytes to the step's own rows
+                p.add(f"s{k}.{i}.rope_kv", self.lib.so101_rope_kv, self.qkv_e.data_ptr(), qd, nq, nk, hd,
+                      w["cos_s"].data_ptr(), w["sin_s"].data_ptr(), self.ck[i].data_ptr() + own, kv,
+                      self.cv[i].data_ptr() + own, kv, H, B, H * qd, bk, bk)  # fmt: skip
+                self._attn(p, f"s{k}.{i}.attn", self.qkv_e.data_ptr(), qd, H * qd, self.ck[i].data_ptr(),
+                           kv, bk, self.cv[i].data_ptr(), kv, bk, self.attn_e, s.q_dim, H * s.q_dim,
+                           Lq=H, Lk=L_ + H, nq=nq, nkv=nk, hd=hd, causal_from=L_, q_offset=L_,
+                           cos=w["cos_s"], sin=w["sin_s"], batch=B)  # fmt: skip
+            else:
+                qv = self.qkv_e[:, : s.q_dim]
+                self._gemm(p, f"s{k}.{i}.q", self.h_e, w[pre + "q"], qv)
+                self._attn(p, f"s{k}.{i}.attn", self.qkv_e.data_ptr(), qd, H * qd, self.kx[i].data_ptr(),
+                           kv, L_ * kv, self.vx[i].data_ptr(), kv, L_ * kv, self.attn_e, s.q_dim,
+                           H * s.q_dim, Lq=H, Lk=L_, nq=nq, nkv=nk, hd=hd, causal_from=L_,
+                           cos=w["cos_c"], sin=w["sin_c"], batch=B)  # fmt: skip
+            self._gemm(p, f"s{k}.{i}.o", self.attn_e, w[pre + "o"], e, residual=e)
+            self._rms(p, f"s{k}.{i}.ln_post", e, w[pre + "ln_post"], self.h_e, M)
+            self._gemm(p, f"s{k}.{i}.gate_up", self.h_e, w[pre + "gate_up"], self.mlp_e, gate=True)
+            self._gemm(p, f"s{k}.{i}.down", self.mlp_e, w[pre + "down"], e, residual=e)
+        p.add(f"s{k}.out+euler", self.lib.so101_expert_out, e.data_ptr(), s.exp_dim, w["exp.norm"].data_ptr(),
+              s.rms_eps, w["act.out.w"].data_ptr(), w["act.out.b"].data_ptr(), x_out.data_ptr(),
+              s.max_action, M, s.max_action, s.exp_dim, dt)  # fmt: skip
+
+    def _build_denoise(self, p: Program) -> None:
+        s, w = self.spec, self.w
+        x = self.noise.view(self.B * self.H, s.max_action)
+        for k in range(s.n_steps):
+            self._build_step(p, k, x, x, -1.0 / s.n_steps)
+        p.add("finish", self.lib.so101_finish, self.noise.data_ptr(), s.max_action, self.state.data_ptr(),
+              self.state_dim, w["norm.state.mean"].data_ptr(), w["norm.state.std"].data_ptr(),
+              w["repr.mean"].data_ptr(), w["repr.std"].data_ptr(), w["norm.action.mean"].data_ptr(),
+              w["norm.action.std"].data_ptr(), self.out.data_ptr(), self.action_dim, self.H, self.repr,
+              self.B)  # fmt: skip
+
+    def velocity_program(self, k: int) -> Program:
+        """v_t at step k of the current x_t (noise buffer) into v_buf (for parity tests)."""
+        p = Program(f"velocity{k}")
+        x = self.noise.view(self.B * self.H, self.spec.max_action)
+        self._build_step(p, k, x, self.v_buf, 1.0)
+        return p
+
+    @torch.no_grad()
+    def calibrate(self, observations, cams, include_patch=False) -> dict[str, float]:
+        """max |input| per vision linear over the observations' frames (bf16 vision)."""
+        names = vision_linear_names(self.spec)
+        amax = torch.zeros(len(names), dtype=torch.float32, device=self.dev)
+        prog = Program("calibrate")
+        self._amax = (amax, {n: i for i, n in enumerate(names)})
+        try:
+            self._build_vision(prog)
+        finally:
+            self._amax = None
+        stream = torch.cuda.current_stream(self.dev).cuda_stream
+        B, C_ = self.B, self.C
+        obs = list(observations)
+        for start in range(0, len(obs), B):
+            chunk = obs[start : start + B]
+            chunk += [chunk[-1]] * (B - len(chunk))
+            frames = np.stack([o[c] for o in chunk for c in cams])
+            self.img.copy_(torch.from_numpy(frames))
+            prog.run(stream)
+        vals = amax.cpu().tolist()
+        return {n: v for n, v in zip(names, vals, strict=True) if include_patch or n != "patch"}
+
+    # ------------------------------------------------------------------ running
+    def run(self, stage: str, stream: int | None = None) -> None:
+        st = torch.cuda.current_stream(self.dev).cuda_stream if stream is None else stream
+        self.progs[stage].run(st)
+
+    def run_chunk(self, stream: int | None = None) -> None:
+        for name in ("vision", "prefix", "denoise"):
+            self.run(name, stream)
+
+    def launches(self) -> int:
+        return sum(len(p) for p in self.progs.values())

@@ -1,0 +1,165 @@
+"""The B200 engine end to end against the reference's float32 golden chunks (tests/golden/).
+
+max |action - float32 reference| <= 1e-2 rad for bf16 and for W8A8 int8 vision
+Stage parity (image rows, prefix K/V, the first velocity) is checked against the
+reference's own intermediates at bf16-level tolerances. Graph replay equals eager replay bit for
+bit, as the reference requires of its Triton path (`tests/test_triton_engine.py:33-47`).
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+from conftest import case_bundle, config0_bundle, golden
+
+from so101_smolvla_edge_b200.bundle import observation
+
+pytestmark = pytest.mark.gpu
+
+ACTION_TOL = 1e-2  # rad
+GPU_CASES = ["small_absolute", "small_delta", "small_velocity", "small64_absolute"]
+
+
+def rel(a, b) -> float:
+    a, b = np.asarray(a, np.float64), np.asarray(b, np.float64)
+    return float(np.abs(a - b).max() / max(np.abs(b).max(), 1e-12))
+
+
+@pytest.fixture(scope="module")
+def config0_engine():
+    from so101_smolvla_edge_b200.engine import Engine
+
+    eng = Engine(config0_bundle(), warmup=1)
+    yield eng
+    del eng
+    torch.cuda.empty_cache()
+
+
+@pytest.mark.parametrize("case", GPU_CASES)
+def test_small_bundles_match_reference(case):
+    """Every action representation, resize + padding, perturbed norms and biases."""
+    from so101_smolvla_edge_b200.engine import Engine
+
+    g = golden(case)
+    b = case_bundle(case)
+    graph = Engine(b, warmup=1)
+    eager = Engine(b, warmup=1, cuda_graph=False)
+    for seed in (0, 1):
+        images, state, noise = observation(b, seed)
+        a = graph.infer(images, state, noise)
+        e = eager.infer(images, state, noise)
+        assert np.array_equal(a, e), "graph replay differs from eager"
+        want = g[f"s{seed}.actions"]
+        err = np.abs(a - want).max()
+        assert err <= ACTION_TOL * max(1.0, np.abs(want).max()), (case, seed, err)
+
+
+def test_config0_stages_match_reference(config0_engine):
+    """configs[0] seed 0: image rows, layer-0 keys/values, layer-1 expert keys, first velocity."""
+    g = golden("config0")
+    eng = config0_engine
+    b = eng.bundle
+    images, state, noise = observation(b, 0)
+    eng._stage([images], [state], [noise])
+    p = eng.path
+    p.run("vision")
+    torch.cuda.synchronize()
+    L, C_ = eng.spec.prefix_len, eng.spec.n_cams
+    img_rows = p.prefix[: C_ * eng.spec.img_tokens].cpu().numpy()
+    assert rel(img_rows, g["s0.img_rows"]) < 2e-2, rel(img_rows, g["s0.img_rows"])
+    p.run("prefix")
+    torch.cuda.synchronize()
+    k0 = p.ck[0][0, :L].float().cpu().numpy()
+    v0 = p.cv[0][0, :L].float().cpu().numpy()
+    kx1 = p.kx[1][0].float().cpu().numpy()
+    assert rel(k0, g["s0.k_0"]) < 2e-2, rel(k0, g["s0.k_0"])
+    assert rel(v0, g["s0.v_0"]) < 2e-2, rel(v0, g["s0.v_0"])
+    assert rel(kx1, g["s0.kx_1"]) < 3e-2, rel(kx1, g["s0.kx_1"])
+    v = eng.step(0)[0].cpu().numpy()
+    assert rel(v, g["s0.v0"]) < 3e-2, rel(v, g["s0.v0"])
+
+
+def test_config0_actions_within_north_star(config0_engine):
+    """configs[0] (3 x 512^2 cameras, 241-token prefix, 10 steps): every golden seed within
+    1e-2 rad of the reference's float32 chunk; replays are deterministic."""
+    g = golden("config0")
+    eng = config0_engine
+    b = eng.bundle
+    errs = []
+    for seed in range(g["actions"].shape[0]):
+        images, state, noise = observation(b, seed)
+        a = eng.infer(images, state, noise)
+        errs.append(np.abs(a - g["actions"][seed]).max())
+        assert np.array_equal(a, eng.infer(images, state, noise))
+    assert max(errs) <= ACTION_TOL, errs
+
+
+def test_batched_equals_single():
+    """infer_batch over B observations agrees with B single-chunk engines."""
+    from so101_smolvla_edge_b200.engine import Engine
+
+    b = case_bundle("small_absolute")
+    obs = [observation(b, s) for s in range(3)]
+    single = Engine(b, warmup=1)
+    batched = Engine(b, warmup=1, batch=3)
+    got = batched.infer_batch([o[0] for o in obs], [o[1] for o in obs], [o[2] for o in obs])
+    for i, (images, state, noise) in enumerate(obs):
+        want = single.infer(images, state, noise)
+        assert np.abs(got[i] - want).max() <= 1e-3 * max(1.0, np.abs(want).max())
+
+
+def test_int8_vision_small_matches_fake_quant_oracle():
+    """W8A8 vision with the golden clips: near the int8 reference chunk and near float32."""
+    from so101_smolvla_edge_b200.engine import Engine
+
+    g = golden("int8_small_absolute")
+    b = case_bundle("small_absolute")
+    clip = dict(zip(g["clip_names"].tolist(), g["clip_values"].tolist(), strict=True))
+    eng = Engine(b, warmup=1, trt_precision="int8", act_clip=clip)
+    images, state, noise = observation(b, 0)
+    a = eng.infer(images, state, noise)
+    scale = max(1.0, np.abs(g["actions_int8"]).max())
+    assert np.abs(a - g["actions_int8"]).max() <= ACTION_TOL * scale
+    assert np.abs(a - g["actions_fp32"]).max() <= ACTION_TOL * scale
+
+
+def test_int8_vision_config0_within_north_star():
+    """configs[4]'s numerics at batch 1: W8A8 SigLIP with the reference's calibration (32 seeded
+    observations), bf16 prefix and expert, within 1e-2 rad of float32."""
+    from so101_smolvla_edge_b200.engine import Engine
+
+    g = golden("int8_config0")
+    b = config0_bundle()
+    clip = dict(zip(g["clip_names"].tolist(), g["clip_values"].tolist(), strict=True))
+    eng = Engine(b, warmup=1, trt_precision="int8", act_clip=clip)
+    images, state, noise = observation(b, 0)
+    a = eng.infer(images, state, noise)
+    assert np.abs(a - g["actions_fp32"]).max() <= ACTION_TOL
+    assert np.abs(a - g["actions_int8"]).max() <= ACTION_TOL
+
+
+def test_calibration_matches_reference_clips():
+    """Engine.calibrate over the reference's 32 calibration frames gives its clips (bf16
+    activations, so within a few bf16 ulps of the float32 maxima)."""
+    from so101_smolvla_edge_b200.engine import Engine
+
+    g = golden("int8_small_absolute")
+    b = case_bundle("small_absolute")
+    eng = Engine(b, warmup=0, cuda_graph=False)
+    clip = eng.calibrate([observation(b, 1000 + i)[0] for i in range(32)])
+    want = dict(zip(g["clip_names"].tolist(), g["clip_values"].tolist(), strict=True))
+    assert sorted(clip) == sorted(want)
+    for k, v in want.items():
+        assert abs(clip[k] - v) <= 2e-2 * v, (k, clip[k], v)
+
+
+def test_unsupported_models_raise():
+    """No fallback: a head size the kernels cannot index raises (the reference would fall back
+    to torch kernels with a log line, `tests/test_triton_engine.py:90-99`)."""
+    from so101_smolvla_edge_b200.engine import Engine
+
+    with pytest.raises(ValueError):
+        Engine(case_bundle("tiny_absolute"), warmup=0)
+    with pytest.raises(ValueError):
+        Engine(case_bundle("small_absolute"), dtype="fp32", warmup=0)

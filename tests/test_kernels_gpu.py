@@ -1,0 +1,302 @@
+"""Each CUDA kernel against the float32 torch expression it replaces, through the C ABI.
+
+BASELINE configs[1] (GEMM sweep: M in {50, 241, 3072} over the engine's projection shapes, with
+each epilogue) and configs[2] (attention: 15 q / 5 kv heads, head_dim 64, RoPE base 1e5, the
+prefix-LM mask over 241 tokens, expert self/cross attention over the cached prefix), plus odd
+sizes. Tolerances follow the reference's own kernel tests (`tests/test_kernels.py`): GEMM one
+output rounding + fp32 accumulation noise, attention 0.02 * max and 2e-3 * mean, RMSNorm 2^-7.
+"""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+F = torch.nn.functional
+
+
+def rnd(*shape, dtype=torch.float32, scale=1.0, seed=0):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    return (torch.randn(*shape, generator=g, device="cuda") * scale).to(dtype)
+
+
+def gemm_ref(x, w, bias=None, residual=None, silu_gate=False, gelu=False):
+    y = x.float() @ w.float().T
+    if bias is not None:
+        y = y + bias.float()
+    if gelu:
+        y = F.gelu(y, approximate="tanh")
+    if silu_gate:
+        g, u = y.chunk(2, dim=-1)
+        y = F.silu(g) * u
+    if residual is not None:
+        y = y + residual.float()
+    return y
+
+
+def close(got, want, out_dtype):
+    """One rounding to the output dtype plus float32 accumulation-order noise
+    (`tests/test_kernels.py:200-204` of the reference)."""
+    eps = 2**-8 if out_dtype == torch.bfloat16 else 1e-5
+    err = (got.float() - want).abs()
+    return bool(err.max() <= 2 * eps * want.abs().max() + 1e-4), float(err.max())
+
+
+# configs[1] (N, K) pairs, then the engine's real fused shapes
+NK = [(960, 960), (320, 960), (5120, 960), (960, 2560), (720, 720), (4096, 720), (720, 2048),
+      (2304, 768), (3072, 768), (768, 3072), (1600, 960), (1600, 720), (960, 720), (720, 960),
+      (320, 320), (768, 768), (960, 12288)]  # fmt: skip
+MS = [50, 241, 3072]
+
+
+@pytest.mark.parametrize("m", MS)
+@pytest.mark.parametrize("n,k", NK)
+@pytest.mark.parametrize("epi", ["none", "residual"])
+def test_gemm_sweep(m, n, k, epi):
+    """every shape and row count, plain and with the fp32 residual epilogue."""
+    from so101_smolvla_edge_b200.ops import linear
+
+    x = rnd(m, k, dtype=torch.bfloat16)
+    w = rnd(n, k, dtype=torch.bfloat16, scale=0.02, seed=1)
+    kw = {}
+    if epi == "residual":
+        kw["residual"] = rnd(m, n, seed=3, scale=10.0)
+    got = linear(x, w, **kw)
+    want = gemm_ref(x, w, **kw)
+    ok, err = close(got, want, got.dtype)
+    assert ok, err
+    # the configs[1] criterion: 1e-2 relative to the output scale
+    assert err <= 1e-2 * want.abs().max()
+
+
+GEMM_SHAPES = [(50, 720, 1600), (50, 960, 720), (50, 720, 4096), (50, 2048, 720), (241, 960, 1600),
+               (241, 960, 5120), (3072, 768, 2304), (7, 104, 40), (64, 64, 64), (1, 4096, 16),
+               (130, 136, 200), (200, 960, 1600)]  # fmt: skip
+
+
+@pytest.mark.parametrize("m,k,n", GEMM_SHAPES)
+@pytest.mark.parametrize("epi", ["none", "bias", "residual", "residual_bf16", "silu_gate", "gelu"])
+def test_linear_epilogues(m, k, n, epi):
+    """Each epilogue matches the float32 reference within one output rounding
+    (`tests/test_kernels.py:207-228` of the reference, plus GELU for SigLIP)."""
+    from so101_smolvla_edge_b200.ops import linear
+
+    if epi == "silu_gate" and n % 2:
+        n += 1
+    x = rnd(m, k, dtype=torch.bfloat16)
+    w = rnd(n, k, dtype=torch.bfloat16, scale=k**-0.5, seed=1)
+    kw = {}
+    if epi in ("bias", "gelu"):
+        kw["bias"] = rnd(n if epi != "silu_gate" else n // 2, seed=2)
+    if epi.startswith("residual"):
+        res_dtype = torch.bfloat16 if epi == "residual_bf16" else torch.float32
+        kw["residual"] = rnd(m, n, seed=3, scale=10.0).to(res_dtype)
+    if epi == "silu_gate":
+        kw["silu_gate"] = True
+    if epi == "gelu":
+        kw["gelu"] = True
+    got = linear(x, w, **kw)
+    want = gemm_ref(x, w, **kw)
+    assert got.shape == want.shape
+    ok, err = close(got, want, got.dtype)
+    assert ok, err
+
+
+@pytest.mark.parametrize("swap,bn", [(1, 16), (1, 32), (1, 48), (1, 64), (0, 64), (0, 128), (0, 256)])
+@pytest.mark.parametrize("split", [1, 2, 3, 7])
+def test_tiles_and_split_k_agree_and_repeat(swap, bn, split):
+    """Every tile shape and split count agrees with the reference and repeats bit for bit
+    (split-K is deterministic: `tests/test_kernels.py:231-243` of the reference)."""
+    from so101_smolvla_edge_b200.ops import linear
+
+    x = rnd(50, 2048, dtype=torch.bfloat16)
+    w = rnd(720, 2048, dtype=torch.bfloat16, scale=2048**-0.5, seed=1)
+    r = rnd(50, 720, seed=2)
+    cfg = (swap, bn, split, 0)
+    a = linear(x, w, residual=r, config=cfg)
+    b = linear(x, w, residual=r, config=cfg)
+    assert torch.equal(a, b)
+    ok, err = close(a, gemm_ref(x, w, residual=r), torch.float32)
+    assert ok, err
+
+
+@pytest.mark.parametrize("swap,bn,split", [(1, 64, 1), (1, 64, 5), (0, 128, 1), (0, 64, 3)])
+def test_silu_gate_tiles(swap, bn, split):
+    from so101_smolvla_edge_b200.ops import linear
+
+    x = rnd(50, 720, dtype=torch.bfloat16)
+    w = rnd(4096, 720, dtype=torch.bfloat16, scale=720**-0.5, seed=1)
+    got = linear(x, w, silu_gate=True, config=(swap, bn, split, 0))
+    ok, err = close(got, gemm_ref(x, w, silu_gate=True), torch.bfloat16)
+    assert ok, err
+
+
+def test_linear_takes_float32_input_like_lin():
+    from so101_smolvla_edge_b200.ops import linear
+
+    x = rnd(50, 720)
+    w = rnd(960, 720, dtype=torch.bfloat16, scale=720**-0.5, seed=1)
+    assert torch.equal(linear(x, w), linear(x.to(torch.bfloat16), w))
+
+
+def test_strided_input_view():
+    """x may be a column slice of a wider buffer (the fused qkv's value columns)."""
+    from so101_smolvla_edge_b200.ops import linear
+
+    qkv = rnd(241, 1600, dtype=torch.bfloat16)
+    v = qkv[:, 1280:]
+    w = rnd(320, 320, dtype=torch.bfloat16, scale=320**-0.5, seed=1)
+    ok, err = close(linear(v, w), gemm_ref(v, w), torch.bfloat16)
+    assert ok, err
+
+
+@pytest.mark.parametrize("m,k,n", [(3072, 768, 2304), (3072, 3072, 768), (192, 12288, 960), (50, 768, 64)])
+def test_int8_gemm_is_the_fake_quant_product(m, k, n):
+    """W8A8: int8 x and w with per-tensor / per-channel scales give the float product of the
+    dequantized operands (exact int32 accumulation)."""
+    from so101_smolvla_edge_b200.ops import linear, quantize_weight
+
+    wf = rnd(n, k, scale=0.02, seed=1)
+    wq, ws = quantize_weight(wf)
+    # IEEE float32 quotients (float64 division rounded once); torch's CUDA division by a Python
+    # scalar multiplies by the reciprocal instead, which can differ in the last bit
+    ws_ref = (wf.abs().amax(1).double() / 127.0).float().clamp(min=1e-8)
+    assert torch.equal(ws, ws_ref)
+    q = (wf.double() / ws_ref.double()[:, None]).float()
+    assert torch.equal(wq.float(), torch.clamp(torch.round(q), -127, 127))
+    xs = 0.05
+    xq = torch.randint(-128, 128, (m, k), device="cuda", dtype=torch.int8)
+    b = rnd(n, seed=2)
+    got = linear(xq, wq, bias=b, x_scale=xs, w_scale=ws, out_dtype=torch.float32)
+    want = (xq.double() @ wq.double().T) * xs * ws.double() + b.double()
+    err = (got.double() - want).abs().max()
+    assert err <= 1e-5 * want.abs().max() + 1e-5, float(err)
+
+
+# ---------------------------------------------------------------------------------- attention
+def attention_ref(q, k, v, n_heads, n_kv, visible, cos=None, sin=None):
+    """q rotated in fp32 and rounded to bf16, k/v expanded to the query heads, fp32 softmax."""
+    lq, lk, hd = q.shape[0], k.shape[0], k.shape[1] // n_kv
+    qq = q[:, : n_heads * hd].reshape(lq, n_heads, hd).float()
+    if cos is not None:
+        c, s = cos[:, None, :], sin[:, None, :]
+        x1, x2 = qq[..., : hd // 2], qq[..., hd // 2 :]
+        qq = torch.cat([x1 * c - x2 * s, x2 * c + x1 * s], -1).to(torch.bfloat16).float()
+    g = n_heads // n_kv
+    kk = k.reshape(lk, n_kv, hd).float().transpose(0, 1).repeat_interleave(g, 0)
+    vv = v.reshape(lk, n_kv, hd).float().transpose(0, 1).repeat_interleave(g, 0)
+    sc = (qq.transpose(0, 1) @ kk.transpose(1, 2)) / hd**0.5
+    if visible is not None:
+        sc = sc.masked_fill(~visible, float("-inf"))
+    return (torch.softmax(sc, -1) @ vv).transpose(0, 1).reshape(lq, n_heads * hd)
+
+
+def rope_tables(pos, hd, base):
+    half = hd // 2
+    exps = (2.0 / hd) * torch.arange(half, dtype=torch.float32, device=pos.device)
+    ang = pos.float()[:, None] / (base**exps)[None, :]
+    return torch.cos(ang), torch.sin(ang)
+
+
+def visibility(lq, lk, causal_from, q_offset):
+    i = torch.arange(lq, device="cuda")[:, None]
+    j = torch.arange(lk, device="cuda")[None, :]
+    return (j < causal_from) | (j <= i + q_offset)
+
+
+@pytest.mark.parametrize("case", ["prefix", "expert_self", "expert_cross", "small", "siglip"])
+def test_attention(case):
+    """the prefix-LM mask over 241 tokens (192 image + 48 text bidirectional, the
+    state token last), expert self attention (50 queries over 241 prefix + 50 causal keys),
+    expert cross attention (50 over 241), RoPE base 1e5; SigLIP 1024 tokens unmasked."""
+    from so101_smolvla_edge_b200.ops import attention
+
+    L, H = 241, 50
+    nq, nk, hd = (15, 5, 64)
+    rope = True
+    if case == "prefix":
+        lq, lk, pos, cf, qo = L, L, torch.arange(L), L - 1, 0
+    elif case == "expert_self":
+        lq, lk, pos, cf, qo = H, L + H, torch.arange(L, L + H), L, L
+    elif case == "expert_cross":
+        lq, lk, pos, cf, qo = H, L, torch.arange(H), L, 0
+    elif case == "small":
+        nq, nk, hd = 4, 2, 32
+        lq, lk, pos, cf, qo = 13, 13, torch.arange(13), 12, 0
+    else:
+        nq, nk, hd, rope = 12, 12, 64, False
+        lq, lk, pos, cf, qo = 1024, 1024, torch.arange(1024), 1024, 0
+    q = rnd(lq, (nq + 2 * nk) * hd, dtype=torch.bfloat16)
+    k = rnd(lk, nk * hd, dtype=torch.bfloat16, seed=1)
+    v = rnd(lk, nk * hd, dtype=torch.bfloat16, seed=2)
+    cos, sin = rope_tables(pos.cuda(), hd, 100_000.0) if rope else (None, None)
+    got = attention(q, k, v, nq, nk, cos=cos, sin=sin, causal_from=cf, q_offset=qo)[0]
+    want = attention_ref(q, k, v, nq, nk, visibility(lq, lk, cf, qo), cos, sin)
+    err = (got.float() - want).abs()
+    assert err.max() <= 0.02 * want.abs().max(), float(err.max())
+    assert err.mean() <= 2e-3 * want.abs().mean() + 1e-4, float(err.mean())
+    again = attention(q, k, v, nq, nk, cos=cos, sin=sin, causal_from=cf, q_offset=qo)[0]
+    assert torch.equal(got, again)
+
+
+def test_attention_batched_and_strided():
+    """A batch of independent problems with k and v as views into the fused qkv rows."""
+    from so101_smolvla_edge_b200.ops import attention
+
+    B, L, nq, nk, hd = 3, 241, 15, 5, 64
+    qkv = rnd(B, L, (nq + 2 * nk) * hd, dtype=torch.bfloat16)
+    k, v = qkv[:, :, nq * hd : (nq + nk) * hd], qkv[:, :, (nq + nk) * hd :]
+    got = attention(qkv, k, v, nq, nk, causal_from=L - 1)
+    for b in range(B):
+        want = attention_ref(qkv[b], k[b], v[b], nq, nk, visibility(L, L, L - 1, 0))
+        assert (got[b].float() - want).abs().max() <= 0.02 * want.abs().max()
+
+
+@pytest.mark.parametrize("rows,offset", [(50, 241), (241, 0), (7, 3)])
+def test_rope_kv(rows, offset):
+    """rope_kv writes rotated k and plain v into their cache rows and nothing else; the
+    rotation is torch's per-operation fp32 arithmetic, so the bf16 keys match bit for bit."""
+    from so101_smolvla_edge_b200.ops import rope_kv
+
+    nq, nk, hd = 15, 5, 64
+    qkv = rnd(rows, (nq + 2 * nk) * hd, dtype=torch.bfloat16, scale=3.0)
+    cos, sin = rope_tables(torch.arange(offset, offset + rows, device="cuda"), hd, 10_000.0)
+    cache_k = torch.zeros(offset + rows + 5, nk * hd, dtype=torch.bfloat16, device="cuda")
+    cache_v = torch.zeros_like(cache_k)
+    rope_kv(qkv, nq, nk, cos, sin, cache_k[offset : offset + rows], cache_v[offset : offset + rows])
+    k = qkv[:, nq * hd : (nq + nk) * hd].reshape(rows, nk, hd).float()
+    c, s = cos[:, None, :], sin[:, None, :]
+    want = torch.cat([k[..., :32] * c - k[..., 32:] * s, k[..., 32:] * c + k[..., :32] * s], -1)
+    want = want.to(torch.bfloat16).reshape(rows, nk * hd)
+    assert torch.equal(cache_k[offset : offset + rows], want)
+    assert torch.equal(cache_v[offset : offset + rows], qkv[:, (nq + nk) * hd :])
+    assert not cache_k[:offset].any() and not cache_k[offset + rows :].any()
+
+
+@pytest.mark.parametrize("rows,n", [(50, 720), (241, 960), (7, 33), (1, 1024)])
+@pytest.mark.parametrize("in_dtype", [torch.float32, torch.bfloat16])
+def test_rms_norm(rows, n, in_dtype):
+    from so101_smolvla_edge_b200.ops import rms_norm
+
+    x = rnd(1, rows, n, scale=30.0).to(in_dtype)
+    w = 1 + 0.1 * rnd(n, seed=1)
+    want = F.rms_norm(x.float(), (n,), w, 1e-5).to(torch.bfloat16)
+    got = rms_norm(x, w, 1e-5)
+    assert got.shape == want.shape and got.dtype == torch.bfloat16
+    assert (got.float() - want.float()).abs().max() <= 2**-7 * want.float().abs().max()
+    assert (got.float() - want.float()).abs().mean() <= 1e-3 * want.float().abs().mean()
+
+
+def test_layer_norm_and_pixel_shuffle():
+    """LayerNorm then the SmolVLM pixel shuffle, written in one pass."""
+    from so101_smolvla_edge_b200.ops import layer_norm
+
+    x = rnd(2 * 1024, 768, scale=3.0)
+    w, b = 1 + 0.1 * rnd(768, seed=1), 0.1 * rnd(768, seed=2)
+    ln = F.layer_norm(x, (768,), w, b, 1e-6)
+    plain = layer_norm(x, w, b, 1e-6)
+    assert (plain.float() - ln).abs().max() <= 2**-7 * ln.abs().max()
+    shuf = layer_norm(x, w, b, 1e-6, shuffle=4, tokens_per_image=1024)
+    v = ln.reshape(2, 8, 4, 8, 4, 768).permute(0, 1, 3, 2, 4, 5).reshape(2 * 64, 768 * 16)
+    assert (shuf.float() - v).abs().max() <= 2**-7 * v.abs().max()
