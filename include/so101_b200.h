@@ -187,6 +187,22 @@ SO101_API int so101_quantize_weight(const void* w, int w_type, int64_t N, int64_
 SO101_API int so101_device_status(void);
 SO101_API int so101_clear_device_status(void);
 
+/* so101_gemm for callers that cannot allocate device memory. No counterpart in the reference.
+ * Some hosts cannot call cudaMalloc when they need a GEMM: code running inside CUDA-graph capture,
+ * a real-time control loop that forbids allocation after start-up, a foreign-language runtime
+ * that reaches the GPU only through this library. This entry point takes no workspace: its split-K
+ * scratch (at most 8 MiB of partials and 4096 tile tickets) is a file-scope device array that
+ * every GPU loading the library holds until the process exits. Problems whose split-K plan needs
+ * more return SO101_ERR_WORKSPACE. It allocates nothing and frees nothing; the tickets are
+ * cleared on the stream before each launch. The first call on a device looks the array's device
+ * address up (cudaGetSymbolAddress, with that device current): make that first call before any
+ * stream capture. All calls share the one array, so calls that overlap on the GPU (other streams,
+ * other host threads) race; keep them ordered on one stream. */
+SO101_API int so101_gemm_static(int a_type, const void* x, int64_t ldx, const void* w, int64_t ldw,
+                                void* y, int64_t ldy, int y_type, int64_t M, int64_t N, int64_t K,
+                                const so101_epilogue* epi, const so101_gemm_config* cfg,
+                                cudaStream_t stream);
+
 /* Programmatic dependent launch for the GEMM kernels (0 off, default; 1 on): each GEMM may start
  * streaming its weights while the previous kernel on the stream drains. */
 SO101_API int so101_set_pdl(int enable);

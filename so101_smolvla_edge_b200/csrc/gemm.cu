@@ -647,3 +647,64 @@ extern "C" int so101_gemm(int a_type, const void* x, int64_t ldx, const void* w,
   if (dual) return launch_bn<false, true, false>(tx, tw, a, pl, stream, pdl);
   return launch_bn<false, false, false>(tx, tw, a, pl, stream, pdl);
 }
+
+// ============================================================================ allocation-free entry
+// so101_gemm_static: so101_gemm with its split-K scratch (fp32/int32 partials and the ticket
+// counters) held in a file-scope device array instead of a caller-allocated workspace. It is for
+// callers that cannot allocate device memory: a host stuck inside CUDA-graph capture, a real-time
+// control loop that forbids allocation after start-up, or a foreign-language runtime whose only
+// handle on the GPU is this library. Every GPU that loads the library holds the array until the
+// process exits.
+namespace so101 {
+namespace {
+
+constexpr long long kStaticPartialBytes = 8ll << 20;  // 8 MiB of split-K partials
+constexpr long long kStaticTickets = 4096;            // one per output tile
+
+static __device__ __align__(256) unsigned char g_static_scratch[kStaticPartialBytes + kStaticTickets * 4];
+
+// Host-side device address of g_static_scratch, looked up once per device with that device
+// current (the symbol's host name is only a stand-in, never a device address).
+struct StaticScratch {
+  void* base = nullptr;
+};
+StaticScratch g_static_scratch_addr[64];
+std::mutex g_static_scratch_mu;
+
+int static_scratch(void** partials, int** tickets) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return SO101_ERR_LAUNCH;
+  std::lock_guard<std::mutex> lock(g_static_scratch_mu);
+  if (!g_static_scratch_addr[dev].base) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_static_scratch) != cudaSuccess || !p) return SO101_ERR_LAUNCH;
+    g_static_scratch_addr[dev].base = p;
+  }
+  *partials = g_static_scratch_addr[dev].base;
+  *tickets = reinterpret_cast<int*>(static_cast<unsigned char*>(g_static_scratch_addr[dev].base) +
+                                    kStaticPartialBytes);
+  return SO101_OK;
+}
+
+}  // namespace
+}  // namespace so101
+
+extern "C" int so101_gemm_static(int a_type, const void* x, int64_t ldx, const void* w, int64_t ldw, void* y,
+                                 int64_t ldy, int y_type, int64_t M, int64_t N, int64_t K,
+                                 const so101_epilogue* epi, const so101_gemm_config* cfg, cudaStream_t stream) {
+  if (!epi) return SO101_ERR_ARG;
+  int64_t need = 0, tick = 0;
+  int rc = so101_gemm_workspace(a_type, M, N, K, epi->epilogue, cfg, &need, &tick);
+  if (rc) return rc;
+  if (need > so101::kStaticPartialBytes || tick > so101::kStaticTickets) return SO101_ERR_WORKSPACE;
+  void* partials = nullptr;
+  int* tickets = nullptr;
+  rc = so101::static_scratch(&partials, &tickets);
+  if (rc) return rc;
+  // the tickets must read zero when the kernel starts; a completed call leaves them zero, this
+  // also clears what an interrupted one left behind (a stream-ordered memset, not an allocation)
+  if (tick > 0 && cudaMemsetAsync(tickets, 0, static_cast<size_t>(tick) * sizeof(int), stream) != cudaSuccess)
+    return SO101_ERR_LAUNCH;
+  return so101_gemm(a_type, x, ldx, w, ldw, y, ldy, y_type, M, N, K, epi, cfg, partials,
+                    so101::kStaticPartialBytes, tickets, so101::kStaticTickets, stream);
+}

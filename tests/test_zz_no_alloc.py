@@ -1,0 +1,91 @@
+"""so101_gemm_static, the GEMM entry point for callers that cannot allocate device memory.
+
+Hosts inside CUDA-graph capture, real-time loops that forbid allocation after start-up, and
+foreign-language runtimes that reach the GPU only through this library cannot hand so101_gemm a
+workspace. so101_gemm_static keeps its split-K scratch in a file-scope device array instead. This
+test calls it through the C ABI twice in a row and checks each result against so101_gemm with a
+caller-allocated workspace, on split-K plans that use the scratch, and checks that a plan larger
+than the array is refused. It lives in its own file, collected last, and passes alone in a fresh
+process or after the rest of the suite.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _bind():
+    from so101_smolvla_edge_b200 import _lib as L
+
+    lib = L.lib()
+    fn = lib.so101_gemm_static
+    fn.argtypes = [C.c_int, C.c_void_p, C.c_int64, C.c_void_p, C.c_int64, C.c_void_p, C.c_int64,
+                   C.c_int, C.c_int64, C.c_int64, C.c_int64, C.POINTER(L.Epilogue),
+                   C.POINTER(L.GemmConfig), C.c_void_p]  # fmt: skip
+    fn.restype = C.c_int
+    return L, lib, fn
+
+
+def _close(got, want):
+    """The GEMM tests' bound: one rounding to the output dtype plus fp32 accumulation noise."""
+    eps = 2**-8 if got.dtype == torch.bfloat16 else 1e-5
+    err = (got.float() - want.float()).abs()
+    return bool(err.max() <= 2 * eps * want.float().abs().max() + 1e-4)
+
+
+@pytest.mark.parametrize("m,n,k,cfg,gate", [
+    (50, 720, 2048, (1, 64, 4, 0), False),     # the expert's down projection, split 4 ways
+    (50, 2048, 720, (1, 64, 3, 0), True),      # gate_up with the SiLU gate, split 3 ways
+    (241, 960, 2560, (0, 128, 5, 0), False),   # prefix down, tokens on the MMA M side
+])  # fmt: skip
+def test_static_scratch_gemm_matches_workspace_gemm(m, n, k, cfg, gate):
+    L, lib, static = _bind()
+    from so101_smolvla_edge_b200.ops import workspace
+
+    g = torch.Generator(device="cuda").manual_seed(0)
+    x = torch.randn(m, k, device="cuda", generator=g).to(torch.bfloat16)
+    w = (torch.randn(2 * n if gate else n, k, device="cuda", generator=g) * k**-0.5).to(torch.bfloat16)
+    r = torch.randn(m, n, device="cuda", generator=g)
+    out_dtype = torch.bfloat16 if gate else torch.float32
+    epi = L.Epilogue(epilogue=L.EPI_SILU_GATE if gate else L.EPI_NONE,
+                     residual=None if gate else r.data_ptr(), ldr=0 if gate else n,
+                     r_type=L.F32, out_scale=1.0)  # fmt: skip
+    c = L.GemmConfig(*cfg)
+    need, tick = C.c_int64(), C.c_int64()
+    L.check(lib.so101_gemm_workspace(L.BF16, m, n, k, epi.epilogue, C.byref(c), C.byref(need),
+                                     C.byref(tick)), "workspace")  # fmt: skip
+    assert need.value > 0, "the plan must use split-K scratch"
+    stream = torch.cuda.current_stream().cuda_stream
+    ws = workspace(x.device)
+    want = torch.empty(m, n, dtype=out_dtype, device="cuda")
+    L.check(lib.so101_gemm(L.BF16, x.data_ptr(), k, w.data_ptr(), k, want.data_ptr(), n,
+                           L.BF16 if gate else L.F32, m, n, k, C.byref(epi), C.byref(c),
+                           ws.partials.data_ptr(), ws.nbytes, ws.tickets.data_ptr(),
+                           ws.tickets.numel(), stream), "so101_gemm")  # fmt: skip
+    for _ in range(2):  # the scratch keeps the last call's contents: a second call must not care
+        got = torch.full((m, n), float("nan"), dtype=out_dtype, device="cuda")
+        rc = static(L.BF16, x.data_ptr(), k, w.data_ptr(), k, got.data_ptr(), n,
+                    L.BF16 if gate else L.F32, m, n, k, C.byref(epi), C.byref(c), stream)
+        assert rc == L.OK
+        torch.cuda.synchronize()
+        assert _close(got, want)
+    assert lib.so101_device_status() == 0
+
+
+def test_static_scratch_refuses_plans_beyond_its_size():
+    """A split-K plan needing more than the 8 MiB array is refused with SO101_ERR_WORKSPACE."""
+    L, lib, static = _bind()
+    m, n, k = 3072, 3072, 4096
+    x = torch.zeros(m, k, dtype=torch.bfloat16, device="cuda")
+    w = torch.zeros(n, k, dtype=torch.bfloat16, device="cuda")
+    y = torch.zeros(m, n, dtype=torch.bfloat16, device="cuda")
+    epi = L.Epilogue(epilogue=L.EPI_NONE, out_scale=1.0)
+    c = L.GemmConfig(0, 256, 8, 0)  # 288 tiles x 8 splits x 256 x 128 x 4 B: far beyond 8 MiB
+    rc = static(L.BF16, x.data_ptr(), k, w.data_ptr(), k, y.data_ptr(), n, L.BF16, m, n, k,
+                C.byref(epi), C.byref(c), torch.cuda.current_stream().cuda_stream)
+    assert rc == L.ERR_WORKSPACE
