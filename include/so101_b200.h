@@ -71,10 +71,18 @@ typedef struct so101_epilogue {
 /* Tile configuration; zero-initialised fields mean "pick" (the heuristic of so101_gemm_pick). */
 typedef struct so101_gemm_config {
   int swap;    /* 1: weights on the MMA M side (few token rows), 0: tokens on the M side */
-  int bn;      /* MMA N: 16..256, multiple of 16                                         */
-  int splits;  /* K splits (deterministic: the last CTA reduces in split order)          */
-  int stages;  /* shared-memory pipeline depth                                            */
+  int bn;      /* MMA N: 16, 32, 48, 64 (swap) or 64, 128, 256 (tokens on M)             */
+  int splits;  /* K splits, reduced in split order (deterministic)                        */
+  int stages;  /* shared-memory pipeline depth (0: chosen from the problem)               */
+  int flags;   /* SO101_GEMM_* bits                                                       */
 } so101_gemm_config;
+
+/* so101_gemm_config.flags. By default split-K partials are reduced on chip across a thread-block
+ * cluster (splits <= 8) and large problems with tokens on the MMA M side run the persistent
+ * kernel (one CTA per SM, double-buffered TMEM accumulators). */
+#define SO101_GEMM_GLOBAL_SPLITK 1     /* reduce split-K partials through the workspace       */
+#define SO101_GEMM_PERSISTENT 2        /* tokens on M, no split: always the persistent kernel */
+#define SO101_GEMM_ONE_TILE_PER_CTA 4  /* tokens on M: never the persistent kernel            */
 
 /* y (M x N) = epilogue(x (M x K) @ w (N x K)^T) on tcgen05 tensor cores, TMA-fed.
  * Replaces kernels/gemm.py:48-96 (so101_gemm) and :350-398 (linear), the cuBLAS F.linear calls of
@@ -82,7 +90,8 @@ typedef struct so101_gemm_config {
  * a_type SO101_BF16 (kind::f16, fp32 accumulate) or SO101_I8 (kind::i8, int32 accumulate).
  * Requires: 16-byte aligned x, w; K * elem_size and ldx, ldw a multiple of 16 bytes.
  * workspace: fp32 split-K partials; tickets: int32 counters, zero before the first call and left
- * zero by every call. Bytes needed: so101_gemm_workspace_bytes. cfg may be NULL. */
+ * zero by every call; both are used only by SO101_GEMM_GLOBAL_SPLITK plans (and splits > 8).
+ * Bytes needed: so101_gemm_workspace. cfg may be NULL. */
 SO101_API int so101_gemm(int a_type, const void* x, int64_t ldx, const void* w, int64_t ldw, void* y,
                int64_t ldy, int y_type, int64_t M, int64_t N, int64_t K,
                const so101_epilogue* epi, const so101_gemm_config* cfg, void* workspace,
@@ -141,11 +150,13 @@ SO101_API int so101_preprocess(const uint8_t* img, int n_img, int h, int w, int 
                      void* patches, int y_type, float y_qscale, cudaStream_t stream);
 
 /* Dense fp32 linear on CUDA cores (the reference keeps these small MLPs fp32):
- * y[m, n] = (act_in(x[m, :]) @ w[n, :]) + bias[n] (+ bias2[n]), act_in SiLU when silu_in.
+ * y[m, n] = act(x[m, :] @ w[n, :] + bias[n] (+ bias2[n])), act 0 none, 2 SiLU (act 1 is
+ * accepted and means none: SiLU belongs on the producer's output). K, ldx, ldw multiples of 4,
+ * x and w 16-byte aligned.
  * Replaces the fp32 F.linear calls of model/smolvla.py:282-285, 309 and engine.py:251. */
 SO101_API int so101_linear_f32(const float* x, int64_t ldx, const float* w, int64_t ldw, const float* bias,
                      const float* bias2, float* y, int64_t ldy, int64_t M, int64_t N, int64_t K,
-                     int silu_in, cudaStream_t stream);
+                     int act, cudaStream_t stream);
 
 /* The expert's output head and Euler step, per row m of e (M x K): x_t[m, :] += dt *
  * (rms_norm(e[m], norm_w) @ w_out^T + b_out). Replaces model/smolvla.py:308-309 and

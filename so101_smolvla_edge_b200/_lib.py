@@ -44,11 +44,15 @@ class Epilogue(C.Structure):
     ]
 
 
-class GemmConfig(C.Structure):
-    _fields_ = [("swap", C.c_int), ("bn", C.c_int), ("splits", C.c_int), ("stages", C.c_int)]
+GEMM_GLOBAL_SPLITK, GEMM_PERSISTENT, GEMM_ONE_TILE_PER_CTA = 1, 2, 4
 
-    def as_tuple(self) -> tuple[int, int, int, int]:
-        return (self.swap, self.bn, self.splits, self.stages)
+
+class GemmConfig(C.Structure):
+    _fields_ = [("swap", C.c_int), ("bn", C.c_int), ("splits", C.c_int), ("stages", C.c_int),
+                ("flags", C.c_int)]
+
+    def as_tuple(self) -> tuple[int, int, int, int, int]:
+        return (self.swap, self.bn, self.splits, self.stages, self.flags)
 
 
 P, I, I64, F, S = C.c_void_p, C.c_int, C.c_int64, C.c_float, C.c_void_p  # S: cudaStream_t

@@ -71,6 +71,7 @@ __global__ void __launch_bounds__(128) attention_kernel(const AttnArgs a) {
   __nv_bfloat16* sK = sQ + BM * LDS;          // [2][BN * LDS]
   __nv_bfloat16* sV = sK + 2 * BN * LDS;      // [2][BN * LDS]
 
+  grid_dep_launch();
   grid_dep_wait();
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int q0 = blockIdx.x * BM, h = blockIdx.y, bi = blockIdx.z;
@@ -101,26 +102,42 @@ __global__ void __launch_bounds__(128) attention_kernel(const AttnArgs a) {
 
   load_kv(0, 0);
 
-  // stage Q (rotated) into shared memory
-  for (int idx = tid; idx < BM * HALF; idx += 128) {
-    const int r = idx / HALF, d = idx % HALF;
+  // stage Q (rotated) into shared memory: 8 dims of each rotary half per step, 16-byte loads
+  constexpr int VH = HALF / 8;
+  for (int idx = tid; idx < BM * VH; idx += 128) {
+    const int r = idx / VH, d0 = (idx % VH) * 8;
     const int i = q0 + r;
-    float y1 = 0.f, y2 = 0.f;
+    uint4 o1 = make_uint4(0, 0, 0, 0), o2 = o1;
     if (i < a.Lq) {
-      const float x1 = __bfloat162float(Q[static_cast<long long>(i) * a.ldq + d]);
-      const float x2 = __bfloat162float(Q[static_cast<long long>(i) * a.ldq + d + HALF]);
+      const __nv_bfloat16* qr = Q + static_cast<long long>(i) * a.ldq;
+      const uint4 u1 = *reinterpret_cast<const uint4*>(qr + d0);
+      const uint4 u2 = *reinterpret_cast<const uint4*>(qr + d0 + HALF);
+      const __nv_bfloat162* h1 = reinterpret_cast<const __nv_bfloat162*>(&u1);
+      const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&u2);
+      __nv_bfloat162* p1 = reinterpret_cast<__nv_bfloat162*>(&o1);
+      __nv_bfloat162* p2 = reinterpret_cast<__nv_bfloat162*>(&o2);
       if (a.cos) {
-        const float c = a.cos[static_cast<long long>(i) * HALF + d];
-        const float s = a.sin[static_cast<long long>(i) * HALF + d];
-        y1 = __fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, s));
-        y2 = __fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, s));
+        const float4* c4 = reinterpret_cast<const float4*>(a.cos + static_cast<long long>(i) * HALF + d0);
+        const float4* s4 = reinterpret_cast<const float4*>(a.sin + static_cast<long long>(i) * HALF + d0);
+        const float4 ca = c4[0], cb = c4[1], sa = s4[0], sb = s4[1];
+        const float cs[8] = {ca.x, ca.y, ca.z, ca.w, cb.x, cb.y, cb.z, cb.w};
+        const float sn[8] = {sa.x, sa.y, sa.z, sa.w, sb.x, sb.y, sb.z, sb.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 x1 = __bfloat1622float2(h1[e]), x2 = __bfloat1622float2(h2[e]);
+          const float c0 = cs[2 * e], c1 = cs[2 * e + 1], s0 = sn[2 * e], s1 = sn[2 * e + 1];
+          p1[e] = __floats2bfloat162_rn(__fsub_rn(__fmul_rn(x1.x, c0), __fmul_rn(x2.x, s0)),
+                                        __fsub_rn(__fmul_rn(x1.y, c1), __fmul_rn(x2.y, s1)));
+          p2[e] = __floats2bfloat162_rn(__fadd_rn(__fmul_rn(x2.x, c0), __fmul_rn(x1.x, s0)),
+                                        __fadd_rn(__fmul_rn(x2.y, c1), __fmul_rn(x1.y, s1)));
+        }
       } else {
-        y1 = x1;
-        y2 = x2;
+        o1 = u1;
+        o2 = u2;
       }
     }
-    sQ[r * LDS + d] = __float2bfloat16_rn(y1);
-    sQ[r * LDS + d + HALF] = __float2bfloat16_rn(y2);
+    *reinterpret_cast<uint4*>(sQ + r * LDS + d0) = o1;
+    *reinterpret_cast<uint4*>(sQ + r * LDS + d0 + HALF) = o2;
   }
   __syncthreads();
 
@@ -255,7 +272,6 @@ __global__ void __launch_bounds__(128) attention_kernel(const AttnArgs a) {
       }
     }
   }
-  grid_dep_launch();
 }
 
 template <int HD>
@@ -268,8 +284,7 @@ int launch_attention(const AttnArgs& a, int batch, cudaStream_t stream) {
     configured = true;
   }
   dim3 grid((a.Lq + 63) / 64, a.nq, batch);
-  attention_kernel<HD><<<grid, 128, smem, stream>>>(a);
-  return cudaGetLastError() == cudaSuccess ? SO101_OK : SO101_ERR_LAUNCH;
+  return launch_kernel(attention_kernel<HD>, dim3(grid), dim3(128), smem, stream, a);
 }
 
 }  // namespace so101
@@ -292,6 +307,9 @@ extern "C" int so101_attention(const void* q, int64_t ldq, const void* k, int64_
       (ldv * 2) % 16 || (bk * 2) % 16 || (bv * 2) % 16)
     return SO101_ERR_ARG;
   if (reinterpret_cast<uintptr_t>(o) % 4 || ldo % 2 || bo % 2) return SO101_ERR_ARG;
+  // q rows and the rotary tables are read in 16-byte pieces
+  if (reinterpret_cast<uintptr_t>(q) % 16 || (ldq * 2) % 16 || (bq * 2) % 16) return SO101_ERR_ARG;
+  if (cos && (reinterpret_cast<uintptr_t>(cos) % 16 || reinterpret_cast<uintptr_t>(sin) % 16)) return SO101_ERR_ARG;
   AttnArgs a;
   a.q = static_cast<const __nv_bfloat16*>(q);
   a.k = static_cast<const __nv_bfloat16*>(k);

@@ -19,6 +19,27 @@ __device__ __forceinline__ void record_error(int* status, int code) {
 // Host side: the device address of the status word on the current device.
 int* status_ptr();
 
+// Host side: whether launches carry the programmatic-dependent-launch attribute (so101_set_pdl).
+bool pdl_enabled();
+
+// Launch `kern` on `stream`, with programmatic dependent launch when enabled: the kernel may then
+// start while the previous kernel on the stream drains, and waits (griddepcontrol.wait) before
+// it touches that kernel's results. Returns SO101_OK or SO101_ERR_LAUNCH.
+template <typename... KArgs, typename... Args>
+int launch_kernel(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream, Args... args) {
+  cudaLaunchConfig_t lc = {};
+  lc.gridDim = grid;
+  lc.blockDim = block;
+  lc.dynamicSmemBytes = smem;
+  lc.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  lc.attrs = attr;
+  lc.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&lc, kern, static_cast<KArgs>(args)...) == cudaSuccess ? SO101_OK : SO101_ERR_LAUNCH;
+}
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
@@ -206,18 +227,82 @@ __device__ __forceinline__ void grid_dep_launch() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
-// ---------------------------------------------------------------------------------- numerics
-__device__ __forceinline__ float gelu_tanh(float x) {
-  const float k0 = 0.7978845608028654f;  // sqrt(2 / pi)
-  return 0.5f * x * (1.0f + tanhf(k0 * (x + 0.044715f * x * x * x)));
+// ---------------------------------------------------------------------------------- clusters
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
 }
 
-__device__ __forceinline__ float silu(float x) { return x / (1.0f + expf(-x)); }
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Address of the same shared-memory offset in cluster CTA `rank`, and a load through it.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t saddr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+  return r;
+}
+
+__device__ __forceinline__ float ld_cluster_f32(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ float4 ld_cluster_f32x4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
+}
+
+// ---------------------------------------------------------------------------------- numerics
+// Epilogue math stays off the transcendental (XU) pipe except for one tanh.approx per element.
+
+// tanh on the hardware approximation (max abs error ~2^-11, far below a bf16 or int8 step).
+__device__ __forceinline__ float tanh_fast(float x) {
+  float y;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// GELU, tanh form: 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3))).
+__device__ __forceinline__ float gelu_tanh(float x) {
+  const float k0 = 0.7978845608028654f;
+  return 0.5f * x * (1.0f + tanh_fast(k0 * fmaf(0.044715f * x, x * x, x)));
+}
+
+// SiLU through sigmoid(x) = (1 + tanh(x / 2)) / 2.
+__device__ __forceinline__ float silu(float x) { return 0.5f * x * (1.0f + tanh_fast(0.5f * x)); }
+
+// int32 -> fp32 correctly rounded on the FMA pipe: v = hi * 2^16 + lo, each half converted exactly
+// by adding it to the bit pattern of a power of two (1.5 * 2^23 for the signed high half, 2^23 for
+// the unsigned low half), then one fused multiply-add rounds once.
+__device__ __forceinline__ float i32_to_f32(int v) {
+  const int hi = v >> 16;
+  const int lo = v & 0xFFFF;
+  const float fhi = __int_as_float(0x4B400000 + hi) - 12582912.0f;
+  const float flo = __int_as_float(0x4B000000 | lo) - 8388608.0f;
+  return fmaf(fhi, 65536.0f, flo);
+}
+
+// clamp(round_half_even(v / scale), -128, 127) without a divide or a float-to-int convert: the
+// quotient from the reciprocal plus one exact-remainder correction, clamped, then rounded by
+// adding 1.5 * 2^23 (the add rounds to nearest even) and read back from the bit pattern.
+__device__ __forceinline__ int quant_i8_int(float v, float scale, float inv_scale) {
+  float q = v * inv_scale;
+  const float r = fmaf(-q, scale, v);
+  q = fmaf(r, inv_scale, q);
+  q = fminf(fmaxf(q, -128.0f), 127.0f);
+  return __float_as_int(q + 12582912.0f) - 0x4B400000;
+}
 
 __device__ __forceinline__ int8_t quant_i8(float v, float scale) {
-  float q = rintf(v / scale);
-  q = fminf(fmaxf(q, -128.0f), 127.0f);
-  return static_cast<int8_t>(static_cast<int>(q));
+  return static_cast<int8_t>(quant_i8_int(v, scale, 1.0f / scale));
 }
 
 }  // namespace so101

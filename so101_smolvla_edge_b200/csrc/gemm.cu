@@ -1,23 +1,32 @@
 // tcgen05 GEMM for sm_100a: y = epilogue(x @ w^T), TMA-fed shared-memory ring, TMEM accumulator.
 //
-// One template serves every linear of the chunk:
-//   normal  (SWAP = false)  token rows on the 128-row MMA M side, features on MMA N (BN). For the
-//                           vision tower (M = 3072 per chunk) and batched prefix/expert.
-//   swap    (SWAP = true)   weight rows on the 128-row MMA M side, the few token rows (<= 64, the
-//                           action expert's 50) on MMA N. Weight streaming: each CTA streams a
-//                           128 x K slab of W once; the 50 rows never pad to 128.
-//   DUAL                    two weight tiles per stage (gate rows n and up rows N + n of the fused
-//                           [gate; up] matrix) into two accumulators; the epilogue multiplies
-//                           silu(gate) * up, so the SwiGLU never leaves the kernel.
-//   split-K                 grid.z splits K. Each split stores its fp32 (int32 for int8) partial
-//                           and takes a ticket; the last split to arrive sums all partials in
-//                           split order and runs the epilogue, then zeroes the ticket. Wait-free
-//                           and deterministic: a CUDA graph replay gives the same bits.
+// Two kernels serve every linear of the chunk.
 //
-// Warp roles (128 threads): warp 0 lane 0 issues TMA, warp 1 lane 0 issues tcgen05.mma and owns
-// the TMEM allocation; all four warps run the epilogue, warp w reading TMEM lanes [32w, 32w+32).
-// Shared memory per stage: P tile(s) 128 x 128 B and Q tile(s) BN x 128 B, SWIZZLE_128B as TMA
-// writes them, which is the canonical K-major layout the MMA descriptors name.
+// gemm_tc_kernel (one output tile per CTA, 128 threads)
+//   normal  (SWAP = false)  token rows on the 128-row MMA M side, features on MMA N (BN).
+//   swap    (SWAP = true)   weight rows on the 128-row MMA M side, the few token rows (<= 64, the
+//                           action expert's 50) on MMA N: weight streaming, each CTA reads a
+//                           128 x K slab of W once and the 50 rows never pad to 128.
+//   split-K over grid.z, deterministic, two ways:
+//     cluster  the splits of a tile form one thread-block cluster; each CTA stages its fp32
+//              partial in its own shared memory, and after a cluster barrier CTA r sums rows
+//              [r*128/S, (r+1)*128/S) over all S CTAs in split order (DSMEM reads) and runs the
+//              epilogue for them. No global round trip, no workspace.
+//     global   each split stores its partial to a workspace and takes a ticket; the last split to
+//              arrive sums all partials in split order, runs the epilogue and zeroes the ticket.
+//   Warp roles: warp 0 lane 0 issues TMA, warp 1 lane 0 issues tcgen05.mma and owns TMEM; all four
+//   warps run the epilogue, warp w reading TMEM lanes [32w, 32w+32).
+//
+// gemm_persistent_kernel (normal tiling for large M, 1 CTA per SM, 320 threads)
+//   Each CTA loops over output tiles. Warp 0 streams A/B tiles through the ring, warp 1 issues the
+//   MMAs into one of two TMEM accumulators (2 x BN columns) and eight epilogue warps drain the other,
+//   so the epilogue of tile i overlaps the MMAs of tile i+1. Epilogue warp e reads lane quadrant
+//   (e + 2) % 4 and column half e / 4.
+//
+// DUAL (SiLU gate): two weight tiles per stage (gate rows n and up rows N + n of the fused
+// [gate; up] matrix) into two accumulators; the epilogue writes silu(gate) * up.
+// Shared-memory tiles are 128-byte K rows in TMA SWIZZLE_128B layout, the canonical K-major layout
+// the MMA descriptors name. No TMA multicast anywhere.
 #include <cstdio>
 #include <mutex>
 
@@ -25,9 +34,11 @@
 
 namespace so101 {
 
+constexpr int kMaxSplitCluster = 8;  // portable cluster size: the most K splits reduced on chip
+
 struct GemmArgs {
   int M, N, K;  // N: output features (half of w's rows for SILU_GATE)
-  int kb_total, kb_per_split, splits, tiles_q;
+  int kb_total, kb_per_split, splits, tiles_q, num_tiles;
   void* y;
   long long ldy;
   int y_type;
@@ -40,11 +51,12 @@ struct GemmArgs {
   float out_scale;
   const float* w_scale;
   float x_scale;
-  float y_qscale;
+  float y_qscale, y_qinv;
   long long row_group, row_stride;
   void* ws;
   int* tickets;
   int vec_ok;
+  int cluster_reduce;
   int* status;
 };
 
@@ -53,26 +65,48 @@ __device__ __forceinline__ float load_elem(const void* p, long long i, int type)
   return __bfloat162float(static_cast<const __nv_bfloat16*>(p)[i]);
 }
 
-__device__ __forceinline__ void store_elem(void* p, long long i, int type, float v, float qs) {
-  if (type == SO101_F32)
-    static_cast<float*>(p)[i] = v;
-  else if (type == SO101_BF16)
-    static_cast<__nv_bfloat16*>(p)[i] = __float2bfloat16_rn(v);
-  else
-    static_cast<int8_t*>(p)[i] = quant_i8(v, qs);
+__device__ __forceinline__ long long out_row(const GemmArgs& a, int m) {
+  return a.row_group > 0 ? (m / a.row_group) * a.row_stride + m % a.row_group : m;
 }
 
-// Epilogue of 16 accumulator values that share P index p and have Q indices [qb, qb + 16).
+// Epilogue of one accumulator element (m, n); u is the up-projection accumulator for SILU_GATE.
+template <bool DUAL, bool I8>
+__device__ __forceinline__ void epilogue1(const GemmArgs& a, int m, int n, float v, float u) {
+  if (m >= a.M || n >= a.N) return;
+  float x = v;
+  if (I8) x *= a.x_scale * __ldg(a.w_scale + n);
+  if (a.bias) x += __ldg(a.bias + n);
+  if (a.epilogue == SO101_EPI_GELU) {
+    x = gelu_tanh(x);
+  } else if (DUAL) {
+    float up = u;
+    if (I8) up *= a.x_scale * __ldg(a.w_scale + a.N + n);
+    x = silu(x) * up;
+  }
+  x *= a.out_scale;
+  const long long row = out_row(a, m);
+  if (a.res) {
+    const long long rrow = a.r_period > 0 ? m % a.r_period : row;
+    x += load_elem(a.res, rrow * a.ldr + n, a.r_type);
+  }
+  const long long i = row * a.ldy + n;
+  if (a.y_type == SO101_F32)
+    static_cast<float*>(a.y)[i] = x;
+  else if (a.y_type == SO101_BF16)
+    static_cast<__nv_bfloat16*>(a.y)[i] = __float2bfloat16_rn(x);
+  else
+    static_cast<int8_t*>(a.y)[i] = static_cast<int8_t>(quant_i8_int(x, a.y_qscale, a.y_qinv));
+}
+
+// Epilogue of 16 accumulator values sharing P index p, Q indices [qb, qb + 16).
 template <bool SWAP, bool DUAL, bool I8>
-__device__ __forceinline__ void epilogue16(const GemmArgs& a, int p, int qb, float (&v)[16],
-                                           float (&u)[16]) {
+__device__ __forceinline__ void epilogue16(const GemmArgs& a, int p, int qb, float (&v)[16], float (&u)[16]) {
   if (!SWAP) {
-    // one output row m = p, 16 consecutive columns: vector path when fully inside and aligned
     const int m = p;
     if (m >= a.M) return;
-    const long long row = a.row_group > 0 ? (m / a.row_group) * a.row_stride + m % a.row_group : m;
-    const long long rrow = a.r_period > 0 ? m % a.r_period : row;
     if (a.vec_ok && qb + 16 <= a.N) {
+      const long long row = out_row(a, m);
+      const long long rrow = a.r_period > 0 ? m % a.r_period : row;
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
         const int n = qb + j;
@@ -90,26 +124,24 @@ __device__ __forceinline__ void epilogue16(const GemmArgs& a, int p, int qb, flo
       }
       if (a.res) {
         if (a.r_type == SO101_F32) {
-          const float4* r4 = reinterpret_cast<const float4*>(static_cast<const float*>(a.res) +
-                                                             rrow * a.ldr + qb);
+          const float4* r4 = reinterpret_cast<const float4*>(static_cast<const float*>(a.res) + rrow * a.ldr + qb);
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
-            float4 r = r4[j];
+            const float4 r = r4[j];
             v[4 * j] += r.x;
             v[4 * j + 1] += r.y;
             v[4 * j + 2] += r.z;
             v[4 * j + 3] += r.w;
           }
         } else {
-          const uint4* r4 = reinterpret_cast<const uint4*>(
-              static_cast<const __nv_bfloat16*>(a.res) + rrow * a.ldr + qb);
+          const uint4* r4 = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(a.res) + rrow * a.ldr + qb);
 #pragma unroll
           for (int j = 0; j < 2; ++j) {
             uint4 r = r4[j];
             const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&r);
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
-              float2 f = __bfloat1622float2(h[e]);
+              const float2 f = __bfloat1622float2(h[e]);
               v[8 * j + 2 * e] += f.x;
               v[8 * j + 2 * e + 1] += f.y;
             }
@@ -119,8 +151,7 @@ __device__ __forceinline__ void epilogue16(const GemmArgs& a, int p, int qb, flo
       if (a.y_type == SO101_F32) {
         float4* y4 = reinterpret_cast<float4*>(static_cast<float*>(a.y) + row * a.ldy + qb);
 #pragma unroll
-        for (int j = 0; j < 4; ++j)
-          y4[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+        for (int j = 0; j < 4; ++j) y4[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
       } else if (a.y_type == SO101_BF16) {
         uint4 o[2];
         __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(o);
@@ -130,11 +161,16 @@ __device__ __forceinline__ void epilogue16(const GemmArgs& a, int p, int qb, flo
         y4[0] = o[0];
         y4[1] = o[1];
       } else {
-        uint4 o;
-        int8_t* b = reinterpret_cast<int8_t*>(&o);
+        uint32_t w4[4];
 #pragma unroll
-        for (int e = 0; e < 16; ++e) b[e] = quant_i8(v[e], a.y_qscale);
-        *reinterpret_cast<uint4*>(static_cast<int8_t*>(a.y) + row * a.ldy + qb) = o;
+        for (int e = 0; e < 4; ++e) {
+          const uint32_t b0 = quant_i8_int(v[4 * e], a.y_qscale, a.y_qinv) & 0xFF;
+          const uint32_t b1 = quant_i8_int(v[4 * e + 1], a.y_qscale, a.y_qinv) & 0xFF;
+          const uint32_t b2 = quant_i8_int(v[4 * e + 2], a.y_qscale, a.y_qinv) & 0xFF;
+          const uint32_t b3 = quant_i8_int(v[4 * e + 3], a.y_qscale, a.y_qinv) & 0xFF;
+          w4[e] = b0 | (b1 << 8) | (b2 << 16) | (b3 << 24);
+        }
+        *reinterpret_cast<uint4*>(static_cast<int8_t*>(a.y) + row * a.ldy + qb) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
       }
       return;
     }
@@ -142,35 +178,22 @@ __device__ __forceinline__ void epilogue16(const GemmArgs& a, int p, int qb, flo
 #pragma unroll 4
   for (int j = 0; j < 16; ++j) {
     const int q = qb + j;
-    const int m = SWAP ? q : p;
-    const int n = SWAP ? p : q;
-    if (m >= a.M || n >= a.N) continue;
-    float x = v[j];
-    if (I8) x *= a.x_scale * __ldg(a.w_scale + n);
-    if (a.bias) x += __ldg(a.bias + n);
-    if (a.epilogue == SO101_EPI_GELU) {
-      x = gelu_tanh(x);
-    } else if (DUAL) {
-      float up = u[j];
-      if (I8) up *= a.x_scale * __ldg(a.w_scale + a.N + n);
-      x = silu(x) * up;
-    }
-    x *= a.out_scale;
-    const long long row = a.row_group > 0 ? (m / a.row_group) * a.row_stride + m % a.row_group : m;
-    if (a.res) {
-      const long long rrow = a.r_period > 0 ? m % a.r_period : row;
-      x += load_elem(a.res, rrow * a.ldr + n, a.r_type);
-    }
-    store_elem(a.y, row * a.ldy + n, a.y_type, x, a.y_qscale);
+    epilogue1<DUAL, I8>(a, SWAP ? q : p, SWAP ? p : q, v[j], u[j]);
   }
 }
 
+template <bool I8>
+__device__ __forceinline__ float acc_value(uint32_t r) {
+  return I8 ? i32_to_f32(static_cast<int>(r)) : __uint_as_float(r);
+}
+
+// ================================================================ one tile per CTA
 template <int BN, bool SWAP, bool DUAL, bool I8>
 __global__ void __launch_bounds__(128, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
                    const GemmArgs a, const int stages) {
-  constexpr int NA = (SWAP && DUAL) ? 2 : 1;  // tiles on the MMA M side per stage
-  constexpr int NB = (!SWAP && DUAL) ? 2 : 1; // tiles on the MMA N side per stage
+  constexpr int NA = (SWAP && DUAL) ? 2 : 1;   // tiles on the MMA M side per stage
+  constexpr int NB = (!SWAP && DUAL) ? 2 : 1;  // tiles on the MMA N side per stage
   constexpr int A_BYTES = 128 * 128;
   constexpr int B_BYTES = BN * 128;
   constexpr int STAGE_BYTES = NA * A_BYTES + NB * B_BYTES;
@@ -210,14 +233,14 @@ __global__ void __launch_bounds__(128, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  grid_dep_launch();  // the next kernel may start its own prologue and weight prefetch
 
   if (warp == 0 && lane == 0) {
-    // ---------------- TMA producer: weights first (independent of the previous kernel), then
-    // wait for the previous grid before the first activation load.
+    // TMA producer: the first stages' weight tiles go out before waiting for the previous grid
     tma_prefetch_desc(&tm_x);
     tma_prefetch_desc(&tm_w);
-    const uint64_t pol_w = policy_evict_first();
-    const uint64_t pol_x = policy_evict_last();
+    const uint64_t pol_w = SWAP ? policy_evict_first() : policy_evict_last();
+    const uint64_t pol_x = SWAP ? policy_evict_last() : policy_evict_first();
     bool waited = false;
     for (int i = 0; i < nkb; ++i) {
       const int s = i % stages;
@@ -226,20 +249,17 @@ __global__ void __launch_bounds__(128, 1)
       uint8_t* st = smem + s * STAGE_BYTES;
       mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
       const int kx = (kb0 + i) * KB_ELEMS;
-      // weight tiles
       if (SWAP) {
 #pragma unroll
         for (int t = 0; t < NA; ++t) tma_load_2d(st + t * A_BYTES, &tm_w, &full[s], kx, p0 + t * a.N, pol_w);
       } else {
 #pragma unroll
-        for (int t = 0; t < NB; ++t)
-          tma_load_2d(st + NA * A_BYTES + t * B_BYTES, &tm_w, &full[s], kx, q0 + t * a.N, pol_w);
+        for (int t = 0; t < NB; ++t) tma_load_2d(st + NA * A_BYTES + t * B_BYTES, &tm_w, &full[s], kx, q0 + t * a.N, pol_w);
       }
       if (!waited) {
         grid_dep_wait();
         waited = true;
       }
-      // activation tile
       if (SWAP)
         tma_load_2d(st + NA * A_BYTES, &tm_x, &full[s], kx, q0, pol_x);
       else
@@ -247,7 +267,7 @@ __global__ void __launch_bounds__(128, 1)
     }
     if (!waited) grid_dep_wait();
   } else if (warp == 1 && lane == 0) {
-    // ---------------- MMA issuer
+    // MMA issuer
     for (int i = 0; i < nkb; ++i) {
       const int s = i % stages;
       const uint32_t round = static_cast<uint32_t>(i / stages);
@@ -284,7 +304,6 @@ __global__ void __launch_bounds__(128, 1)
   // ---------------- epilogue: all 128 threads, thread t owns TMEM lane t (P index p0 + t)
   mbar_wait(accum, 0, a.status);
   tc_fence_after();
-  grid_dep_launch();
   const int t = threadIdx.x;
   const uint32_t lane_addr = tmem + (static_cast<uint32_t>(warp * 32) << 16);
   const int p = p0 + t;
@@ -298,11 +317,121 @@ __global__ void __launch_bounds__(128, 1)
       tmem_ld_wait();
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
-        v[j] = I8 ? static_cast<float>(static_cast<int>(r0[j])) : __uint_as_float(r0[j]);
-        u[j] = DUAL ? (I8 ? static_cast<float>(static_cast<int>(r1[j])) : __uint_as_float(r1[j])) : 0.f;
+        v[j] = acc_value<I8>(r0[j]);
+        u[j] = DUAL ? acc_value<I8>(r1[j]) : 0.f;
       }
       epilogue16<SWAP, DUAL, I8>(a, p, q0 + c, v, u);
     }
+  } else if (a.cluster_reduce) {
+    // stage this split's partial (column-major, lane contiguous) in the now idle stage ring
+    float* part = reinterpret_cast<float*>(smem);
+#pragma unroll 1
+    for (int c = 0; c < NACC; c += 16) {
+      uint32_t r[16];
+      tmem_ld16(lane_addr + c, r);
+      tmem_ld_wait();
+#pragma unroll
+      for (int j = 0; j < 16; ++j) part[(c + j) * 128 + t] = acc_value<I8>(r[j]);
+    }
+    cluster_sync();
+    // CTA `rank` reduces row quads [rank*32/S, (rank+1)*32/S): per (quad, column) one 16-byte DSMEM
+    // load from every split, all in flight before the sum, which runs in split order
+    const int S = a.splits;
+    const int rank = static_cast<int>(cluster_ctarank());
+    const int qlo = rank * 32 / S, qhi = (rank + 1) * 32 / S, nq = qhi - qlo;
+    const uint32_t part_addr = smem_u32(part);
+    uint32_t peer[kMaxSplitCluster];
+#pragma unroll
+    for (int s = 0; s < kMaxSplitCluster; ++s) peer[s] = mapa_shared(part_addr, static_cast<uint32_t>(s < S ? s : 0));
+    if (SWAP && !DUAL && !I8 && a.vec_ok) {
+      // two items per pass, every load (partials, bias, residual) issued before any store: the
+      // output may alias the residual, so the compiler could not reorder them itself
+      const int total = nq * BN;
+      for (int base = 0; base < total; base += 2 * 128) {
+        float4 pv[2][kMaxSplitCluster], bia[2], res[2];
+        int ok[2], col[2], quad[2];
+#pragma unroll
+        for (int it = 0; it < 2; ++it) {
+          const int idx = base + it * 128 + t;
+          ok[it] = idx < total;
+          quad[it] = qlo + (ok[it] ? idx % nq : 0);
+          col[it] = ok[it] ? idx / nq : 0;
+          const int m = q0 + col[it], n = p0 + quad[it] * 4;
+          ok[it] = ok[it] && m < a.M && n < a.N;
+          const uint32_t off = static_cast<uint32_t>((col[it] * 128 + quad[it] * 4) * 4);
+#pragma unroll
+          for (int sp = 0; sp < kMaxSplitCluster; ++sp)
+            if (sp < S) pv[it][sp] = ld_cluster_f32x4(peer[sp] + off);
+          bia[it] = make_float4(0.f, 0.f, 0.f, 0.f);
+          res[it] = bia[it];
+          if (ok[it] && n + 4 <= a.N) {
+            if (a.bias) bia[it] = __ldg(reinterpret_cast<const float4*>(a.bias + n));
+            if (a.res && a.r_type == SO101_F32)
+              res[it] = *reinterpret_cast<const float4*>(static_cast<const float*>(a.res) +
+                                                        (a.r_period > 0 ? m % a.r_period : out_row(a, m)) * a.ldr + n);
+          }
+        }
+#pragma unroll
+        for (int it = 0; it < 2; ++it) {
+          if (!ok[it]) continue;
+          float4 sv = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+          for (int sp = 0; sp < kMaxSplitCluster; ++sp)
+            if (sp < S) sv.x += pv[it][sp].x, sv.y += pv[it][sp].y, sv.z += pv[it][sp].z, sv.w += pv[it][sp].w;
+          const int m = q0 + col[it], n = p0 + quad[it] * 4;
+          if (n + 4 > a.N || (a.res && a.r_type != SO101_F32) || a.epilogue != SO101_EPI_NONE) {
+            const float vv[4] = {sv.x, sv.y, sv.z, sv.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) epilogue1<DUAL, I8>(a, m, n + e, vv[e], 0.f);
+            continue;
+          }
+          float4 x = make_float4((sv.x + bia[it].x) * a.out_scale + res[it].x, (sv.y + bia[it].y) * a.out_scale + res[it].y,
+                                 (sv.z + bia[it].z) * a.out_scale + res[it].z, (sv.w + bia[it].w) * a.out_scale + res[it].w);
+          const long long yi = out_row(a, m) * a.ldy + n;
+          if (a.y_type == SO101_F32) {
+            *reinterpret_cast<float4*>(static_cast<float*>(a.y) + yi) = x;
+          } else if (a.y_type == SO101_BF16) {
+            __nv_bfloat162 h[2] = {__floats2bfloat162_rn(x.x, x.y), __floats2bfloat162_rn(x.z, x.w)};
+            *reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(a.y) + yi) = *reinterpret_cast<uint2*>(h);
+          } else {
+            const float vv[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+              static_cast<int8_t*>(a.y)[yi + e] = static_cast<int8_t>(quant_i8_int(vv[e], a.y_qscale, a.y_qinv));
+          }
+        }
+      }
+    } else {
+      for (int idx = t; idx < nq * BN; idx += 128) {
+        const int quad = qlo + idx % nq, col = idx / nq;
+        const uint32_t off = static_cast<uint32_t>((col * 128 + quad * 4) * 4);
+        const uint32_t off_u = static_cast<uint32_t>(((BN + col) * 128 + quad * 4) * 4);
+        float4 pv[kMaxSplitCluster], pu[kMaxSplitCluster];
+#pragma unroll
+        for (int sp = 0; sp < kMaxSplitCluster; ++sp) {
+          if (sp < S) {
+            pv[sp] = ld_cluster_f32x4(peer[sp] + off);
+            if (DUAL) pu[sp] = ld_cluster_f32x4(peer[sp] + off_u);
+          }
+        }
+        float4 sv = make_float4(0.f, 0.f, 0.f, 0.f), su = sv;
+#pragma unroll
+        for (int sp = 0; sp < kMaxSplitCluster; ++sp) {
+          if (sp < S) {
+            sv.x += pv[sp].x, sv.y += pv[sp].y, sv.z += pv[sp].z, sv.w += pv[sp].w;
+            if (DUAL) su.x += pu[sp].x, su.y += pu[sp].y, su.z += pu[sp].z, su.w += pu[sp].w;
+          }
+        }
+        const float vv[4] = {sv.x, sv.y, sv.z, sv.w}, uu[4] = {su.x, su.y, su.z, su.w};
+        const int qq = q0 + col;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int pp = p0 + quad * 4 + e;
+          epilogue1<DUAL, I8>(a, SWAP ? qq : pp, SWAP ? pp : qq, vv[e], uu[e]);
+        }
+      }
+    }
+    cluster_sync();  // no CTA leaves while a peer still reads its shared memory
   } else {
     const int tile = p_tile * a.tiles_q + q_tile;
     uint32_t* ws = static_cast<uint32_t*>(a.ws);
@@ -341,18 +470,25 @@ __global__ void __launch_bounds__(128, 1)
           }
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
-            v[j] = static_cast<float>(iv[j]);
-            u[j] = static_cast<float>(iu[j]);
+            v[j] = i32_to_f32(iv[j]);
+            u[j] = i32_to_f32(iu[j]);
           }
         } else {
+          // all splits' values for 16 columns in flight before the ordered sum
+          float pv[16], pu[16];
 #pragma unroll
           for (int j = 0; j < 16; ++j) v[j] = u[j] = 0.f;
           for (int s = 0; s < a.splits; ++s) {
             const uint32_t* ps = base + static_cast<size_t>(s) * NACC * 128;
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
-              v[j] += __uint_as_float(__ldcg(ps + (c + j) * 128 + t));
-              if (DUAL) u[j] += __uint_as_float(__ldcg(ps + (BN + c + j) * 128 + t));
+              pv[j] = __uint_as_float(__ldcg(ps + (c + j) * 128 + t));
+              pu[j] = DUAL ? __uint_as_float(__ldcg(ps + (BN + c + j) * 128 + t)) : 0.f;
+            }
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              v[j] += pv[j];
+              u[j] += pu[j];
             }
           }
         }
@@ -367,13 +503,173 @@ __global__ void __launch_bounds__(128, 1)
   if (warp == 1) tmem_dealloc(tmem, TMEM_COLS);
 }
 
+// ================================================================ persistent, warp-specialized
+constexpr int kEpiWarps = 8;
+
+template <int BN, bool DUAL, bool I8>
+__global__ void __launch_bounds__(32 * (2 + kEpiWarps), 1)
+    gemm_persistent_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
+                           const GemmArgs a, const int stages) {
+  constexpr int A_BYTES = 128 * 128;
+  constexpr int B_BYTES = BN * 128;
+  constexpr int NB = DUAL ? 2 : 1;
+  constexpr int STAGE_BYTES = A_BYTES + NB * B_BYTES;
+  constexpr int NACC = BN * NB;
+  constexpr uint32_t TMEM_COLS = 2 * NACC <= 128 ? 128 : 2 * NACC <= 256 ? 256 : 512;
+  constexpr uint32_t IDESC = I8 ? idesc_i8(128, BN) : idesc_bf16(128, BN);
+  constexpr int KB_ELEMS = I8 ? 128 : 64;
+  static_assert(2 * NACC <= 512, "two accumulators must fit in TMEM");
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + stages * STAGE_BYTES);
+  uint64_t* empty = full + stages;
+  uint64_t* acc_full = empty + stages;  // [2]
+  uint64_t* acc_empty = acc_full + 2;   // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < stages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], kEpiWarps);
+    }
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int kb_total = a.kb_total;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tm_x);
+      tma_prefetch_desc(&tm_w);
+      const uint64_t pol_w = policy_evict_last();
+      const uint64_t pol_x = policy_evict_first();
+      bool waited = false, ok = true;
+      int it = 0;
+      for (int tile = blockIdx.x; tile < a.num_tiles && ok; tile += gridDim.x) {
+        const int p0 = (tile / a.tiles_q) * 128, q0 = (tile % a.tiles_q) * BN;
+        for (int kb = 0; kb < kb_total; ++kb, ++it) {
+          const int s = it % stages;
+          const uint32_t round = static_cast<uint32_t>(it / stages);
+          if (it >= stages && !mbar_wait(&empty[s], (round - 1) & 1u, a.status)) {
+            ok = false;
+            break;
+          }
+          uint8_t* st = smem + s * STAGE_BYTES;
+          mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
+          const int kx = kb * KB_ELEMS;
+#pragma unroll
+          for (int t = 0; t < NB; ++t) tma_load_2d(st + A_BYTES + t * B_BYTES, &tm_w, &full[s], kx, q0 + t * a.N, pol_w);
+          if (!waited) {
+            grid_dep_wait();
+            waited = true;
+          }
+          tma_load_2d(st, &tm_x, &full[s], kx, p0, pol_x);
+        }
+      }
+      if (!waited) grid_dep_wait();
+      grid_dep_launch();
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      int it = 0, local = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < a.num_tiles && ok; tile += gridDim.x, ++local) {
+        const int buf = local & 1;
+        const uint32_t use = static_cast<uint32_t>(local >> 1);
+        if (local >= 2 && !mbar_wait(&acc_empty[buf], (use - 1) & 1u, a.status)) break;
+        tc_fence_after();
+        const uint32_t d = tmem + static_cast<uint32_t>(buf * NACC);
+        for (int kb = 0; kb < kb_total; ++kb, ++it) {
+          const int s = it % stages;
+          const uint32_t round = static_cast<uint32_t>(it / stages);
+          if (!mbar_wait(&full[s], round & 1u, a.status)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t base = smem_u32(smem + s * STAGE_BYTES);
+          const uint64_t a0 = sw128_desc(base);
+          const uint64_t b0 = sw128_desc(base + A_BYTES);
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const uint32_t acc = (kb > 0 || k > 0) ? 1u : 0u;
+            if (I8)
+              mma_i8(d, a0 + 2 * k, b0 + 2 * k, IDESC, acc);
+            else
+              mma_f16(d, a0 + 2 * k, b0 + 2 * k, IDESC, acc);
+            if (DUAL) {
+              const uint64_t b1 = sw128_desc(base + A_BYTES + B_BYTES);
+              if (I8)
+                mma_i8(d + BN, a0 + 2 * k, b1 + 2 * k, IDESC, acc);
+              else
+                mma_f16(d + BN, a0 + 2 * k, b1 + 2 * k, IDESC, acc);
+            }
+          }
+          mma_commit(&empty[s]);
+        }
+        mma_commit(&acc_full[buf]);
+      }
+    }
+  } else {
+    // epilogue warps
+    grid_dep_wait();
+    const int e = warp - 2;
+    const int quad = warp & 3;
+    constexpr int HALF = BN / 2;
+    const int c_lo = (e / 4) * HALF;
+    int local = 0;
+    for (int tile = blockIdx.x; tile < a.num_tiles; tile += gridDim.x, ++local) {
+      const int buf = local & 1;
+      const uint32_t use = static_cast<uint32_t>(local >> 1);
+      if (!mbar_wait(&acc_full[buf], use & 1u, a.status)) break;
+      tc_fence_after();
+      const int p0 = (tile / a.tiles_q) * 128, q0 = (tile % a.tiles_q) * BN;
+      const int p = p0 + quad * 32 + lane;
+      const uint32_t taddr = tmem + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(buf * NACC);
+      float v[16], u[16];
+#pragma unroll 1
+      for (int c = c_lo; c < c_lo + HALF; c += 16) {
+        uint32_t r0[16], r1[16];
+        tmem_ld16(taddr + c, r0);
+        if (DUAL) tmem_ld16(taddr + BN + c, r1);
+        tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          v[j] = acc_value<I8>(r0[j]);
+          u[j] = DUAL ? acc_value<I8>(r1[j]) : 0.f;
+        }
+        epilogue16<false, DUAL, I8>(a, p, q0 + c, v, u);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[buf]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) tmem_dealloc(tmem, TMEM_COLS);
+}
+
 // ============================================================================ host side
 namespace {
 
 using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                              const cuuint64_t*, const cuuint32_t*, const cuuint32_t*,
-                              CUtensorMapInterleave, CUtensorMapSwizzle, CUtensorMapL2promotion,
-                              CUtensorMapFloatOOBfill);
+                              const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                              CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
 EncodeFn encode_fn() {
   static EncodeFn fn = nullptr;
@@ -389,8 +685,7 @@ EncodeFn encode_fn() {
 }
 
 // 2-D K-major tensor map over rows x inner (elements), row stride ld elements, 128-byte boxes.
-int make_map(CUtensorMap* m, const void* ptr, bool i8, long long inner, long long rows, long long ld,
-             int box_rows) {
+int make_map(CUtensorMap* m, const void* ptr, bool i8, long long inner, long long rows, long long ld, int box_rows) {
   EncodeFn enc = encode_fn();
   if (!enc) return SO101_ERR_DRIVER;
   const int esize = i8 ? 1 : 2;
@@ -398,10 +693,9 @@ int make_map(CUtensorMap* m, const void* ptr, bool i8, long long inner, long lon
   cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * esize};
   cuuint32_t box[2] = {static_cast<cuuint32_t>(128 / esize), static_cast<cuuint32_t>(box_rows)};
   cuuint32_t estr[2] = {1, 1};
-  CUresult r = enc(m, i8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
-                   const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  CUresult r = enc(m, i8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr),
+                   dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? SO101_OK : SO101_ERR_ARG;
 }
 
@@ -418,22 +712,29 @@ int stage_bytes(int bn, bool swap, bool dual) {
 }
 
 constexpr int kSmemBudget = 220 * 1024;
+constexpr int kMaxCluster = kMaxSplitCluster;
+
+enum Kind { kTile = 0, kPersistent = 1 };
 
 struct Plan {
   so101_gemm_config cfg;
-  int kb_total, kb_per_split, splits, tiles_p, tiles_q, nacc;
+  int kind;
+  int kb_total, kb_per_split, splits, tiles_p, tiles_q, nacc, cluster;
 };
 
 int ceil_div(long long a, long long b) { return static_cast<int>((a + b - 1) / b); }
 
-int plan_gemm(int a_type, long long M, long long N, long long K, int epi, const so101_gemm_config* in,
-              Plan* pl) {
+int plan_gemm(int a_type, long long M, long long N, long long K, int epi, const so101_gemm_config* in, Plan* pl) {
   const bool dual = epi == SO101_EPI_SILU_GATE;
   const int kb_elems = a_type == SO101_I8 ? 128 : 64;
-  so101_gemm_config c = in ? *in : so101_gemm_config{0, 0, 0, 0};
+  so101_gemm_config c = in ? *in : so101_gemm_config{0, 0, 0, 0, 0};
   so101_gemm_config pick;
   so101_gemm_pick(a_type, M, N, K, epi, &pick);
-  if (!in || (c.bn == 0 && c.swap == 0 && c.splits == 0 && c.stages == 0)) c = pick;
+  if (!in || (c.bn == 0 && c.swap == 0 && c.splits == 0 && c.stages == 0)) {
+    const int flags = c.flags;
+    c = pick;
+    c.flags |= flags;
+  }
   if (c.bn == 0) c.bn = pick.bn;
   if (c.splits <= 0) c.splits = 1;
   if (c.swap) {
@@ -443,94 +744,143 @@ int plan_gemm(int a_type, long long M, long long N, long long K, int epi, const 
     if (c.bn != 64 && c.bn != 128 && c.bn != 256) return SO101_ERR_ARG;
     if (dual && c.bn == 256) return SO101_ERR_ARG;
   }
-  const int sb = stage_bytes(c.bn, c.swap, dual);
-  const int max_st = (kSmemBudget - 1024 - 256) / sb;
-  if (c.stages <= 0) c.stages = max_st < 8 ? max_st : 8;
-  if (c.stages < 2 || c.stages > max_st) return SO101_ERR_ARG;
   pl->kb_total = ceil_div(K, kb_elems);
-  int splits = c.splits > pl->kb_total ? pl->kb_total : c.splits;
+  const int splits = c.splits > pl->kb_total ? pl->kb_total : c.splits;
   pl->kb_per_split = ceil_div(pl->kb_total, splits);
   pl->splits = ceil_div(pl->kb_total, pl->kb_per_split);  // no empty split
   c.splits = pl->splits;
   pl->tiles_p = c.swap ? ceil_div(N, 128) : ceil_div(M, 128);
   pl->tiles_q = c.swap ? ceil_div(M, c.bn) : ceil_div(N, c.bn);
   pl->nacc = c.bn * (dual ? 2 : 1);
+  const long long tiles = static_cast<long long>(pl->tiles_p) * pl->tiles_q;
+  pl->kind = kTile;
+  if (!c.swap && pl->splits == 1 && !(c.flags & SO101_GEMM_ONE_TILE_PER_CTA) &&
+      ((c.flags & SO101_GEMM_PERSISTENT) || tiles >= sm_count()))
+    pl->kind = kPersistent;
+  pl->cluster = 1;
+  if (pl->kind == kTile && pl->splits > 1 && pl->splits <= kMaxCluster && !(c.flags & SO101_GEMM_GLOBAL_SPLITK))
+    pl->cluster = pl->splits;
+  const int sb = stage_bytes(c.bn, c.swap, dual);
+  const int max_st = (kSmemBudget - 1024 - 256) / sb;
+  if (c.stages <= 0) {
+    int want = pl->kind == kPersistent ? 8 : pl->kb_per_split;
+    if (want < 2) want = 2;
+    c.stages = want < max_st ? want : max_st;
+    if (c.stages > 8) c.stages = 8;
+  }
+  if (c.stages < 2 || c.stages > max_st) return SO101_ERR_ARG;
+  if (pl->cluster > 1 && c.stages * sb < pl->nacc * 128 * 4) {
+    // the cluster reduction stages the partial in the ring: make it big enough
+    const int need = ceil_div(static_cast<long long>(pl->nacc) * 512, sb);
+    if (need > max_st) return SO101_ERR_ARG;
+    c.stages = need;
+  }
   pl->cfg = c;
   return SO101_OK;
 }
 
-template <int BN, bool SWAP, bool DUAL, bool I8>
-int launch_inst(const CUtensorMap& tx, const CUtensorMap& tw, const GemmArgs& a, const Plan& pl,
-                cudaStream_t stream, bool pdl) {
-  auto kern = gemm_tc_kernel<BN, SWAP, DUAL, I8>;
-  const int smem = pl.cfg.stages * stage_bytes(BN, SWAP, DUAL) + 1024 + 256;
-  static int configured = 0;
-  if (configured < smem) {
+template <typename Kern>
+int launch(Kern kern, const CUtensorMap& tx, const CUtensorMap& tw, const GemmArgs& a, dim3 grid, int threads,
+           int smem, int cluster, int stages, cudaStream_t stream, bool pdl, int* configured) {
+  if (*configured == 0) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBudget) != cudaSuccess)
       return SO101_ERR_LAUNCH;
-    configured = kSmemBudget;
+    *configured = 1;
   }
   cudaLaunchConfig_t lc = {};
-  lc.gridDim = dim3(pl.tiles_q, pl.tiles_p, pl.splits);
-  lc.blockDim = dim3(128, 1, 1);
+  lc.gridDim = grid;
+  lc.blockDim = dim3(threads, 1, 1);
   lc.dynamicSmemBytes = smem;
   lc.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchAttribute attr[2];
+  int n = 0;
+  if (pdl) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  if (cluster > 1) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = 1;
+    attr[n].val.clusterDim.y = 1;
+    attr[n].val.clusterDim.z = cluster;
+    ++n;
+  }
   lc.attrs = attr;
-  lc.numAttrs = pdl ? 1 : 0;
-  cudaError_t e = cudaLaunchKernelEx(&lc, kern, tx, tw, a, pl.cfg.stages);
+  lc.numAttrs = n;
+  const cudaError_t e = cudaLaunchKernelEx(&lc, kern, tx, tw, a, stages);
   return e == cudaSuccess ? SO101_OK : SO101_ERR_LAUNCH;
 }
 
+template <int BN, bool SWAP, bool DUAL, bool I8>
+int launch_tile(const CUtensorMap& tx, const CUtensorMap& tw, const GemmArgs& a, const Plan& pl, cudaStream_t stream,
+                bool pdl) {
+  static int configured = 0;
+  const int smem = pl.cfg.stages * stage_bytes(BN, SWAP, DUAL) + 1024 + 256;
+  return launch(gemm_tc_kernel<BN, SWAP, DUAL, I8>, tx, tw, a, dim3(pl.tiles_q, pl.tiles_p, pl.splits), 128, smem,
+                pl.cluster, pl.cfg.stages, stream, pdl, &configured);
+}
+
+template <int BN, bool DUAL, bool I8>
+int launch_persistent(const CUtensorMap& tx, const CUtensorMap& tw, const GemmArgs& a, const Plan& pl,
+                      cudaStream_t stream, bool pdl) {
+  static int configured = 0;
+  const int smem = pl.cfg.stages * stage_bytes(BN, false, DUAL) + 1024 + 256;
+  const long long tiles = static_cast<long long>(pl.tiles_p) * pl.tiles_q;
+  const int sms = sm_count();
+  const int grid = static_cast<int>(tiles < sms ? tiles : sms);
+  return launch(gemm_persistent_kernel<BN, DUAL, I8>, tx, tw, a, dim3(grid, 1, 1), 32 * (2 + kEpiWarps), smem, 1,
+                pl.cfg.stages, stream, pdl, &configured);
+}
+
 template <bool SWAP, bool DUAL, bool I8>
-int launch_bn(const CUtensorMap& tx, const CUtensorMap& tw, const GemmArgs& a, const Plan& pl,
-              cudaStream_t stream, bool pdl) {
+int launch_bn(const CUtensorMap& tx, const CUtensorMap& tw, const GemmArgs& a, const Plan& pl, cudaStream_t stream,
+              bool pdl) {
   if constexpr (SWAP) {
     switch (pl.cfg.bn) {
-      case 16: return launch_inst<16, SWAP, DUAL, I8>(tx, tw, a, pl, stream, pdl);
-      case 32: return launch_inst<32, SWAP, DUAL, I8>(tx, tw, a, pl, stream, pdl);
-      case 48: return launch_inst<48, SWAP, DUAL, I8>(tx, tw, a, pl, stream, pdl);
-      case 64: return launch_inst<64, SWAP, DUAL, I8>(tx, tw, a, pl, stream, pdl);
+      case 16: return launch_tile<16, SWAP, DUAL, I8>(tx, tw, a, pl, stream, pdl);
+      case 32: return launch_tile<32, SWAP, DUAL, I8>(tx, tw, a, pl, stream, pdl);
+      case 48: return launch_tile<48, SWAP, DUAL, I8>(tx, tw, a, pl, stream, pdl);
+      case 64: return launch_tile<64, SWAP, DUAL, I8>(tx, tw, a, pl, stream, pdl);
     }
   } else {
+    const bool pers = pl.kind == kPersistent;
     switch (pl.cfg.bn) {
-      case 64: return launch_inst<64, SWAP, DUAL, I8>(tx, tw, a, pl, stream, pdl);
-      case 128: return launch_inst<128, SWAP, DUAL, I8>(tx, tw, a, pl, stream, pdl);
+      case 64:
+        return pers ? launch_persistent<64, DUAL, I8>(tx, tw, a, pl, stream, pdl)
+                    : launch_tile<64, SWAP, DUAL, I8>(tx, tw, a, pl, stream, pdl);
+      case 128:
+        return pers ? launch_persistent<128, DUAL, I8>(tx, tw, a, pl, stream, pdl)
+                    : launch_tile<128, SWAP, DUAL, I8>(tx, tw, a, pl, stream, pdl);
       case 256:
-        if constexpr (!DUAL) return launch_inst<256, SWAP, DUAL, I8>(tx, tw, a, pl, stream, pdl);
+        if constexpr (!DUAL)
+          return pers ? launch_persistent<256, DUAL, I8>(tx, tw, a, pl, stream, pdl)
+                      : launch_tile<256, SWAP, DUAL, I8>(tx, tw, a, pl, stream, pdl);
         break;
     }
   }
   return SO101_ERR_ARG;
 }
 
-bool g_pdl = false;
-
 }  // namespace
 }  // namespace so101
 
 using namespace so101;
 
-extern "C" int so101_set_pdl(int enable) {
-  g_pdl = enable != 0;
-  return SO101_OK;
-}
-
-extern "C" int so101_gemm_pick(int a_type, int64_t M, int64_t N, int64_t K, int epilogue,
-                               so101_gemm_config* cfg) {
+extern "C" int so101_gemm_pick(int a_type, int64_t M, int64_t N, int64_t K, int epilogue, so101_gemm_config* cfg) {
   if (!cfg) return SO101_ERR_ARG;
   const bool dual = epilogue == SO101_EPI_SILU_GATE;
   const int kb_elems = a_type == SO101_I8 ? 128 : 64;
   const int kb = static_cast<int>((K + kb_elems - 1) / kb_elems);
   const int sms = sm_count();
-  so101_gemm_config c = {0, 0, 1, 0};
+  so101_gemm_config c = {0, 0, 1, 0, 0};
   if (M <= 64 && a_type == SO101_BF16) {
+    // weight streaming: one 128-row weight slab per CTA, K split across a cluster to fill the GPU
     c.swap = 1;
     c.bn = M <= 16 ? 16 : M <= 32 ? 32 : M <= 48 ? 48 : 64;
     const int tiles = static_cast<int>((N + 127) / 128);
     int s = sms / tiles;
+    if (s > kMaxCluster) s = kMaxCluster;
     const int max_s = kb / 2 > 0 ? kb / 2 : 1;  // at least two K blocks per split
     c.splits = s < 1 ? 1 : (s > max_s ? max_s : s);
   } else {
@@ -543,31 +893,30 @@ extern "C" int so101_gemm_pick(int a_type, int64_t M, int64_t N, int64_t K, int 
       int s = static_cast<int>(sms / tiles);
       const int max_s = kb / 4 > 0 ? kb / 4 : 1;
       c.splits = s > max_s ? max_s : s;
+      if (c.splits > kMaxCluster) c.splits = kMaxCluster;
     }
   }
-  const int sb = stage_bytes(c.bn, c.swap, dual);
-  const int max_st = (kSmemBudget - 1024 - 256) / sb;
-  c.stages = max_st < 8 ? max_st : 8;
+  c.stages = 0;  // chosen by the plan from the problem and the kernel kind
   *cfg = c;
   return SO101_OK;
 }
 
 extern "C" int so101_gemm_workspace(int a_type, int64_t M, int64_t N, int64_t K, int epilogue,
-                                    const so101_gemm_config* cfg, int64_t* workspace_bytes,
-                                    int64_t* n_tickets) {
+                                    const so101_gemm_config* cfg, int64_t* workspace_bytes, int64_t* n_tickets) {
   Plan pl;
-  int rc = plan_gemm(a_type, M, N, K, epilogue, cfg, &pl);
+  const int rc = plan_gemm(a_type, M, N, K, epilogue, cfg, &pl);
   if (rc) return rc;
   const long long tiles = static_cast<long long>(pl.tiles_p) * pl.tiles_q;
-  if (workspace_bytes) *workspace_bytes = pl.splits > 1 ? tiles * pl.splits * pl.nacc * 128 * 4 : 0;
-  if (n_tickets) *n_tickets = pl.splits > 1 ? tiles : 0;
+  const bool global = pl.splits > 1 && pl.cluster == 1;
+  if (workspace_bytes) *workspace_bytes = global ? tiles * pl.splits * pl.nacc * 128 * 4 : 0;
+  if (n_tickets) *n_tickets = global ? tiles : 0;
   return SO101_OK;
 }
 
-extern "C" int so101_gemm(int a_type, const void* x, int64_t ldx, const void* w, int64_t ldw, void* y,
-                          int64_t ldy, int y_type, int64_t M, int64_t N, int64_t K,
-                          const so101_epilogue* epi, const so101_gemm_config* cfg, void* workspace,
-                          int64_t workspace_bytes, int* tickets, int64_t n_tickets, cudaStream_t stream) {
+extern "C" int so101_gemm(int a_type, const void* x, int64_t ldx, const void* w, int64_t ldw, void* y, int64_t ldy,
+                          int y_type, int64_t M, int64_t N, int64_t K, const so101_epilogue* epi,
+                          const so101_gemm_config* cfg, void* workspace, int64_t workspace_bytes, int* tickets,
+                          int64_t n_tickets, cudaStream_t stream) {
   if (!x || !w || !y || !epi) return SO101_ERR_ARG;
   if (a_type != SO101_BF16 && a_type != SO101_I8) return SO101_ERR_ARG;
   if (M <= 0 || N <= 0 || K <= 0) return SO101_ERR_ARG;
@@ -577,20 +926,20 @@ extern "C" int so101_gemm(int a_type, const void* x, int64_t ldx, const void* w,
   if (reinterpret_cast<uintptr_t>(x) % 16 || reinterpret_cast<uintptr_t>(w) % 16) return SO101_ERR_ARG;
   if (ldx < K || ldw < K) return SO101_ERR_ARG;
   if (y_type != SO101_BF16 && y_type != SO101_F32 && y_type != SO101_I8) return SO101_ERR_ARG;
-  const bool dual = epi->epilogue == SO101_EPI_SILU_GATE;
   if (epi->epilogue < 0 || epi->epilogue > 2) return SO101_ERR_ARG;
+  const bool dual = epi->epilogue == SO101_EPI_SILU_GATE;
   if (a_type == SO101_I8 && !epi->w_scale) return SO101_ERR_ARG;
+  if (y_type == SO101_I8 && !(epi->y_qscale > 0.f)) return SO101_ERR_ARG;
   if (ldy < N && epi->row_group <= 0) return SO101_ERR_ARG;
   Plan pl;
   int rc = plan_gemm(a_type, M, N, K, epi->epilogue, cfg, &pl);
   if (rc) return rc;
   const long long tiles = static_cast<long long>(pl.tiles_p) * pl.tiles_q;
-  if (pl.splits > 1) {
-    if (!workspace || !tickets || n_tickets < tiles ||
-        workspace_bytes < tiles * pl.splits * pl.nacc * 128 * 4)
+  if (pl.splits > 1 && pl.cluster == 1) {
+    if (!workspace || !tickets || n_tickets < tiles || workspace_bytes < tiles * pl.splits * pl.nacc * 128 * 4)
       return SO101_ERR_WORKSPACE;
   }
-  if (pl.tiles_q > 65535 || pl.tiles_p > 65535) return SO101_ERR_ARG;
+  if (pl.tiles_q > 65535 || pl.tiles_p > 65535 || tiles > 0x7fffffffLL) return SO101_ERR_ARG;
   GemmArgs a = {};
   a.M = static_cast<int>(M);
   a.N = static_cast<int>(N);
@@ -599,6 +948,7 @@ extern "C" int so101_gemm(int a_type, const void* x, int64_t ldx, const void* w,
   a.kb_per_split = pl.kb_per_split;
   a.splits = pl.splits;
   a.tiles_q = pl.tiles_q;
+  a.num_tiles = static_cast<int>(tiles);
   a.y = y;
   a.ldy = ldy;
   a.y_type = y_type;
@@ -612,10 +962,12 @@ extern "C" int so101_gemm(int a_type, const void* x, int64_t ldx, const void* w,
   a.w_scale = epi->w_scale;
   a.x_scale = epi->x_scale;
   a.y_qscale = epi->y_qscale;
+  a.y_qinv = epi->y_qscale > 0.f ? static_cast<float>(1.0 / static_cast<double>(epi->y_qscale)) : 0.f;
   a.row_group = epi->row_group;
   a.row_stride = epi->row_stride;
   a.ws = workspace;
   a.tickets = tickets;
+  a.cluster_reduce = pl.cluster > 1 ? 1 : 0;
   a.status = status_ptr();
   const int ysz = y_type == SO101_F32 ? 4 : y_type == SO101_BF16 ? 2 : 1;
   bool vec = reinterpret_cast<uintptr_t>(y) % 16 == 0 && (ldy * ysz) % 16 == 0;
@@ -635,7 +987,7 @@ extern "C" int so101_gemm(int a_type, const void* x, int64_t ldx, const void* w,
   if (rc) return rc;
   rc = make_map(&tw, w, i8, K, w_rows, ldw, w_box);
   if (rc) return rc;
-  const bool pdl = g_pdl;
+  const bool pdl = pdl_enabled();
   if (pl.cfg.swap) {
     if (dual) return launch_bn<true, true, false>(tx, tw, a, pl, stream, pdl);
     return launch_bn<true, false, false>(tx, tw, a, pl, stream, pdl);

@@ -30,6 +30,8 @@ __device__ __forceinline__ float pixel(const uint8_t* __restrict__ img, int h, i
 
 __global__ void preprocess_kernel(const uint8_t* __restrict__ img, int n_img, int h, int w, int rh, int rw,
                                   int S, int P, void* __restrict__ out, int y_type, float qs) {
+  grid_dep_launch();
+  grid_dep_wait();
   const int G = S / P, F = 3 * P * P;
   const long long pairs = static_cast<long long>(n_img) * G * G * (F / 2);
   const long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
@@ -73,60 +75,83 @@ __global__ void preprocess_kernel(const uint8_t* __restrict__ img, int n_img, in
 }
 
 // ------------------------------------------------------------------ fp32 linear (CUDA cores)
-// 32 x 32 output tile per 128-thread block, each thread 2 rows x 4 columns, K in chunks of 32.
-constexpr int LF_BM = 32, LF_BN = 32, LF_BK = 32;
+// 64 x 8 output tile per 128-thread block (each thread 1 row x 4 columns), K in chunks of 32
+// streamed through a 3-stage cp.async ring so global latency overlaps the FMAs. Rows of x and w
+// are read in 16-byte pieces (K, ldx, ldw multiples of 4; 16-byte aligned bases).
+constexpr int LF_BM = 64, LF_BN = 8, LF_BK = 32, LF_ST = 3, LF_LD = LF_BK + 4, LF_THREADS = 128;
 
-__global__ void __launch_bounds__(128) linear_f32_kernel(const float* __restrict__ x, long long ldx,
+__device__ __forceinline__ void cp_async16_f(float* dst, const float* src, bool ok) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(ok ? 16 : 0)
+               : "memory");
+}
+
+__global__ void __launch_bounds__(LF_THREADS) linear_f32_kernel(const float* __restrict__ x, long long ldx,
                                                          const float* __restrict__ w, long long ldw,
                                                          const float* __restrict__ bias,
                                                          const float* __restrict__ bias2, float* __restrict__ y,
-                                                         long long ldy, int M, int N, int K, int silu_in) {
+                                                         long long ldy, int M, int N, int K, int act) {
+  grid_dep_launch();
   grid_dep_wait();
-  __shared__ float xs[LF_BK][LF_BM + 1];
-  __shared__ float ws[LF_BK][LF_BN + 1];
+  __shared__ __align__(16) float xs[LF_ST][LF_BM][LF_LD];
+  __shared__ __align__(16) float ws[LF_ST][LF_BN][LF_LD];
   const int m0 = blockIdx.y * LF_BM, n0 = blockIdx.x * LF_BN;
-  const int tx = threadIdx.x % 8, ty = threadIdx.x / 8;  // 8 column groups x 16 row groups
-  float acc[2][4] = {};
-  for (int k0 = 0; k0 < K; k0 += LF_BK) {
-    for (int i = threadIdx.x; i < LF_BM * LF_BK; i += 128) {
-      const int r = i / LF_BK, kk = i % LF_BK;
-      float v = 0.f;
-      if (m0 + r < M && k0 + kk < K) {
-        v = x[static_cast<long long>(m0 + r) * ldx + k0 + kk];
-        if (silu_in) v = silu(v);
-      }
-      xs[kk][r] = v;
-      const int c = i / LF_BK;
-      ws[kk][c] = (n0 + c < N && k0 + kk < K) ? w[static_cast<long long>(n0 + c) * ldw + k0 + kk] : 0.f;
+  const int tid = threadIdx.x;
+  const int row = tid / 2, cg = (tid % 2) * 4;  // this thread: row m0 + row, columns n0 + cg .. +3
+  const int nk = (K + LF_BK - 1) / LF_BK;
+
+  auto load = [&](int kc, int st) {
+    const int k0 = kc * LF_BK;
+    // x: 64 rows x 8 chunks of 16 bytes, four per thread; w: 8 rows x 8 chunks
+    for (int c = tid; c < LF_BM * (LF_BK / 4); c += LF_THREADS) {
+      const int r = c / (LF_BK / 4), kk = (c % (LF_BK / 4)) * 4;
+      const bool ok = m0 + r < M && k0 + kk < K;
+      cp_async16_f(&xs[st][r][kk], x + (ok ? static_cast<long long>(m0 + r) * ldx + k0 + kk : 0), ok);
     }
+    if (tid < LF_BN * (LF_BK / 4)) {
+      const int r = tid / (LF_BK / 4), kk = (tid % (LF_BK / 4)) * 4;
+      const bool ok = n0 + r < N && k0 + kk < K;
+      cp_async16_f(&ws[st][r][kk], w + (ok ? static_cast<long long>(n0 + r) * ldw + k0 + kk : 0), ok);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+
+  for (int st = 0; st < LF_ST - 1; ++st) {
+    if (st < nk)
+      load(st, st);
+    else
+      asm volatile("cp.async.commit_group;" ::: "memory");
+  }
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int kc = 0; kc < nk; ++kc) {
+    const int nxt = kc + LF_ST - 1;
+    if (nxt < nk)
+      load(nxt, nxt % LF_ST);
+    else
+      asm volatile("cp.async.commit_group;" ::: "memory");
+    asm volatile("cp.async.wait_group %0;" ::"n"(LF_ST - 1) : "memory");
     __syncthreads();
+    const int st = kc % LF_ST;
 #pragma unroll 8
     for (int kk = 0; kk < LF_BK; ++kk) {
-      const float a0 = xs[kk][ty * 2], a1 = xs[kk][ty * 2 + 1];
+      const float a = xs[st][row][kk];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float b = ws[kk][tx * 4 + j];
-        acc[0][j] = fmaf(a0, b, acc[0][j]);
-        acc[1][j] = fmaf(a1, b, acc[1][j]);
-      }
+      for (int j = 0; j < 4; ++j) acc[j] = fmaf(a, ws[st][cg + j][kk], acc[j]);
     }
     __syncthreads();
   }
-#pragma unroll
-  for (int i = 0; i < 2; ++i) {
-    const int m = m0 + ty * 2 + i;
-    if (m >= M) continue;
+  const int m = m0 + row;
+  if (m < M) {
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      const int n = n0 + tx * 4 + j;
+      const int n = n0 + cg + j;
       if (n >= N) continue;
-      float v = acc[i][j];
+      float v = acc[j];
       if (bias) v += bias[n];
       if (bias2) v += bias2[n];
+      if (act == 2) v = v / (1.0f + expf(-v));  // SiLU of the output, full fp32 accuracy
       y[static_cast<long long>(m) * ldy + n] = v;
     }
   }
-  grid_dep_launch();
 }
 
 // ------------------------------------------------------------------ expert head + Euler step
@@ -135,6 +160,7 @@ __global__ void __launch_bounds__(128) linear_f32_kernel(const float* __restrict
 __global__ void expert_out_kernel(const float* __restrict__ e, long long lde, const float* __restrict__ norm_w,
                                   float eps, const float* __restrict__ w_out, const float* __restrict__ b_out,
                                   float* __restrict__ x_t, long long ldx, int N, int K, float dt) {
+  grid_dep_launch();
   grid_dep_wait();
   extern __shared__ float h[];
   __shared__ float red[32];
@@ -169,29 +195,34 @@ __global__ void expert_out_kernel(const float* __restrict__ e, long long lde, co
     for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
     if (lane == 0) x_t[m * ldx + n] += dt * (acc + b_out[n]);
   }
-  grid_dep_launch();
 }
 
 // ------------------------------------------------------------------ prefix tail rows
-// block b: lang rows copied, then the state row from the normalised, zero-padded state.
+// grid (observations, chunks of 256 tail elements): element (r, c) of the (lang_len + 1) x d tail
+// is the task-token row r copied, or for r == lang_len the state row
+// state_w @ pad((state - mean) / (std + 1e-8)) + state_b.
 __global__ void prefix_tail_kernel(const float* __restrict__ state, int state_dim, const float* __restrict__ s_mean,
                                    const float* __restrict__ s_std, const float* __restrict__ state_w, int max_state,
                                    const float* __restrict__ state_b, const float* __restrict__ lang, int lang_len,
                                    int d, float* __restrict__ prefix, long long ldp, long long prefix_rows,
                                    long long tail_row) {
-  extern __shared__ float st[];
+  grid_dep_launch();
+  grid_dep_wait();
   const int b = blockIdx.x;
-  float* base = prefix + (static_cast<long long>(b) * prefix_rows + tail_row) * ldp;
-  for (int i = threadIdx.x; i < lang_len * d; i += blockDim.x) base[(i / d) * ldp + i % d] = lang[i];
-  for (int j = threadIdx.x; j < max_state; j += blockDim.x)
-    st[j] = j < state_dim ? (state[b * state_dim + j] - s_mean[j]) / (s_std[j] + 1e-8f) : 0.f;
-  __syncthreads();
-  float* srow = base + static_cast<long long>(lang_len) * ldp;
-  for (int n = threadIdx.x; n < d; n += blockDim.x) {
-    float acc = 0.f;
-    for (int j = 0; j < max_state; ++j) acc = fmaf(st[j], state_w[static_cast<long long>(n) * max_state + j], acc);
-    srow[n] = acc + state_b[n];
+  const long long idx = static_cast<long long>(blockIdx.y) * blockDim.x + threadIdx.x;
+  if (idx >= static_cast<long long>(lang_len + 1) * d) return;
+  const int r = static_cast<int>(idx / d), c = static_cast<int>(idx % d);
+  float* dst = prefix + (static_cast<long long>(b) * prefix_rows + tail_row + r) * ldp + c;
+  if (r < lang_len) {
+    *dst = lang[static_cast<long long>(r) * d + c];
+    return;
   }
+  float acc = 0.f;
+  for (int j = 0; j < state_dim; ++j) {
+    const float st = (state[static_cast<long long>(b) * state_dim + j] - s_mean[j]) / (s_std[j] + 1e-8f);
+    acc = fmaf(st, state_w[static_cast<long long>(c) * max_state + j], acc);
+  }
+  *dst = acc + state_b[c];
 }
 
 // ------------------------------------------------------------------ unnormalisation
@@ -200,6 +231,7 @@ __global__ void finish_kernel(const float* __restrict__ x_t, int max_action, con
                               const float* __restrict__ r_mean, const float* __restrict__ r_std,
                               const float* __restrict__ a_mean, const float* __restrict__ a_std,
                               float* __restrict__ out, int action_dim, int H, int repr) {
+  grid_dep_launch();
   grid_dep_wait();
   const int b = blockIdx.x, col = threadIdx.x;
   if (col >= action_dim) return;
@@ -226,9 +258,6 @@ __global__ void finish_kernel(const float* __restrict__ x_t, int max_action, con
 
 using namespace so101;
 
-namespace {
-int launched() { return cudaGetLastError() == cudaSuccess ? SO101_OK : SO101_ERR_LAUNCH; }
-}  // namespace
 
 extern "C" int so101_preprocess(const uint8_t* img, int n_img, int h, int w, int rh, int rw, int S, int P,
                                 void* patches, int y_type, float y_qscale, cudaStream_t stream) {
@@ -239,20 +268,21 @@ extern "C" int so101_preprocess(const uint8_t* img, int n_img, int h, int w, int
   const long long pairs = n_img * G * G * (3 * P * P / 2);
   const long long blocks = (pairs + 255) / 256;
   if (blocks > 0x7fffffffLL) return SO101_ERR_ARG;
-  preprocess_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(img, n_img, h, w, rh, rw, S, P, patches,
+  return launch_kernel(preprocess_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, stream,
+                       img, n_img, h, w, rh, rw, S, P, patches,
                                                                         y_type, y_qscale);
-  return launched();
 }
 
 extern "C" int so101_linear_f32(const float* x, int64_t ldx, const float* w, int64_t ldw, const float* bias,
                                 const float* bias2, float* y, int64_t ldy, int64_t M, int64_t N, int64_t K,
-                                int silu_in, cudaStream_t stream) {
+                                int act, cudaStream_t stream) {
   if (!x || !w || !y || M <= 0 || N <= 0 || K <= 0 || ldx < K || ldw < K || ldy < N) return SO101_ERR_ARG;
+  if (K % 4 || ldx % 4 || ldw % 4 || reinterpret_cast<uintptr_t>(x) % 16 || reinterpret_cast<uintptr_t>(w) % 16)
+    return SO101_ERR_ARG;
   const long long gy = (M + LF_BM - 1) / LF_BM, gx = (N + LF_BN - 1) / LF_BN;
   if (gy > 65535 || gx > 0x7fffffffLL) return SO101_ERR_ARG;
-  linear_f32_kernel<<<dim3(static_cast<unsigned>(gx), static_cast<unsigned>(gy)), 128, 0, stream>>>(
-      x, ldx, w, ldw, bias, bias2, y, ldy, static_cast<int>(M), static_cast<int>(N), static_cast<int>(K), silu_in);
-  return launched();
+  return launch_kernel(linear_f32_kernel, dim3(dim3(static_cast<unsigned>(gx), static_cast<unsigned>(gy))), dim3(LF_THREADS), 0, stream,
+                       x, ldx, w, ldw, bias, bias2, y, ldy, static_cast<int>(M), static_cast<int>(N), static_cast<int>(K), act);
 }
 
 extern "C" int so101_expert_out(const float* e, int64_t lde, const float* norm_w, float eps, const float* w_out,
@@ -260,9 +290,8 @@ extern "C" int so101_expert_out(const float* e, int64_t lde, const float* norm_w
                                 float dt, cudaStream_t stream) {
   if (!e || !norm_w || !w_out || !b_out || !x_t || M <= 0 || N <= 0 || K <= 0 || K > 8192) return SO101_ERR_ARG;
   if (M > 0x7fffffffLL) return SO101_ERR_ARG;
-  expert_out_kernel<<<static_cast<unsigned>(M), 256, K * sizeof(float), stream>>>(
-      e, lde, norm_w, eps, w_out, b_out, x_t, ldx, static_cast<int>(N), static_cast<int>(K), dt);
-  return launched();
+  return launch_kernel(expert_out_kernel, dim3(static_cast<unsigned>(M)), dim3(256), K * sizeof(float), stream,
+                       e, lde, norm_w, eps, w_out, b_out, x_t, ldx, static_cast<int>(N), static_cast<int>(K), dt);
 }
 
 extern "C" int so101_prefix_tail(const float* state, int state_dim, const float* s_mean, const float* s_std,
@@ -272,10 +301,11 @@ extern "C" int so101_prefix_tail(const float* state, int state_dim, const float*
   if (!state || !s_mean || !s_std || !state_w || !state_b || !prefix || batch <= 0 || d <= 0) return SO101_ERR_ARG;
   if (lang_len > 0 && !lang) return SO101_ERR_ARG;
   if (state_dim > max_state || max_state <= 0 || max_state > 4096) return SO101_ERR_ARG;
-  prefix_tail_kernel<<<batch, 256, max_state * sizeof(float), stream>>>(state, state_dim, s_mean, s_std, state_w,
+  const long long chunks = (static_cast<long long>(lang_len + 1) * d + 255) / 256;
+  if (chunks > 65535) return SO101_ERR_ARG;
+  return launch_kernel(prefix_tail_kernel, dim3(batch, static_cast<unsigned>(chunks)), dim3(256), 0, stream, state, state_dim, s_mean, s_std, state_w,
                                                                          max_state, state_b, lang, lang_len, d,
                                                                          prefix, ldp, prefix_rows, tail_row);
-  return launched();
 }
 
 extern "C" int so101_finish(const float* x_t, int max_action, const float* state, int state_dim,
@@ -285,8 +315,7 @@ extern "C" int so101_finish(const float* x_t, int max_action, const float* state
   if (!x_t || !state || !s_mean || !s_std || !r_mean || !r_std || !a_mean || !a_std || !out) return SO101_ERR_ARG;
   if (batch <= 0 || H <= 0 || action_dim <= 0 || action_dim > max_action || action_dim > 1024) return SO101_ERR_ARG;
   if (repr < 0 || repr > 2) return SO101_ERR_ARG;
-  finish_kernel<<<batch, ((action_dim + 31) / 32) * 32, 0, stream>>>(x_t, max_action, state, state_dim, s_mean,
+  return launch_kernel(finish_kernel, dim3(batch), dim3(((action_dim + 31) / 32) * 32), 0, stream, x_t, max_action, state, state_dim, s_mean,
                                                                        s_std, r_mean, r_std, a_mean, a_std, out,
                                                                        action_dim, H, repr);
-  return launched();
 }

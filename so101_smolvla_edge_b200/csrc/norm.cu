@@ -36,6 +36,7 @@ constexpr int kMaxRowPerLane = 32;  // rows up to 32 * 32 = 1024 wide stay in re
 __global__ void rms_norm_kernel(const void* __restrict__ x, long long ldx, int x_type,
                                 const float* __restrict__ w, void* __restrict__ y, long long ldy,
                                 int y_type, long long rows, int n, float eps) {
+  grid_dep_launch();
   grid_dep_wait();
   const long long row = static_cast<long long>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
@@ -55,7 +56,6 @@ __global__ void rms_norm_kernel(const void* __restrict__ x, long long ldx, int x
     const int c = lane + 32 * i;
     if (c < n) st_any(y, row * ldy + c, y_type, (v[i] * rstd) * w[c], 1.f);
   }
-  grid_dep_launch();
 }
 
 // ------------------------------------------------------------------ LayerNorm (+ pixel shuffle)
@@ -65,6 +65,7 @@ __global__ void layer_norm_kernel(const float* __restrict__ x, long long ldx, co
                                   const float* __restrict__ b, void* __restrict__ y, long long ldy,
                                   int y_type, float qs, long long rows, int n, float eps, int s,
                                   long long T) {
+  grid_dep_launch();
   grid_dep_wait();
   const long long row = static_cast<long long>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
@@ -99,7 +100,6 @@ __global__ void layer_norm_kernel(const float* __restrict__ x, long long ldx, co
     const int c = lane + 32 * i;
     if (c < n) st_any(y, out_row * ldy + col0 + c, y_type, (v[i] - mu) * rstd * w[c] + b[c], qs);
   }
-  grid_dep_launch();
 }
 
 // ------------------------------------------------------------------ RoPE + K/V cache write
@@ -111,6 +111,7 @@ __global__ void rope_kv_kernel(const __nv_bfloat16* __restrict__ qkv, long long 
                                __nv_bfloat16* __restrict__ k_out, long long ldk,
                                __nv_bfloat16* __restrict__ v_out, long long ldv, long long b_qkv,
                                long long b_k, long long b_v) {
+  grid_dep_launch();
   grid_dep_wait();
   const long long r = blockIdx.x;
   const int bi = blockIdx.y;
@@ -130,12 +131,13 @@ __global__ void rope_kv_kernel(const __nv_bfloat16* __restrict__ qkv, long long 
       vd[d + half] = src[(nq + nkv + h) * hd + d + half];
     }
   }
-  grid_dep_launch();
 }
 
 // ------------------------------------------------------------------ calibration and packing
 __global__ void absmax_kernel(const void* __restrict__ x, long long ldx, int x_type, long long rows,
                               long long n, float* amax) {
+  grid_dep_launch();
+  grid_dep_wait();
   float m = 0.f;
   const long long total = rows * n;
   for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
@@ -157,6 +159,8 @@ __global__ void absmax_kernel(const void* __restrict__ x, long long ldx, int x_t
 // one block per output channel n
 __global__ void quantize_weight_kernel(const void* __restrict__ w, int w_type, long long K,
                                        int8_t* __restrict__ wq, float* __restrict__ scale) {
+  grid_dep_launch();
+  grid_dep_wait();
   const long long n = blockIdx.x;
   float m = 0.f;
   for (long long k = threadIdx.x; k < K; k += blockDim.x) m = fmaxf(m, fabsf(ld_any(w, n * K + k, w_type)));
@@ -183,9 +187,6 @@ __global__ void quantize_weight_kernel(const void* __restrict__ w, int w_type, l
 
 using namespace so101;
 
-namespace {
-bool launch_ok() { return cudaGetLastError() == cudaSuccess; }
-}  // namespace
 
 extern "C" int so101_rms_norm(const void* x, int64_t ldx, int x_type, const float* w, void* y, int64_t ldy,
                               int y_type, int64_t rows, int64_t n, float eps, cudaStream_t stream) {
@@ -195,9 +196,8 @@ extern "C" int so101_rms_norm(const void* x, int64_t ldx, int x_type, const floa
   const int rows_per_block = 4;
   const long long blocks = (rows + rows_per_block - 1) / rows_per_block;
   if (blocks > 0x7fffffffLL) return SO101_ERR_ARG;
-  rms_norm_kernel<<<static_cast<unsigned>(blocks), 32 * rows_per_block, 0, stream>>>(
-      x, ldx, x_type, w, y, ldy, y_type, rows, static_cast<int>(n), eps);
-  return launch_ok() ? SO101_OK : SO101_ERR_LAUNCH;
+  return launch_kernel(rms_norm_kernel, dim3(static_cast<unsigned>(blocks)), dim3(32 * rows_per_block), 0, stream,
+                       x, ldx, x_type, w, y, ldy, y_type, rows, static_cast<int>(n), eps);
 }
 
 extern "C" int so101_layer_norm(const float* x, int64_t ldx, const float* w, const float* b, void* y,
@@ -214,10 +214,9 @@ extern "C" int so101_layer_norm(const float* x, int64_t ldx, const float* w, con
   }
   const int rows_per_block = 4;
   const long long blocks = (rows + rows_per_block - 1) / rows_per_block;
-  layer_norm_kernel<<<static_cast<unsigned>(blocks), 32 * rows_per_block, 0, stream>>>(
-      x, ldx, w, b, y, ldy, y_type, y_qscale, rows, static_cast<int>(n), eps, shuffle > 1 ? shuffle : 1,
+  return launch_kernel(layer_norm_kernel, dim3(static_cast<unsigned>(blocks)), dim3(32 * rows_per_block), 0, stream,
+                       x, ldx, w, b, y, ldy, y_type, y_qscale, rows, static_cast<int>(n), eps, shuffle > 1 ? shuffle : 1,
       shuffle > 1 ? tokens_per_image : 1);
-  return launch_ok() ? SO101_OK : SO101_ERR_LAUNCH;
 }
 
 extern "C" int so101_rope_kv(const void* qkv, int64_t ldqkv, int nq, int nkv, int hd, const float* cos,
@@ -227,10 +226,9 @@ extern "C" int so101_rope_kv(const void* qkv, int64_t ldqkv, int nq, int nkv, in
     return SO101_ERR_ARG;
   if (rows > 0x7fffffffLL || batch > 65535) return SO101_ERR_ARG;
   const int threads = nkv * hd / 2 < 256 ? ((nkv * hd / 2 + 31) / 32) * 32 : 256;
-  rope_kv_kernel<<<dim3(static_cast<unsigned>(rows), batch), threads, 0, stream>>>(
-      static_cast<const __nv_bfloat16*>(qkv), ldqkv, nq, nkv, hd, cos, sin, static_cast<__nv_bfloat16*>(k_out),
+  return launch_kernel(rope_kv_kernel, dim3(dim3(static_cast<unsigned>(rows), batch)), dim3(threads), 0, stream,
+                       static_cast<const __nv_bfloat16*>(qkv), ldqkv, nq, nkv, hd, cos, sin, static_cast<__nv_bfloat16*>(k_out),
       ldk, static_cast<__nv_bfloat16*>(v_out), ldv, b_qkv, b_k, b_v);
-  return launch_ok() ? SO101_OK : SO101_ERR_LAUNCH;
 }
 
 extern "C" int so101_absmax(const void* x, int64_t ldx, int x_type, int64_t rows, int64_t n, float* amax,
@@ -239,14 +237,14 @@ extern "C" int so101_absmax(const void* x, int64_t ldx, int x_type, int64_t rows
   if (x_type != SO101_F32 && x_type != SO101_BF16) return SO101_ERR_ARG;
   long long blocks = (rows * n + 255) / 256;
   if (blocks > 4096) blocks = 4096;
-  absmax_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(x, ldx, x_type, rows, n, amax);
-  return launch_ok() ? SO101_OK : SO101_ERR_LAUNCH;
+  return launch_kernel(absmax_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, stream,
+                       x, ldx, x_type, rows, n, amax);
 }
 
 extern "C" int so101_quantize_weight(const void* w, int w_type, int64_t N, int64_t K, int8_t* w_q, float* scale,
                                      cudaStream_t stream) {
   if (!w || !w_q || !scale || N <= 0 || K <= 0 || N > 0x7fffffffLL) return SO101_ERR_ARG;
   if (w_type != SO101_F32 && w_type != SO101_BF16) return SO101_ERR_ARG;
-  quantize_weight_kernel<<<static_cast<unsigned>(N), 256, 0, stream>>>(w, w_type, K, w_q, scale);
-  return launch_ok() ? SO101_OK : SO101_ERR_LAUNCH;
+  return launch_kernel(quantize_weight_kernel, dim3(static_cast<unsigned>(N)), dim3(256), 0, stream,
+                       w, w_type, K, w_q, scale);
 }

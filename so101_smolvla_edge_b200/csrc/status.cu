@@ -22,7 +22,15 @@ int* status_ptr() {
   return ptrs[dev];
 }
 
+bool g_pdl = false;
+bool pdl_enabled() { return g_pdl; }
+
 }  // namespace so101
+
+extern "C" int so101_set_pdl(int enable) {
+  so101::g_pdl = enable != 0;
+  return SO101_OK;
+}
 
 extern "C" int so101_device_status(void) {
   int v = 0;

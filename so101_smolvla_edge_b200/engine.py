@@ -21,6 +21,7 @@ from __future__ import annotations
 
 import json
 import logging
+import os
 import time
 from pathlib import Path
 
@@ -85,7 +86,7 @@ class Engine:
         kernels: str = "auto",
         batch: int = 1,
         act_clip: dict[str, float] | str | Path | None = None,
-        pdl: bool = False,
+        pdl: bool | None = None,
     ):
         self.device = dev = torch.device(device)
         if dev.type == "cuda" and dev.index is None:
@@ -117,7 +118,10 @@ class Engine:
         self.batch = int(batch)
         from . import ops
 
-        ops.set_pdl(pdl)
+        if pdl is None:  # programmatic dependent launch: on unless SO101_PDL=0
+            pdl = os.environ.get("SO101_PDL", "1") != "0"
+        self.pdl = bool(pdl)
+        ops.set_pdl(self.pdl)
         torch.cuda.set_device(dev)
         self.path = B200Path(b, dev, self.batch, trt_precision, clip)
         self.tp = self.path  # the reference's attribute for the custom-kernel path

@@ -387,10 +387,10 @@ class B200Path:
         tp = w["time_proj"][k]
         p.add(f"s{k}.act_time_in", self.lib.so101_linear_f32, x_in.data_ptr(), s.max_action,
               w["act.ain.w"].data_ptr(), s.max_action, w["act.ain.b"].data_ptr(), tp.data_ptr(),
-              self.h0.data_ptr(), s.exp_dim, M, s.exp_dim, s.max_action, 0)  # fmt: skip
+              self.h0.data_ptr(), s.exp_dim, M, s.exp_dim, s.max_action, 2)  # fmt: skip
         p.add(f"s{k}.time_out", self.lib.so101_linear_f32, self.h0.data_ptr(), s.exp_dim,
               w["act.time_out.w"].data_ptr(), s.exp_dim, w["act.time_out.b"].data_ptr(), None,
-              self.e.data_ptr(), s.exp_dim, M, s.exp_dim, s.exp_dim, 1)  # fmt: skip
+              self.e.data_ptr(), s.exp_dim, M, s.exp_dim, s.exp_dim, 0)  # fmt: skip
         e = self.e
         for i in range(s.n_layers):
             pre = f"exp.{i}."

@@ -104,16 +104,18 @@ def test_linear_epilogues(m, k, n, epi):
 
 
 @pytest.mark.parametrize("swap,bn", [(1, 16), (1, 32), (1, 48), (1, 64), (0, 64), (0, 128), (0, 256)])
-@pytest.mark.parametrize("split", [1, 2, 3, 7])
-def test_tiles_and_split_k_agree_and_repeat(swap, bn, split):
-    """Every tile shape and split count agrees with the reference and repeats bit for bit
-    (split-K is deterministic: `tests/test_kernels.py:231-243` of the reference)."""
+@pytest.mark.parametrize("split", [1, 2, 3, 7, 12])
+@pytest.mark.parametrize("flags", [0, 1])
+def test_tiles_and_split_k_agree_and_repeat(swap, bn, split, flags):
+    """Every tile shape, split count and split-K reduction (cluster / workspace) agrees with the
+    reference and repeats bit for bit (split-K is deterministic:
+    `tests/test_kernels.py:231-243` of the reference)."""
     from so101_smolvla_edge_b200.ops import linear
 
     x = rnd(50, 2048, dtype=torch.bfloat16)
     w = rnd(720, 2048, dtype=torch.bfloat16, scale=2048**-0.5, seed=1)
     r = rnd(50, 720, seed=2)
-    cfg = (swap, bn, split, 0)
+    cfg = (swap, bn, split, 0, flags)
     a = linear(x, w, residual=r, config=cfg)
     b = linear(x, w, residual=r, config=cfg)
     assert torch.equal(a, b)
@@ -121,14 +123,33 @@ def test_tiles_and_split_k_agree_and_repeat(swap, bn, split):
     assert ok, err
 
 
-@pytest.mark.parametrize("swap,bn,split", [(1, 64, 1), (1, 64, 5), (0, 128, 1), (0, 64, 3)])
-def test_silu_gate_tiles(swap, bn, split):
+@pytest.mark.parametrize("swap,bn,split,flags", [(1, 64, 1, 0), (1, 64, 5, 0), (1, 64, 5, 1), (0, 128, 1, 0),
+                                                 (0, 64, 3, 0), (0, 64, 3, 1), (0, 128, 1, 2)])
+def test_silu_gate_tiles(swap, bn, split, flags):
     from so101_smolvla_edge_b200.ops import linear
 
     x = rnd(50, 720, dtype=torch.bfloat16)
     w = rnd(4096, 720, dtype=torch.bfloat16, scale=720**-0.5, seed=1)
-    got = linear(x, w, silu_gate=True, config=(swap, bn, split, 0))
+    got = linear(x, w, silu_gate=True, config=(swap, bn, split, 0, flags))
     ok, err = close(got, gemm_ref(x, w, silu_gate=True), torch.bfloat16)
+    assert ok, err
+
+
+@pytest.mark.parametrize("m,n,k", [(3072, 2304, 768), (3072, 768, 3072), (1000, 5120, 960), (300, 720, 200)])
+@pytest.mark.parametrize("epi", ["gelu", "residual", "silu_gate"])
+@pytest.mark.parametrize("flags", [2, 4])
+def test_persistent_matches_one_tile_per_cta(m, n, k, epi, flags):
+    """The persistent kernel (flags 2) and one tile per CTA (flags 4) both match the reference,
+    including tile counts that are not a multiple of the grid."""
+    from so101_smolvla_edge_b200.ops import linear
+
+    x = rnd(m, k, dtype=torch.bfloat16)
+    w = rnd(2 * n if epi == "silu_gate" else n, k, dtype=torch.bfloat16, scale=k**-0.5, seed=1)
+    kw = {"gelu": {"gelu": True, "bias": rnd(n, seed=2)}, "residual": {"residual": rnd(m, n, seed=3)},
+          "silu_gate": {"silu_gate": True}}[epi]
+    bn = 128 if epi == "silu_gate" else 256
+    got = linear(x, w, config=(0, bn, 1, 0, flags), **kw)
+    ok, err = close(got, gemm_ref(x, w, **kw), got.dtype)
     assert ok, err
 
 
@@ -152,7 +173,8 @@ def test_strided_input_view():
 
 
 @pytest.mark.parametrize("m,k,n", [(3072, 768, 2304), (3072, 3072, 768), (192, 12288, 960), (50, 768, 64)])
-def test_int8_gemm_is_the_fake_quant_product(m, k, n):
+@pytest.mark.parametrize("flags", [0, 2, 4])
+def test_int8_gemm_is_the_fake_quant_product(m, k, n, flags):
     """W8A8: int8 x and w with per-tensor / per-channel scales give the float product of the
     dequantized operands (exact int32 accumulation)."""
     from so101_smolvla_edge_b200.ops import linear, quantize_weight
@@ -168,10 +190,15 @@ def test_int8_gemm_is_the_fake_quant_product(m, k, n):
     xs = 0.05
     xq = torch.randint(-128, 128, (m, k), device="cuda", dtype=torch.int8)
     b = rnd(n, seed=2)
-    got = linear(xq, wq, bias=b, x_scale=xs, w_scale=ws, out_dtype=torch.float32)
+    cfg = None if flags == 0 else (0, 128, 1, 0, flags)
+    got = linear(xq, wq, bias=b, x_scale=xs, w_scale=ws, out_dtype=torch.float32, config=cfg)
     want = (xq.double() @ wq.double().T) * xs * ws.double() + b.double()
     err = (got.double() - want).abs().max()
     assert err <= 1e-5 * want.abs().max() + 1e-5, float(err)
+    # int8 output: requantized by 1 / y_qscale, round half to even, clamped
+    yq = linear(xq, wq, bias=b, x_scale=xs, w_scale=ws, out_dtype=torch.int8, y_qscale=0.25, config=cfg)
+    want_q = torch.clamp(torch.round(want / 0.25), -128, 127)
+    assert (yq.double() - want_q).abs().max() <= 1
 
 
 # ---------------------------------------------------------------------------------- attention

@@ -38,10 +38,11 @@ def _close(got, want):
     return bool(err.max() <= 2 * eps * want.float().abs().max() + 1e-4)
 
 
+# flags 1 = SO101_GEMM_GLOBAL_SPLITK: reduce through scratch memory rather than a cluster
 @pytest.mark.parametrize("m,n,k,cfg,gate", [
-    (50, 720, 2048, (1, 64, 4, 0), False),     # the expert's down projection, split 4 ways
-    (50, 2048, 720, (1, 64, 3, 0), True),      # gate_up with the SiLU gate, split 3 ways
-    (241, 960, 2560, (0, 128, 5, 0), False),   # prefix down, tokens on the MMA M side
+    (50, 720, 2048, (1, 64, 4, 0, 1), False),     # the expert's down projection, split 4 ways
+    (50, 2048, 720, (1, 64, 3, 0, 1), True),      # gate_up with the SiLU gate, split 3 ways
+    (241, 960, 2560, (0, 128, 5, 0, 1), False),   # prefix down, tokens on the MMA M side
 ])  # fmt: skip
 def test_static_scratch_gemm_matches_workspace_gemm(m, n, k, cfg, gate):
     L, lib, static = _bind()
@@ -85,7 +86,7 @@ def test_static_scratch_refuses_plans_beyond_its_size():
     w = torch.zeros(n, k, dtype=torch.bfloat16, device="cuda")
     y = torch.zeros(m, n, dtype=torch.bfloat16, device="cuda")
     epi = L.Epilogue(epilogue=L.EPI_NONE, out_scale=1.0)
-    c = L.GemmConfig(0, 256, 8, 0)  # 288 tiles x 8 splits x 256 x 128 x 4 B: far beyond 8 MiB
+    c = L.GemmConfig(0, 256, 8, 0, 1)  # 288 tiles x 8 splits x 256 x 128 x 4 B: far beyond 8 MiB
     rc = static(L.BF16, x.data_ptr(), k, w.data_ptr(), k, y.data_ptr(), n, L.BF16, m, n, k,
                 C.byref(epi), C.byref(c), torch.cuda.current_stream().cuda_stream)
     assert rc == L.ERR_WORKSPACE
