@@ -26,6 +26,7 @@ struct AttnArgs {
   const float* cos;
   const float* sin;
   float scale_log2;
+  int kv_splits;  // > 1: the key tiles are split over a cluster of this many CTAs
 };
 
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
@@ -62,7 +63,7 @@ __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
-template <int HD>
+template <int HD, bool SPLIT>
 __global__ void __launch_bounds__(128) attention_kernel(const AttnArgs a) {
   constexpr int BM = 64, BN = 64, LDS = HD + 8, HALF = HD / 2;
   constexpr int CHUNKS = HD / 8;  // 16-byte chunks per row
@@ -74,7 +75,9 @@ __global__ void __launch_bounds__(128) attention_kernel(const AttnArgs a) {
   grid_dep_launch();
   grid_dep_wait();
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int q0 = blockIdx.x * BM, h = blockIdx.y, bi = blockIdx.z;
+  const int S = SPLIT ? a.kv_splits : 1;
+  const int split = S > 1 ? static_cast<int>(blockIdx.x % S) : 0;
+  const int q0 = (S > 1 ? blockIdx.x / S : blockIdx.x) * BM, h = blockIdx.y, bi = blockIdx.z;
   const int kvh = h / (a.nq / a.nkv);
   const __nv_bfloat16* Q = a.q + bi * a.bq + static_cast<long long>(h) * HD;
   const __nv_bfloat16* K = a.k + bi * a.bk + static_cast<long long>(kvh) * HD;
@@ -85,7 +88,11 @@ __global__ void __launch_bounds__(128) attention_kernel(const AttnArgs a) {
   const long long diag = static_cast<long long>(q0 + BM - 1) + a.q_offset;
   if (diag > last) last = diag;
   if (last > a.Lk - 1) last = a.Lk - 1;
-  const int n_tiles = static_cast<int>((last + BN) / BN);
+  const int all_tiles = static_cast<int>((last + BN) / BN);
+  const int per_split = (all_tiles + S - 1) / S;
+  const int t_begin = split * per_split;
+  const int t_end = min(all_tiles, t_begin + per_split);
+  const int n_tiles = t_end > t_begin ? t_end - t_begin : 0;
 
   auto load_kv = [&](int tile, int buf) {
     const int j0 = tile * BN;
@@ -100,7 +107,7 @@ __global__ void __launch_bounds__(128) attention_kernel(const AttnArgs a) {
     cp_async_commit();
   };
 
-  load_kv(0, 0);
+  if (n_tiles > 0) load_kv(t_begin, 0);
 
   // stage Q (rotated) into shared memory: 8 dims of each rotary half per step, 16-byte loads
   constexpr int VH = HALF / 8;
@@ -159,7 +166,7 @@ __global__ void __launch_bounds__(128) attention_kernel(const AttnArgs a) {
   for (int tile = 0; tile < n_tiles; ++tile) {
     const int buf = tile & 1;
     if (tile + 1 < n_tiles) {
-      load_kv(tile + 1, buf ^ 1);
+      load_kv(t_begin + tile + 1, buf ^ 1);
       cp_async_wait<1>();
     } else {
       cp_async_wait<0>();
@@ -184,7 +191,7 @@ __global__ void __launch_bounds__(128) attention_kernel(const AttnArgs a) {
       }
     }
     // scale, mask, row max
-    const int j0 = tile * BN;
+    const int j0 = (t_begin + tile) * BN;
     float mx0 = -INFINITY, mx1 = -INFINITY;
 #pragma unroll
     for (int t = 0; t < BN / 8; ++t) {
@@ -251,8 +258,92 @@ __global__ void __launch_bounds__(128) attention_kernel(const AttnArgs a) {
   l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
   l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
   l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
-  const float inv0 = 1.f / l0, inv1 = 1.f / l1;
   const long long obase = bi * a.bo + static_cast<long long>(h) * HD;
+  if constexpr (SPLIT) {
+    // this split's unnormalised rows: O in the (now idle) K/V ring, (m, l) in the Q area
+    constexpr int LDO = HD + 4;
+    float* sO = reinterpret_cast<float*>(sK);
+    float* sML = reinterpret_cast<float*>(sQ);   // [64][2]: running max, row sum
+    float* sW = sML + 2 * BM;                    // [64][8]: merge weights
+    const int lr0 = warp * 16 + (lane >> 2), lr1 = lr0 + 8;
+    __syncthreads();  // every warp is done with the Q and K/V areas (a split may have had no tile)
+#pragma unroll
+    for (int t = 0; t < HD / 8; ++t) {
+      const int col = t * 8 + (lane & 3) * 2;
+      *reinterpret_cast<float2*>(sO + lr0 * LDO + col) = make_float2(o[t][0], o[t][1]);
+      *reinterpret_cast<float2*>(sO + lr1 * LDO + col) = make_float2(o[t][2], o[t][3]);
+    }
+    if ((lane & 3) == 0) {
+      sML[2 * lr0] = m0;
+      sML[2 * lr0 + 1] = l0;
+      sML[2 * lr1] = m1;
+      sML[2 * lr1 + 1] = l1;
+    }
+    cluster_sync();
+    // CTA `split` merges rows [split*64/S, (split+1)*64/S) over all splits, in split order
+    const int rlo = split * BM / S, rhi = (split + 1) * BM / S, nr = rhi - rlo;
+    const uint32_t o_addr = smem_u32(sO), ml_addr = smem_u32(sML);
+    if (tid < nr) {
+      const int r = rlo + tid;
+      float ms[8], ls[8], mx = -INFINITY;
+#pragma unroll
+      for (int sp = 0; sp < 8; ++sp) {
+        if (sp < S) {
+          const uint32_t pa = mapa_shared(ml_addr, static_cast<uint32_t>(sp)) + static_cast<uint32_t>(8 * r);
+          ms[sp] = ld_cluster_f32(pa);
+          ls[sp] = ld_cluster_f32(pa + 4);
+          mx = fmaxf(mx, ms[sp]);
+        }
+      }
+      if (mx == -INFINITY) mx = 0.f;
+      float l = 0.f;
+#pragma unroll
+      for (int sp = 0; sp < 8; ++sp) {
+        if (sp < S) {
+          ms[sp] = exp2f(ms[sp] - mx);
+          l += ls[sp] * ms[sp];
+        }
+      }
+      const float inv = 1.f / l;
+#pragma unroll
+      for (int sp = 0; sp < 8; ++sp) sW[8 * tid + sp] = sp < S ? ms[sp] * inv : 0.f;
+    }
+    __syncthreads();
+    for (int idx = tid; idx < nr * (HD / 4); idx += 128) {
+      const int rr = idx / (HD / 4), c4 = (idx % (HD / 4)) * 4;
+      const int row = q0 + rlo + rr;
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      float4 part[8];
+#pragma unroll
+      for (int sp = 0; sp < 8; ++sp)
+        if (sp < S)
+          part[sp] = ld_cluster_f32x4(mapa_shared(o_addr, static_cast<uint32_t>(sp)) +
+                                      static_cast<uint32_t>(((rlo + rr) * LDO + c4) * 4));
+#pragma unroll
+      for (int sp = 0; sp < 8; ++sp) {
+        if (sp < S) {
+          const float wgt = sW[8 * rr + sp];
+          acc.x += part[sp].x * wgt, acc.y += part[sp].y * wgt, acc.z += part[sp].z * wgt, acc.w += part[sp].w * wgt;
+        }
+      }
+      if (row < a.Lq) {
+        const long long off = obase + static_cast<long long>(row) * a.ldo + c4;
+        if (a.o_type == SO101_BF16) {
+          __nv_bfloat162 hv[2] = {__floats2bfloat162_rn(acc.x, acc.y), __floats2bfloat162_rn(acc.z, acc.w)};
+          *reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(a.o) + off) = *reinterpret_cast<uint2*>(hv);
+        } else {
+          int8_t* pq = static_cast<int8_t*>(a.o) + off;
+          pq[0] = quant_i8(acc.x, a.o_qscale);
+          pq[1] = quant_i8(acc.y, a.o_qscale);
+          pq[2] = quant_i8(acc.z, a.o_qscale);
+          pq[3] = quant_i8(acc.w, a.o_qscale);
+        }
+      }
+    }
+    cluster_sync();  // peers keep their shared memory until every merge has read it
+    return;
+  }
+  const float inv0 = 1.f / l0, inv1 = 1.f / l1;
 #pragma unroll
   for (int t = 0; t < HD / 8; ++t) {
     const int col = t * 8 + (lane & 3) * 2;
@@ -279,12 +370,31 @@ int launch_attention(const AttnArgs& a, int batch, cudaStream_t stream) {
   constexpr int smem = (64 * (HD + 8) + 4 * 64 * (HD + 8)) * 2;
   static bool configured = false;
   if (!configured) {
-    if (cudaFuncSetAttribute(attention_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+    if (cudaFuncSetAttribute(attention_kernel<HD, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
+            cudaSuccess ||
+        cudaFuncSetAttribute(attention_kernel<HD, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
+            cudaSuccess)
       return SO101_ERR_LAUNCH;
     configured = true;
   }
-  dim3 grid((a.Lq + 63) / 64, a.nq, batch);
-  return launch_kernel(attention_kernel<HD>, dim3(grid), dim3(128), smem, stream, a);
+  const int q_tiles = (a.Lq + 63) / 64;
+  dim3 grid(q_tiles * a.kv_splits, a.nq, batch);
+  if (a.kv_splits == 1) return launch_kernel(attention_kernel<HD, false>, dim3(grid), dim3(128), smem, stream, a);
+  cudaLaunchConfig_t lc = {};
+  lc.gridDim = grid;
+  lc.blockDim = dim3(128);
+  lc.dynamicSmemBytes = smem;
+  lc.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = a.kv_splits;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  lc.attrs = attr;
+  lc.numAttrs = pdl_enabled() ? 2 : 1;
+  return cudaLaunchKernelEx(&lc, attention_kernel<HD, true>, a) == cudaSuccess ? SO101_OK : SO101_ERR_LAUNCH;
 }
 
 }  // namespace so101
@@ -334,6 +444,23 @@ extern "C" int so101_attention(const void* q, int64_t ldq, const void* k, int64_
   a.cos = cos;
   a.sin = sin;
   a.scale_log2 = static_cast<float>(1.4426950408889634 / sqrt(static_cast<double>(hd)));
+  // few CTAs (the expert's 50 queries, the 241-row prefix): split the key tiles over a cluster
+  {
+    long long last = causal_from - 1;
+    if (Lq - 1 + q_offset > last) last = Lq - 1 + q_offset;
+    if (last > Lk - 1) last = Lk - 1;
+    const long long tiles = (last + 64) / 64;
+    const long long ctas = ((Lq + 63) / 64) * static_cast<long long>(nq) * batch;
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    long long sp = ctas >= sms ? 1 : (sms + ctas - 1) / ctas;
+    if (sp > tiles) sp = tiles;
+    if (sp > 8) sp = 8;
+    if (sp < 1) sp = 1;
+    const long long per = (tiles + sp - 1) / sp;
+    a.kv_splits = static_cast<int>((tiles + per - 1) / per);  // no split without key tiles
+  }
   switch (hd) {
     case 32: return launch_attention<32>(a, batch, stream);
     case 64: return launch_attention<64>(a, batch, stream);

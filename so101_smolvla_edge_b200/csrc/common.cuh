@@ -276,6 +276,23 @@ __device__ __forceinline__ float gelu_tanh(float x) {
   return 0.5f * x * (1.0f + tanh_fast(k0 * fmaf(0.044715f * x, x * x, x)));
 }
 
+// The same GELU in five FMA-pipe operations around the tanh: x * (k0 + k0 * 0.044715 * x^2).
+__device__ __forceinline__ float gelu_tanh_fast(float x) {
+  const float t = tanh_fast(x * fmaf(x * x, 0.7978845608028654f * 0.044715f, 0.7978845608028654f));
+  const float h = 0.5f * x;
+  return fmaf(h, t, h);
+}
+
+// Four values to packed int8 (clamp(round_half_even(v * inv), -128, 127)): the clamped product
+// plus 1.5 * 2^23 holds the rounded integer in the low byte of its bit pattern.
+__device__ __forceinline__ uint32_t pack4_i8(float a, float b, float c, float d, float inv) {
+  const uint32_t qa = __float_as_uint(fminf(fmaxf(a * inv, -128.f), 127.f) + 12582912.0f);
+  const uint32_t qb = __float_as_uint(fminf(fmaxf(b * inv, -128.f), 127.f) + 12582912.0f);
+  const uint32_t qc = __float_as_uint(fminf(fmaxf(c * inv, -128.f), 127.f) + 12582912.0f);
+  const uint32_t qd = __float_as_uint(fminf(fmaxf(d * inv, -128.f), 127.f) + 12582912.0f);
+  return __byte_perm(__byte_perm(qa, qb, 0x0040), __byte_perm(qc, qd, 0x0040), 0x5410);
+}
+
 // SiLU through sigmoid(x) = (1 + tanh(x / 2)) / 2.
 __device__ __forceinline__ float silu(float x) { return 0.5f * x * (1.0f + tanh_fast(0.5f * x)); }
 

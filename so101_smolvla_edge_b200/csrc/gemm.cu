@@ -182,6 +182,96 @@ __device__ __forceinline__ void epilogue16(const GemmArgs& a, int p, int qb, flo
   }
 }
 
+// Lean epilogue of 16 consecutive output columns of row m (tokens on the MMA M side), for chunks
+// fully inside N with vector-aligned rows. kc / kb / ku hold this chunk's per-column constants in
+// shared memory: the dequantization scale (x_scale * w_scale[n], int8 only), the bias, and the
+// up-projection scale (int8 SiLU gate).
+template <bool DUAL, bool I8>
+__device__ __forceinline__ void epilogue_row16_fast(const GemmArgs& a, int m, int qb, const uint32_t (&r0)[16],
+                                                    const uint32_t (&r1)[16], const float* kc, const float* kb,
+                                                    const float* ku) {
+  float v[16];
+#pragma unroll
+  for (int j4 = 0; j4 < 4; ++j4) {
+    const float4 bi = *reinterpret_cast<const float4*>(kb + 4 * j4);
+    const float bb[4] = {bi.x, bi.y, bi.z, bi.w};
+    if constexpr (I8) {
+      const float4 sc = *reinterpret_cast<const float4*>(kc + 4 * j4);
+      const float ss[4] = {sc.x, sc.y, sc.z, sc.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        v[4 * j4 + e] = fmaf(static_cast<float>(static_cast<int>(r0[4 * j4 + e])), ss[e], bb[e]);
+    } else {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) v[4 * j4 + e] = __uint_as_float(r0[4 * j4 + e]) + bb[e];
+    }
+  }
+  if constexpr (DUAL) {
+#pragma unroll
+    for (int j4 = 0; j4 < 4; ++j4) {
+      float su[4] = {1.f, 1.f, 1.f, 1.f};
+      if constexpr (I8) {
+        const float4 sc = *reinterpret_cast<const float4*>(ku + 4 * j4);
+        su[0] = sc.x, su[1] = sc.y, su[2] = sc.z, su[3] = sc.w;
+      }
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float up = I8 ? static_cast<float>(static_cast<int>(r1[4 * j4 + e])) * su[e] : __uint_as_float(r1[4 * j4 + e]);
+        v[4 * j4 + e] = silu(v[4 * j4 + e]) * up;
+      }
+    }
+  } else if (a.epilogue == SO101_EPI_GELU) {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) v[j] = gelu_tanh_fast(v[j]);
+  }
+  if (a.out_scale != 1.f) {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) v[j] *= a.out_scale;
+  }
+  const long long row = out_row(a, m);
+  if (a.res) {
+    const long long rrow = a.r_period > 0 ? m % a.r_period : row;
+    if (a.r_type == SO101_F32) {
+      const float4* r4 = reinterpret_cast<const float4*>(static_cast<const float*>(a.res) + rrow * a.ldr + qb);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float4 r = r4[j];
+        v[4 * j] += r.x, v[4 * j + 1] += r.y, v[4 * j + 2] += r.z, v[4 * j + 3] += r.w;
+      }
+    } else {
+      const uint4* r4 = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(a.res) + rrow * a.ldr + qb);
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        uint4 r = r4[j];
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&r);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = __bfloat1622float2(h[e]);
+          v[8 * j + 2 * e] += f.x, v[8 * j + 2 * e + 1] += f.y;
+        }
+      }
+    }
+  }
+  if (a.y_type == SO101_F32) {
+    float4* y4 = reinterpret_cast<float4*>(static_cast<float*>(a.y) + row * a.ldy + qb);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) y4[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+  } else if (a.y_type == SO101_BF16) {
+    uint4 o[2];
+    __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(o);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) h[e] = __floats2bfloat162_rn(v[2 * e], v[2 * e + 1]);
+    uint4* y4 = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.y) + row * a.ldy + qb);
+    y4[0] = o[0];
+    y4[1] = o[1];
+  } else {
+    const float inv = a.y_qinv;
+    *reinterpret_cast<uint4*>(static_cast<int8_t*>(a.y) + row * a.ldy + qb) =
+        make_uint4(pack4_i8(v[0], v[1], v[2], v[3], inv), pack4_i8(v[4], v[5], v[6], v[7], inv),
+                   pack4_i8(v[8], v[9], v[10], v[11], inv), pack4_i8(v[12], v[13], v[14], v[15], inv));
+  }
+}
+
 template <bool I8>
 __device__ __forceinline__ float acc_value(uint32_t r) {
   return I8 ? i32_to_f32(static_cast<int>(r)) : __uint_as_float(r);
@@ -343,12 +433,12 @@ __global__ void __launch_bounds__(128, 1)
     uint32_t peer[kMaxSplitCluster];
 #pragma unroll
     for (int s = 0; s < kMaxSplitCluster; ++s) peer[s] = mapa_shared(part_addr, static_cast<uint32_t>(s < S ? s : 0));
-    if (SWAP && !DUAL && !I8 && a.vec_ok) {
+    if (SWAP && !I8 && a.vec_ok) {
       // two items per pass, every load (partials, bias, residual) issued before any store: the
       // output may alias the residual, so the compiler could not reorder them itself
       const int total = nq * BN;
       for (int base = 0; base < total; base += 2 * 128) {
-        float4 pv[2][kMaxSplitCluster], bia[2], res[2];
+        float4 pv[2][kMaxSplitCluster], pu[2][DUAL ? kMaxSplitCluster : 1], bia[2], res[2];
         int ok[2], col[2], quad[2];
 #pragma unroll
         for (int it = 0; it < 2; ++it) {
@@ -359,9 +449,14 @@ __global__ void __launch_bounds__(128, 1)
           const int m = q0 + col[it], n = p0 + quad[it] * 4;
           ok[it] = ok[it] && m < a.M && n < a.N;
           const uint32_t off = static_cast<uint32_t>((col[it] * 128 + quad[it] * 4) * 4);
+          const uint32_t off_u = static_cast<uint32_t>(((BN + col[it]) * 128 + quad[it] * 4) * 4);
 #pragma unroll
-          for (int sp = 0; sp < kMaxSplitCluster; ++sp)
-            if (sp < S) pv[it][sp] = ld_cluster_f32x4(peer[sp] + off);
+          for (int sp = 0; sp < kMaxSplitCluster; ++sp) {
+            if (sp < S) {
+              pv[it][sp] = ld_cluster_f32x4(peer[sp] + off);
+              if constexpr (DUAL) pu[it][sp] = ld_cluster_f32x4(peer[sp] + off_u);
+            }
+          }
           bia[it] = make_float4(0.f, 0.f, 0.f, 0.f);
           res[it] = bia[it];
           if (ok[it] && n + 4 <= a.N) {
@@ -374,19 +469,29 @@ __global__ void __launch_bounds__(128, 1)
 #pragma unroll
         for (int it = 0; it < 2; ++it) {
           if (!ok[it]) continue;
-          float4 sv = make_float4(0.f, 0.f, 0.f, 0.f);
+          float4 sv = make_float4(0.f, 0.f, 0.f, 0.f), su = sv;
 #pragma unroll
-          for (int sp = 0; sp < kMaxSplitCluster; ++sp)
-            if (sp < S) sv.x += pv[it][sp].x, sv.y += pv[it][sp].y, sv.z += pv[it][sp].z, sv.w += pv[it][sp].w;
+          for (int sp = 0; sp < kMaxSplitCluster; ++sp) {
+            if (sp < S) {
+              sv.x += pv[it][sp].x, sv.y += pv[it][sp].y, sv.z += pv[it][sp].z, sv.w += pv[it][sp].w;
+              if constexpr (DUAL) su.x += pu[it][sp].x, su.y += pu[it][sp].y, su.z += pu[it][sp].z, su.w += pu[it][sp].w;
+            }
+          }
           const int m = q0 + col[it], n = p0 + quad[it] * 4;
-          if (n + 4 > a.N || (a.res && a.r_type != SO101_F32) || a.epilogue != SO101_EPI_NONE) {
-            const float vv[4] = {sv.x, sv.y, sv.z, sv.w};
+          if (n + 4 > a.N || (a.res && a.r_type != SO101_F32) || a.epilogue == SO101_EPI_GELU) {
+            const float vv[4] = {sv.x, sv.y, sv.z, sv.w}, uu[4] = {su.x, su.y, su.z, su.w};
 #pragma unroll
-            for (int e = 0; e < 4; ++e) epilogue1<DUAL, I8>(a, m, n + e, vv[e], 0.f);
+            for (int e = 0; e < 4; ++e) epilogue1<DUAL, I8>(a, m, n + e, vv[e], uu[e]);
             continue;
           }
-          float4 x = make_float4((sv.x + bia[it].x) * a.out_scale + res[it].x, (sv.y + bia[it].y) * a.out_scale + res[it].y,
-                                 (sv.z + bia[it].z) * a.out_scale + res[it].z, (sv.w + bia[it].w) * a.out_scale + res[it].w);
+          float4 x;
+          if constexpr (DUAL) {
+            x = make_float4(silu(sv.x) * su.x * a.out_scale, silu(sv.y) * su.y * a.out_scale,
+                            silu(sv.z) * su.z * a.out_scale, silu(sv.w) * su.w * a.out_scale);
+          } else {
+            x = make_float4((sv.x + bia[it].x) * a.out_scale + res[it].x, (sv.y + bia[it].y) * a.out_scale + res[it].y,
+                            (sv.z + bia[it].z) * a.out_scale + res[it].z, (sv.w + bia[it].w) * a.out_scale + res[it].w);
+          }
           const long long yi = out_row(a, m) * a.ldy + n;
           if (a.y_type == SO101_F32) {
             *reinterpret_cast<float4*>(static_cast<float*>(a.y) + yi) = x;
@@ -505,6 +610,8 @@ __global__ void __launch_bounds__(128, 1)
 
 // ================================================================ persistent, warp-specialized
 constexpr int kEpiWarps = 8;
+constexpr int kBarrierBytes = 256;                    // ring barriers, accumulator barriers, TMEM slot
+constexpr int kConstBytes = kEpiWarps * 3 * 128 * 4;  // column constants, BN <= 256
 
 template <int BN, bool DUAL, bool I8>
 __global__ void __launch_bounds__(32 * (2 + kEpiWarps), 1)
@@ -527,6 +634,8 @@ __global__ void __launch_bounds__(32 * (2 + kEpiWarps), 1)
   uint64_t* acc_full = empty + stages;  // [2]
   uint64_t* acc_empty = acc_full + 2;   // [2]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  // per epilogue warp: this tile's column constants (scale, bias, up scale) for its column half
+  float* consts = reinterpret_cast<float*>(smem + stages * STAGE_BYTES + kBarrierBytes);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
@@ -639,6 +748,18 @@ __global__ void __launch_bounds__(32 * (2 + kEpiWarps), 1)
       const int p0 = (tile / a.tiles_q) * 128, q0 = (tile % a.tiles_q) * BN;
       const int p = p0 + quad * 32 + lane;
       const uint32_t taddr = tmem + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(buf * NACC);
+      float* kc = consts + e * 3 * HALF;
+      float* kb = kc + HALF;
+      float* ku = kb + HALF;
+      __syncwarp();
+      for (int j = lane; j < HALF; j += 32) {
+        const int n = q0 + c_lo + j;
+        const bool in = n < a.N;
+        kc[j] = I8 ? (in ? a.x_scale * __ldg(a.w_scale + n) : 0.f) : 1.f;
+        kb[j] = (a.bias && in) ? __ldg(a.bias + n) : 0.f;
+        ku[j] = (I8 && DUAL && in) ? a.x_scale * __ldg(a.w_scale + a.N + n) : 1.f;
+      }
+      __syncwarp();
       float v[16], u[16];
 #pragma unroll 1
       for (int c = c_lo; c < c_lo + HALF; c += 16) {
@@ -646,12 +767,16 @@ __global__ void __launch_bounds__(32 * (2 + kEpiWarps), 1)
         tmem_ld16(taddr + c, r0);
         if (DUAL) tmem_ld16(taddr + BN + c, r1);
         tmem_ld_wait();
+        if (a.vec_ok && p < a.M && q0 + c + 16 <= a.N) {
+          epilogue_row16_fast<DUAL, I8>(a, p, q0 + c, r0, r1, kc + (c - c_lo), kb + (c - c_lo), ku + (c - c_lo));
+        } else {
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          v[j] = acc_value<I8>(r0[j]);
-          u[j] = DUAL ? acc_value<I8>(r1[j]) : 0.f;
+          for (int j = 0; j < 16; ++j) {
+            v[j] = acc_value<I8>(r0[j]);
+            u[j] = DUAL ? acc_value<I8>(r1[j]) : 0.f;
+          }
+          epilogue16<false, DUAL, I8>(a, p, q0 + c, v, u);
         }
-        epilogue16<false, DUAL, I8>(a, p, q0 + c, v, u);
       }
       tc_fence_before();
       __syncwarp();
@@ -761,7 +886,7 @@ int plan_gemm(int a_type, long long M, long long N, long long K, int epi, const 
   if (pl->kind == kTile && pl->splits > 1 && pl->splits <= kMaxCluster && !(c.flags & SO101_GEMM_GLOBAL_SPLITK))
     pl->cluster = pl->splits;
   const int sb = stage_bytes(c.bn, c.swap, dual);
-  const int max_st = (kSmemBudget - 1024 - 256) / sb;
+  const int max_st = (kSmemBudget - 1024 - 256 - (pl->kind == kPersistent ? kConstBytes : 0)) / sb;
   if (c.stages <= 0) {
     int want = pl->kind == kPersistent ? 8 : pl->kb_per_split;
     if (want < 2) want = 2;
@@ -825,7 +950,7 @@ template <int BN, bool DUAL, bool I8>
 int launch_persistent(const CUtensorMap& tx, const CUtensorMap& tw, const GemmArgs& a, const Plan& pl,
                       cudaStream_t stream, bool pdl) {
   static int configured = 0;
-  const int smem = pl.cfg.stages * stage_bytes(BN, false, DUAL) + 1024 + 256;
+  const int smem = pl.cfg.stages * stage_bytes(BN, false, DUAL) + 1024 + kBarrierBytes + kConstBytes;
   const long long tiles = static_cast<long long>(pl.tiles_p) * pl.tiles_q;
   const int sms = sm_count();
   const int grid = static_cast<int>(tiles < sms ? tiles : sms);

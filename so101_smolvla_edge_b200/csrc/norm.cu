@@ -102,6 +102,96 @@ __global__ void layer_norm_kernel(const float* __restrict__ x, long long ldx, co
   }
 }
 
+// ------------------------------------------------------------------ vectorized row kernels
+// One warp per row, lane l holding float4 groups l, l + 32, ... (G groups, n <= 128 G, n % 4 == 0,
+// 16-byte aligned rows): the row is read once with 16-byte loads and written with packed stores.
+__device__ __forceinline__ void store4(void* y, long long i, int type, float a, float b, float c, float d, float inv) {
+  if (type == SO101_F32) {
+    *reinterpret_cast<float4*>(static_cast<float*>(y) + i) = make_float4(a, b, c, d);
+  } else if (type == SO101_BF16) {
+    __nv_bfloat162 h[2] = {__floats2bfloat162_rn(a, b), __floats2bfloat162_rn(c, d)};
+    *reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(y) + i) = *reinterpret_cast<uint2*>(h);
+  } else {
+    *reinterpret_cast<uint32_t*>(static_cast<int8_t*>(y) + i) = pack4_i8(a, b, c, d, inv);
+  }
+}
+
+template <int G>
+__global__ void layer_norm_vec_kernel(const float* __restrict__ x, long long ldx, const float* __restrict__ w,
+                                      const float* __restrict__ b, void* __restrict__ y, long long ldy, int y_type,
+                                      float inv_qs, long long rows, int n, float eps, int s, long long T) {
+  grid_dep_launch();
+  grid_dep_wait();
+  const long long row = static_cast<long long>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const float4* xr = reinterpret_cast<const float4*>(x + row * ldx);
+  float4 v[G];
+  float sum = 0.f;
+#pragma unroll
+  for (int i = 0; i < G; ++i) {
+    const int g = lane + 32 * i;
+    v[i] = 4 * g < n ? xr[g] : make_float4(0.f, 0.f, 0.f, 0.f);
+    sum += (v[i].x + v[i].y) + (v[i].z + v[i].w);
+  }
+  const float inv_n = 1.0f / static_cast<float>(n);
+  const float mu = warp_sum(sum) * inv_n;
+  float var = 0.f;
+#pragma unroll
+  for (int i = 0; i < G; ++i) {
+    if (4 * (lane + 32 * i) < n) {
+      const float a0 = v[i].x - mu, a1 = v[i].y - mu, a2 = v[i].z - mu, a3 = v[i].w - mu;
+      var += (a0 * a0 + a1 * a1) + (a2 * a2 + a3 * a3);
+    }
+  }
+  const float rstd = rsqrtf(warp_sum(var) * inv_n + eps);
+  long long orow = row, col0 = 0;
+  if (s > 1) {
+    const long long img = row / T, tok = row % T;
+    const int side = static_cast<int>(sqrtf(static_cast<float>(T)) + 0.5f);
+    const int hi = static_cast<int>(tok / side), wi = static_cast<int>(tok % side);
+    orow = img * (T / (s * s)) + (hi / s) * (side / s) + wi / s;
+    col0 = static_cast<long long>((hi % s) * s + wi % s) * n;
+  }
+#pragma unroll
+  for (int i = 0; i < G; ++i) {
+    const int c = 4 * (lane + 32 * i);
+    if (c >= n) continue;
+    const float4 ww = __ldg(reinterpret_cast<const float4*>(w + c));
+    const float4 bb = __ldg(reinterpret_cast<const float4*>(b + c));
+    store4(y, orow * ldy + col0 + c, y_type, (v[i].x - mu) * rstd * ww.x + bb.x, (v[i].y - mu) * rstd * ww.y + bb.y,
+           (v[i].z - mu) * rstd * ww.z + bb.z, (v[i].w - mu) * rstd * ww.w + bb.w, inv_qs);
+  }
+}
+
+template <int G>
+__global__ void rms_norm_vec_kernel(const float* __restrict__ x, long long ldx, const float* __restrict__ w,
+                                    void* __restrict__ y, long long ldy, int y_type, long long rows, int n, float eps) {
+  grid_dep_launch();
+  grid_dep_wait();
+  const long long row = static_cast<long long>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const float4* xr = reinterpret_cast<const float4*>(x + row * ldx);
+  float4 v[G];
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < G; ++i) {
+    const int g = lane + 32 * i;
+    v[i] = 4 * g < n ? xr[g] : make_float4(0.f, 0.f, 0.f, 0.f);
+    ss += (v[i].x * v[i].x + v[i].y * v[i].y) + (v[i].z * v[i].z + v[i].w * v[i].w);
+  }
+  const float rstd = rsqrtf(warp_sum(ss) / static_cast<float>(n) + eps);
+#pragma unroll
+  for (int i = 0; i < G; ++i) {
+    const int c = 4 * (lane + 32 * i);
+    if (c >= n) continue;
+    const float4 ww = __ldg(reinterpret_cast<const float4*>(w + c));
+    store4(y, row * ldy + c, y_type, (v[i].x * rstd) * ww.x, (v[i].y * rstd) * ww.y, (v[i].z * rstd) * ww.z,
+           (v[i].w * rstd) * ww.w, 1.f);
+  }
+}
+
 // ------------------------------------------------------------------ RoPE + K/V cache write
 // grid (rows, batch); thread j < nkv * hd/2 rotates pair (d, d + hd/2) of kv head j / (hd/2) and
 // copies the two value columns at the same positions. The rotation is rounded per operation
@@ -188,6 +278,13 @@ __global__ void quantize_weight_kernel(const void* __restrict__ w, int w_type, l
 using namespace so101;
 
 
+namespace {
+bool vec_ok(const void* x, long long ldx, int esz, const void* y, long long ldy, int ysz, const float* w, long long n) {
+  return n % 4 == 0 && reinterpret_cast<uintptr_t>(x) % 16 == 0 && (ldx * esz) % 16 == 0 &&
+         reinterpret_cast<uintptr_t>(y) % 16 == 0 && (ldy * ysz) % 16 == 0 && reinterpret_cast<uintptr_t>(w) % 16 == 0;
+}
+}  // namespace
+
 extern "C" int so101_rms_norm(const void* x, int64_t ldx, int x_type, const float* w, void* y, int64_t ldy,
                               int y_type, int64_t rows, int64_t n, float eps, cudaStream_t stream) {
   if (!x || !w || !y || rows <= 0 || n <= 0 || n > 32 * kMaxRowPerLane) return SO101_ERR_ARG;
@@ -196,6 +293,22 @@ extern "C" int so101_rms_norm(const void* x, int64_t ldx, int x_type, const floa
   const int rows_per_block = 4;
   const long long blocks = (rows + rows_per_block - 1) / rows_per_block;
   if (blocks > 0x7fffffffLL) return SO101_ERR_ARG;
+  const int ysz = y_type == SO101_F32 ? 4 : 2;
+  if (x_type == SO101_F32 && vec_ok(x, ldx, 4, y, ldy, ysz, w, n) && (ldy * ysz) % 16 == 0) {
+    const dim3 g(static_cast<unsigned>(blocks)), bl(32 * rows_per_block);
+    const float* xf = static_cast<const float*>(x);
+    const int ni = static_cast<int>(n);
+    switch ((n + 127) / 128) {
+      case 1: return launch_kernel(rms_norm_vec_kernel<1>, g, bl, 0, stream, xf, ldx, w, y, ldy, y_type, rows, ni, eps);
+      case 2: return launch_kernel(rms_norm_vec_kernel<2>, g, bl, 0, stream, xf, ldx, w, y, ldy, y_type, rows, ni, eps);
+      case 3: return launch_kernel(rms_norm_vec_kernel<3>, g, bl, 0, stream, xf, ldx, w, y, ldy, y_type, rows, ni, eps);
+      case 4: return launch_kernel(rms_norm_vec_kernel<4>, g, bl, 0, stream, xf, ldx, w, y, ldy, y_type, rows, ni, eps);
+      case 5: return launch_kernel(rms_norm_vec_kernel<5>, g, bl, 0, stream, xf, ldx, w, y, ldy, y_type, rows, ni, eps);
+      case 6: return launch_kernel(rms_norm_vec_kernel<6>, g, bl, 0, stream, xf, ldx, w, y, ldy, y_type, rows, ni, eps);
+      case 7: return launch_kernel(rms_norm_vec_kernel<7>, g, bl, 0, stream, xf, ldx, w, y, ldy, y_type, rows, ni, eps);
+      case 8: return launch_kernel(rms_norm_vec_kernel<8>, g, bl, 0, stream, xf, ldx, w, y, ldy, y_type, rows, ni, eps);
+    }
+  }
   return launch_kernel(rms_norm_kernel, dim3(static_cast<unsigned>(blocks)), dim3(32 * rows_per_block), 0, stream,
                        x, ldx, x_type, w, y, ldy, y_type, rows, static_cast<int>(n), eps);
 }
@@ -214,6 +327,23 @@ extern "C" int so101_layer_norm(const float* x, int64_t ldx, const float* w, con
   }
   const int rows_per_block = 4;
   const long long blocks = (rows + rows_per_block - 1) / rows_per_block;
+  const int ysz = y_type == SO101_F32 ? 4 : y_type == SO101_BF16 ? 2 : 1;
+  if (vec_ok(x, ldx, 4, y, ldy, ysz, w, n) && reinterpret_cast<uintptr_t>(b) % 16 == 0) {
+    const dim3 g(static_cast<unsigned>(blocks)), bl(32 * rows_per_block);
+    const float inv = y_type == SO101_I8 ? static_cast<float>(1.0 / static_cast<double>(y_qscale)) : 1.f;
+    const int ni = static_cast<int>(n), sh = shuffle > 1 ? shuffle : 1;
+    const long long T = shuffle > 1 ? tokens_per_image : 1;
+    switch ((n + 127) / 128) {
+      case 1: return launch_kernel(layer_norm_vec_kernel<1>, g, bl, 0, stream, x, ldx, w, b, y, ldy, y_type, inv, rows, ni, eps, sh, T);
+      case 2: return launch_kernel(layer_norm_vec_kernel<2>, g, bl, 0, stream, x, ldx, w, b, y, ldy, y_type, inv, rows, ni, eps, sh, T);
+      case 3: return launch_kernel(layer_norm_vec_kernel<3>, g, bl, 0, stream, x, ldx, w, b, y, ldy, y_type, inv, rows, ni, eps, sh, T);
+      case 4: return launch_kernel(layer_norm_vec_kernel<4>, g, bl, 0, stream, x, ldx, w, b, y, ldy, y_type, inv, rows, ni, eps, sh, T);
+      case 5: return launch_kernel(layer_norm_vec_kernel<5>, g, bl, 0, stream, x, ldx, w, b, y, ldy, y_type, inv, rows, ni, eps, sh, T);
+      case 6: return launch_kernel(layer_norm_vec_kernel<6>, g, bl, 0, stream, x, ldx, w, b, y, ldy, y_type, inv, rows, ni, eps, sh, T);
+      case 7: return launch_kernel(layer_norm_vec_kernel<7>, g, bl, 0, stream, x, ldx, w, b, y, ldy, y_type, inv, rows, ni, eps, sh, T);
+      case 8: return launch_kernel(layer_norm_vec_kernel<8>, g, bl, 0, stream, x, ldx, w, b, y, ldy, y_type, inv, rows, ni, eps, sh, T);
+    }
+  }
   return launch_kernel(layer_norm_kernel, dim3(static_cast<unsigned>(blocks)), dim3(32 * rows_per_block), 0, stream,
                        x, ldx, w, b, y, ldy, y_type, y_qscale, rows, static_cast<int>(n), eps, shuffle > 1 ? shuffle : 1,
       shuffle > 1 ? tokens_per_image : 1);

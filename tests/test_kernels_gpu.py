@@ -232,7 +232,7 @@ def visibility(lq, lk, causal_from, q_offset):
     return (j < causal_from) | (j <= i + q_offset)
 
 
-@pytest.mark.parametrize("case", ["prefix", "expert_self", "expert_cross", "small", "siglip"])
+@pytest.mark.parametrize("case", ["prefix", "expert_self", "expert_cross", "small", "siglip", "odd"])
 def test_attention(case):
     """the prefix-LM mask over 241 tokens (192 image + 48 text bidirectional, the
     state token last), expert self attention (50 queries over 241 prefix + 50 causal keys),
@@ -251,6 +251,9 @@ def test_attention(case):
     elif case == "small":
         nq, nk, hd = 4, 2, 32
         lq, lk, pos, cf, qo = 13, 13, torch.arange(13), 12, 0
+    elif case == "odd":  # key tiles that do not divide evenly over the split cluster, head_dim 128
+        nq, nk, hd = 4, 1, 128
+        lq, lk, pos, cf, qo = 37, 450, torch.arange(413, 450), 413, 413
     else:
         nq, nk, hd, rope = 12, 12, 64, False
         lq, lk, pos, cf, qo = 1024, 1024, torch.arange(1024), 1024, 0
