@@ -165,6 +165,38 @@ def run_reference(args) -> None:
     }), flush=True)  # fmt: skip
 
 
+# ------------------------------------------------------------------------------ ranks
+class Ranks:
+    """The bench's only cross-rank traffic: a barrier and a max around the timed region.
+
+    `device` is where the reduction tensor lives (a CUDA device for NCCL, the CPU for gloo)."""
+
+    def __init__(self, world: int, device=None):
+        self.world = world
+        self.device = device
+
+    def barrier(self) -> None:
+        if self.world > 1:
+            import torch.distributed as dist
+
+            dist.barrier()
+
+    def max(self, x: float) -> float:
+        if self.world == 1:
+            return float(x)
+        import torch
+        import torch.distributed as dist
+
+        t = torch.tensor([float(x)], dtype=torch.float64, device=self.device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+
+def throughput(world: int, per_rank: int, ms_max: float) -> float:
+    """Whole-job chunks/s: every rank's chunks over the slowest rank's time."""
+    return world * per_rank / (ms_max / 1e3)
+
+
 # ------------------------------------------------------------------------------ ours
 def observations(b, seeds):
     from so101_smolvla_edge_b200.bundle import observation
@@ -249,17 +281,13 @@ def run_ours(args) -> None:
     eng._stage(imgs, states, noises)  # inputs resident in HBM for the device-timed loop
     stream = torch.cuda.current_stream(dev)
 
+    ranks = Ranks(world, dev)
+
     def barrier():
         torch.cuda.synchronize(dev)
-        if world > 1:
-            dist.barrier()
+        ranks.barrier()
 
-    def max_over_ranks(x: float) -> float:
-        if world == 1:
-            return x
-        t = torch.tensor([x], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+    max_over_ranks = ranks.max
 
     # ---- device-timed: one graph replay = 64 chunks per GPU, inputs resident
     for _ in range(args.warmup):
@@ -274,7 +302,7 @@ def run_ours(args) -> None:
         e1.synchronize()
     barrier()
     ms = max_over_ranks(e0.elapsed_time(e1)) / args.steps
-    value = world * BATCH / (ms / 1e3)
+    value = throughput(world, BATCH, ms)
     clk = clocks.summary()
 
     # ---- end to end through the public API (host numpy in, actions out)
@@ -359,7 +387,7 @@ def run_ours(args) -> None:
                        "parallelism": f"replicas x{world} (no collective)",
                        "l2": "inputs larger than L2 (0.7 GB weights, >4 GB activations per replay)",
                        "weights": "seeded configs[0] stand-in"},
-            "e2e": {"value": world * BATCH / (e2e_ms / 1e3), "unit": UNIT,
+            "e2e": {"value": throughput(world, BATCH, e2e_ms), "unit": UNIT,
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
             "gpu_launches": launches * args.steps,
             "pdl": bool(args.pdl),

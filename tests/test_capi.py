@@ -1,0 +1,99 @@
+"""The C ABI library without a GPU: it loads, exports every entry point the header declares, and
+rejects bad arguments on the host before touching the device (no compute call is made here)."""
+
+from __future__ import annotations
+
+import ctypes as C
+
+import pytest
+
+from so101_smolvla_edge_b200 import _lib as L
+
+
+@pytest.fixture(scope="module")
+def lib():
+    return L.lib()
+
+
+def test_library_loads_and_exports_every_header_symbol(lib):
+    names = L.header_symbols()
+    assert len(names) == 19
+    missing = [n for n in names if not hasattr(lib, n)]
+    assert not missing, missing
+    assert lib.so101_version().decode().endswith("sm_100a")
+
+
+def test_bindings_cover_the_header():
+    """Every declared entry point has a ctypes signature (or is bound where it is used)."""
+    bound = set(L.SIGNATURES) | {"so101_version", "so101_gemm_static"}
+    assert set(L.header_symbols()) <= bound
+
+
+def test_status_codes_match_the_header():
+    text = L.HEADER.read_text()
+    for name, value in (("SO101_OK", L.OK), ("SO101_ERR_ARG", L.ERR_ARG), ("SO101_ERR_LAUNCH", L.ERR_LAUNCH),
+                        ("SO101_ERR_WORKSPACE", L.ERR_WORKSPACE), ("SO101_ERR_TIMEOUT", L.ERR_TIMEOUT),
+                        ("SO101_BF16", L.BF16), ("SO101_F32", L.F32), ("SO101_I8", L.I8),
+                        ("SO101_EPI_SILU_GATE", L.EPI_SILU_GATE)):  # fmt: skip
+        assert f"#define {name} {value}" in text, name
+
+
+def test_gemm_rejects_bad_arguments_on_the_host(lib):
+    epi = L.Epilogue(epilogue=L.EPI_NONE, out_scale=1.0)
+    fake = 1 << 20  # never dereferenced: every call below fails its host-side checks
+    rc = lib.so101_gemm(L.BF16, None, 64, fake, 64, fake, 64, L.BF16, 8, 8, 64, C.byref(epi), None,
+                        None, 0, None, 0, None)  # fmt: skip
+    assert rc == L.ERR_ARG  # null x
+    rc = lib.so101_gemm(L.BF16, fake, 100, fake, 100, fake, 8, L.BF16, 8, 8, 100, C.byref(epi), None,
+                        None, 0, None, 0, None)  # fmt: skip
+    assert rc == L.ERR_ARG  # K * 2 bytes not a multiple of 16
+    rc = lib.so101_gemm(L.BF16, fake + 8, 64, fake, 64, fake, 64, L.BF16, 8, 8, 64, C.byref(epi), None,
+                        None, 0, None, 0, None)  # fmt: skip
+    assert rc == L.ERR_ARG  # x not 16-byte aligned
+    bad = L.Epilogue(epilogue=7, out_scale=1.0)
+    rc = lib.so101_gemm(L.BF16, fake, 64, fake, 64, fake, 64, L.BF16, 8, 8, 64, C.byref(bad), None,
+                        None, 0, None, 0, None)  # fmt: skip
+    assert rc == L.ERR_ARG  # unknown epilogue
+    q = L.Epilogue(epilogue=L.EPI_NONE, out_scale=1.0)
+    rc = lib.so101_gemm(L.I8, fake, 64, fake, 64, fake, 64, L.BF16, 8, 8, 64, C.byref(q), None,
+                        None, 0, None, 0, None)  # fmt: skip
+    assert rc == L.ERR_ARG  # int8 operands without weight scales
+
+
+def test_split_k_plans_report_their_workspace(lib):
+    """The global-workspace split-K plan asks for partials and tickets; the cluster plan for none."""
+    need, tick = C.c_int64(), C.c_int64()
+    glob = L.GemmConfig(1, 64, 4, 0, L.GEMM_GLOBAL_SPLITK)
+    assert lib.so101_gemm_workspace(L.BF16, 50, 720, 2048, L.EPI_NONE, C.byref(glob), C.byref(need),
+                                    C.byref(tick)) == L.OK  # fmt: skip
+    assert need.value == 6 * 4 * 64 * 128 * 4 and tick.value == 6
+    clus = L.GemmConfig(1, 64, 4, 0, 0)
+    assert lib.so101_gemm_workspace(L.BF16, 50, 720, 2048, L.EPI_NONE, C.byref(clus), C.byref(need),
+                                    C.byref(tick)) == L.OK  # fmt: skip
+    assert need.value == 0 and tick.value == 0
+    bad = L.GemmConfig(1, 96, 1, 0, 0)  # 96 is not a swap tile width
+    assert lib.so101_gemm_workspace(L.BF16, 50, 720, 2048, L.EPI_NONE, C.byref(bad), C.byref(need),
+                                    C.byref(tick)) == L.ERR_ARG  # fmt: skip
+
+
+def test_gemm_pick_heuristic(lib):
+    """Few token rows stream weights (swap tiling, split over a cluster of at most 8); many rows
+    put tokens on the MMA M side with one split."""
+    cfg = L.GemmConfig()
+    assert lib.so101_gemm_pick(L.BF16, 50, 4096, 720, L.EPI_SILU_GATE, C.byref(cfg)) == L.OK
+    assert cfg.swap == 1 and cfg.bn == 64 and 1 <= cfg.splits <= 8
+    assert lib.so101_gemm_pick(L.I8, 196608, 3072, 768, L.EPI_GELU, C.byref(cfg)) == L.OK
+    assert cfg.swap == 0 and cfg.bn == 256 and cfg.splits == 1
+
+
+def test_other_entry_points_validate_arguments(lib):
+    fake = 1 << 20
+    assert lib.so101_attention(fake, 64, fake, 64, fake, 64, fake, 64, L.BF16, 0.0, 10, 10, 4, 3, 64,
+                               10, 0, None, None, 1, 0, 0, 0, 0, None) == L.ERR_ARG  # nq % nkv
+    assert lib.so101_attention(fake, 64, fake, 64, fake, 64, fake, 64, L.BF16, 0.0, 10, 10, 4, 2, 48,
+                               10, 0, None, None, 1, 0, 0, 0, 0, None) == L.ERR_ARG  # head_dim 48
+    assert lib.so101_rms_norm(fake, 64, L.I8, fake, fake, 64, L.BF16, 4, 64, 1e-5, None) == L.ERR_ARG
+    assert lib.so101_layer_norm(fake, 64, fake, fake, fake, 64, L.I8, 0.0, 4, 64, 1e-6, 1, 0, None) == L.ERR_ARG
+    assert lib.so101_preprocess(fake, 1, 10, 10, 10, 10, 100, 16, fake, L.BF16, 0.0, None) == L.ERR_ARG
+    assert lib.so101_linear_f32(fake, 3, fake, 3, None, None, fake, 3, 2, 3, 3, 0, None) == L.ERR_ARG
+    assert lib.so101_finish(fake, 8, fake, 6, fake, fake, fake, fake, fake, fake, fake, 6, 10, 3, 1, None) == L.ERR_ARG
