@@ -218,6 +218,10 @@ SO101_API int so101_gemm_static(int a_type, const void* x, int64_t ldx, const vo
  * streaming its weights while the previous kernel on the stream drains. */
 SO101_API int so101_set_pdl(int enable);
 
+/* The CUDA error string behind this thread's most recent SO101_ERR_LAUNCH ("" if none). No
+ * counterpart in the reference, whose TensorRT enqueue reports a bare failure. */
+SO101_API const char* so101_last_error(void);
+
 /* Library version string and the compute capability it was built for ("sm_100a"). */
 SO101_API const char* so101_version(void);
 

@@ -101,6 +101,8 @@ def lib() -> C.CDLL:
         fn.restype = C.c_int
     dll.so101_version.restype = C.c_char_p
     dll.so101_version.argtypes = []
+    dll.so101_last_error.restype = C.c_char_p
+    dll.so101_last_error.argtypes = []
     return dll
 
 
@@ -114,6 +116,10 @@ def check(rc: int, what: str) -> None:
     if rc == OK:
         return
     msg = f"{what}: {ERRORS.get(rc, f'status {rc}')}"
+    if rc == ERR_LAUNCH and LIB.exists():
+        cause = lib().so101_last_error().decode()
+        if cause:
+            msg += f" ({cause})"
     if rc == ERR_ARG:
         raise ValueError(msg)
     raise KernelError(msg)

@@ -370,11 +370,10 @@ int launch_attention(const AttnArgs& a, int batch, cudaStream_t stream) {
   constexpr int smem = (64 * (HD + 8) + 4 * 64 * (HD + 8)) * 2;
   static bool configured = false;
   if (!configured) {
-    if (cudaFuncSetAttribute(attention_kernel<HD, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
-            cudaSuccess ||
-        cudaFuncSetAttribute(attention_kernel<HD, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
-            cudaSuccess)
-      return SO101_ERR_LAUNCH;
+    cudaError_t e = cudaFuncSetAttribute(attention_kernel<HD, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(attention_kernel<HD, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return launch_error(e);
     configured = true;
   }
   const int q_tiles = (a.Lq + 63) / 64;
@@ -394,8 +393,16 @@ int launch_attention(const AttnArgs& a, int batch, cudaStream_t stream) {
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   lc.attrs = attr;
   lc.numAttrs = pdl_enabled() ? 2 : 1;
-  return cudaLaunchKernelEx(&lc, attention_kernel<HD, true>, a) == cudaSuccess ? SO101_OK : SO101_ERR_LAUNCH;
+  const cudaError_t e = cudaLaunchKernelEx(&lc, attention_kernel<HD, true>, a);
+  return e == cudaSuccess ? SO101_OK : launch_error(e);
 }
+
+bool attention_tc_eligible(const void* q, long long ldq, const void* k, long long ldk, const void* v, long long ldv,
+                           long long Lq, long long Lk, int nq, int nkv, int hd, long long causal_from,
+                           const float* cos, long long bq, long long bk, long long bv, int o_type);
+int attention_tc_launch(const void* q, long long ldq, const void* k, long long ldk, const void* v, long long ldv,
+                        void* o, long long ldo, int o_type, float o_qscale, long long L, int heads, int batch,
+                        cudaStream_t stream);
 
 }  // namespace so101
 
@@ -420,6 +427,9 @@ extern "C" int so101_attention(const void* q, int64_t ldq, const void* k, int64_
   // q rows and the rotary tables are read in 16-byte pieces
   if (reinterpret_cast<uintptr_t>(q) % 16 || (ldq * 2) % 16 || (bq * 2) % 16) return SO101_ERR_ARG;
   if (cos && (reinterpret_cast<uintptr_t>(cos) % 16 || reinterpret_cast<uintptr_t>(sin) % 16)) return SO101_ERR_ARG;
+  if (attention_tc_eligible(q, ldq, k, ldk, v, ldv, Lq, Lk, nq, nkv, hd, causal_from, cos, bq, bk, bv, o_type) &&
+      ldo % 8 == 0 && bo == Lq * ldo && reinterpret_cast<uintptr_t>(o) % 16 == 0)
+    return attention_tc_launch(q, ldq, k, ldk, v, ldv, o, ldo, o_type, o_qscale, Lq, nq, batch, stream);
   AttnArgs a;
   a.q = static_cast<const __nv_bfloat16*>(q);
   a.k = static_cast<const __nv_bfloat16*>(k);

@@ -22,6 +22,10 @@ int* status_ptr();
 // Host side: whether launches carry the programmatic-dependent-launch attribute (so101_set_pdl).
 bool pdl_enabled();
 
+// Host side: remember the CUDA error behind an SO101_ERR_LAUNCH (so101_last_error reports it) and
+// return that status.
+int launch_error(cudaError_t e);
+
 // Launch `kern` on `stream`, with programmatic dependent launch when enabled: the kernel may then
 // start while the previous kernel on the stream drains, and waits (griddepcontrol.wait) before
 // it touches that kernel's results. Returns SO101_OK or SO101_ERR_LAUNCH.
@@ -37,7 +41,8 @@ int launch_kernel(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cu
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   lc.attrs = attr;
   lc.numAttrs = pdl_enabled() ? 1 : 0;
-  return cudaLaunchKernelEx(&lc, kern, static_cast<KArgs>(args)...) == cudaSuccess ? SO101_OK : SO101_ERR_LAUNCH;
+  const cudaError_t e = cudaLaunchKernelEx(&lc, kern, static_cast<KArgs>(args)...);
+  return e == cudaSuccess ? SO101_OK : launch_error(e);
 }
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {

@@ -908,8 +908,8 @@ template <typename Kern>
 int launch(Kern kern, const CUtensorMap& tx, const CUtensorMap& tw, const GemmArgs& a, dim3 grid, int threads,
            int smem, int cluster, int stages, cudaStream_t stream, bool pdl, int* configured) {
   if (*configured == 0) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBudget) != cudaSuccess)
-      return SO101_ERR_LAUNCH;
+    const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBudget);
+    if (e != cudaSuccess) return launch_error(e);
     *configured = 1;
   }
   cudaLaunchConfig_t lc = {};
@@ -934,7 +934,7 @@ int launch(Kern kern, const CUtensorMap& tx, const CUtensorMap& tw, const GemmAr
   lc.attrs = attr;
   lc.numAttrs = n;
   const cudaError_t e = cudaLaunchKernelEx(&lc, kern, tx, tw, a, stages);
-  return e == cudaSuccess ? SO101_OK : SO101_ERR_LAUNCH;
+  return e == cudaSuccess ? SO101_OK : launch_error(e);
 }
 
 template <int BN, bool SWAP, bool DUAL, bool I8>

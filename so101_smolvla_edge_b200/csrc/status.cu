@@ -25,6 +25,14 @@ int* status_ptr() {
 bool g_pdl = false;
 bool pdl_enabled() { return g_pdl; }
 
+thread_local cudaError_t g_last_error = cudaSuccess;
+
+int launch_error(cudaError_t e) {
+  g_last_error = e;
+  cudaGetLastError();  // a failed launch leaves no sticky error; clear the non-sticky one
+  return SO101_ERR_LAUNCH;
+}
+
 }  // namespace so101
 
 extern "C" int so101_set_pdl(int enable) {
@@ -42,6 +50,10 @@ extern "C" int so101_clear_device_status(void) {
   const int zero = 0;
   return cudaMemcpyToSymbol(so101::g_device_status, &zero, sizeof(int)) == cudaSuccess ? SO101_OK
                                                                                        : SO101_ERR_LAUNCH;
+}
+
+extern "C" const char* so101_last_error(void) {
+  return so101::g_last_error == cudaSuccess ? "" : cudaGetErrorString(so101::g_last_error);
 }
 
 extern "C" const char* so101_version(void) { return "so101_b200 0.1.0 sm_100a"; }

@@ -17,15 +17,16 @@ def lib():
 
 def test_library_loads_and_exports_every_header_symbol(lib):
     names = L.header_symbols()
-    assert len(names) == 19
+    assert len(names) == 20
     missing = [n for n in names if not hasattr(lib, n)]
     assert not missing, missing
     assert lib.so101_version().decode().endswith("sm_100a")
+    assert lib.so101_last_error() == b""
 
 
 def test_bindings_cover_the_header():
     """Every declared entry point has a ctypes signature (or is bound where it is used)."""
-    bound = set(L.SIGNATURES) | {"so101_version", "so101_gemm_static"}
+    bound = set(L.SIGNATURES) | {"so101_version", "so101_last_error", "so101_gemm_static"}
     assert set(L.header_symbols()) <= bound
 
 

@@ -270,6 +270,30 @@ def test_attention(case):
     assert torch.equal(got, again)
 
 
+@pytest.mark.parametrize("out", ["bf16", "int8"])
+def test_siglip_attention_batched(out):
+    """The vision tower's attention: 3 images x 12 heads x 1024 tokens, q/k/v as column slices of
+    the fused qkv rows, unmasked (the tcgen05 path), bf16 or int8 output."""
+    from so101_smolvla_edge_b200.ops import attention
+
+    B, L, H, hd = 3, 1024, 12, 64
+    qkv = rnd(B, L, 3 * H * hd, dtype=torch.bfloat16, scale=2.0)
+    q, k, v = qkv[:, :, : H * hd], qkv[:, :, H * hd : 2 * H * hd], qkv[:, :, 2 * H * hd :]
+    qs = 0.02
+    got = attention(q, k, v, H, H, out_dtype=torch.int8 if out == "int8" else torch.bfloat16,
+                    out_qscale=qs if out == "int8" else None)  # fmt: skip
+    for b in range(B):
+        want = attention_ref(qkv[b], k[b], v[b], H, H, None)
+        if out == "int8":
+            want_q = torch.clamp(torch.round(want / qs), -128, 127)
+            assert (got[b].float() - want_q).abs().max() <= 1
+        else:
+            err = (got[b].float() - want).abs()
+            assert err.max() <= 0.02 * want.abs().max() and err.mean() <= 2e-3 * want.abs().mean() + 1e-4
+    again = attention(q, k, v, H, H, out_dtype=got.dtype, out_qscale=qs if out == "int8" else None)
+    assert torch.equal(got, again)
+
+
 def test_attention_batched_and_strided():
     """A batch of independent problems with k and v as views into the fused qkv rows."""
     from so101_smolvla_edge_b200.ops import attention
