@@ -40,7 +40,13 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 BATCH = 64
-METRIC = "batched chunks/s (64 obs/GPU, W8A8 vision, 50x12 actions, 10 steps)"
+
+
+def metric_name(batch: int) -> str:
+    return f"batched chunks/s ({batch} obs/GPU, W8A8 vision, 50x12 actions, 10 steps)"
+
+
+METRIC = metric_name(BATCH)
 UNIT = "chunks/s"
 CALIB_SEEDS = range(1000, 1032)
 
@@ -274,9 +280,10 @@ def run_ours(args) -> None:
 
     b = seeded_bundle()
     clip = calibrate(b, dev)
-    eng = Engine(b, device=dev, batch=BATCH, trt_precision="int8", act_clip=clip, warmup=2,
+    batch = args.batch
+    eng = Engine(b, device=dev, batch=batch, trt_precision="int8", act_clip=clip, warmup=2,
                  pdl=args.pdl)
-    obs = observations(b, range(rank * BATCH, (rank + 1) * BATCH))
+    obs = observations(b, range(rank * batch, (rank + 1) * batch))
     imgs, states, noises = [o[0] for o in obs], [o[1] for o in obs], [o[2] for o in obs]
     eng._stage(imgs, states, noises)  # inputs resident in HBM for the device-timed loop
     stream = torch.cuda.current_stream(dev)
@@ -302,7 +309,7 @@ def run_ours(args) -> None:
         e1.synchronize()
     barrier()
     ms = max_over_ranks(e0.elapsed_time(e1)) / args.steps
-    value = throughput(world, BATCH, ms)
+    value = throughput(world, batch, ms)
     clk = clocks.summary()
 
     # ---- end to end through the public API (host numpy in, actions out)
@@ -332,7 +339,7 @@ def run_ours(args) -> None:
     with torch.cuda.nvtx.range("roofline_kernel"):
         kms = time_call(fn, cargs)
     s = b.spec
-    M, N, K = BATCH * s.n_cams * s.n_patches, s.vis_mlp, s.vis_dim
+    M, N, K = batch * s.n_cams * s.n_patches, s.vis_mlp, s.vis_dim
     pk, src = peaks()
     int8_peak = 2.0 * pk["bf16_tflops"]
     roof = {"kernel": "gemm_tc_kernel<256,normal,int8> vis.0.fc1", "bound": "tensor",
@@ -378,16 +385,17 @@ def run_ours(args) -> None:
     if rank == 0:
         cpu = cpu_chunks_per_s() if world == 1 and not args.no_cpu else None
         line = {
-            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "metric": metric_name(batch), "value": value, "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "weak",
             "vs_baseline": None, "dtype": "int8+bf16", "data": "synthetic",
-            "config": {"workload": "configs[4]: 64 observations/GPU x (3 x 512^2 u8 cameras, 241-token "
-                                   "prefix, 10 denoise steps), W8A8 SigLIP + bf16 prefix/expert",
-                       "global_batch": world * BATCH, "per_gpu_batch": BATCH,
+            "config": {"workload": f"configs[4]: {batch} observations/GPU x (3 x 512^2 u8 cameras, "
+                                   "241-token prefix, 10 denoise steps), W8A8 SigLIP + bf16 prefix/expert",
+                       "global_batch": world * batch, "per_gpu_batch": batch,
                        "parallelism": f"replicas x{world} (no collective)",
                        "l2": "inputs larger than L2 (0.7 GB weights, >4 GB activations per replay)",
                        "weights": "seeded configs[0] stand-in"},
-            "e2e": {"value": throughput(world, BATCH, e2e_ms), "unit": UNIT,
+            "e2e": {"value": throughput(world, batch, e2e_ms), "unit": UNIT,
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
             "gpu_launches": launches * args.steps,
             "pdl": bool(args.pdl),
@@ -411,6 +419,9 @@ def main() -> None:
     ap.add_argument("--latency-chunks", type=int, default=200)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--pdl", type=int, default=1, help="programmatic dependent launch (1 on, 0 off)")
+    ap.add_argument("--batch", type=int, default=BATCH,
+                    help=f"observations per GPU per step (the metric is quoted at {BATCH}; smaller "
+                         "batches are for profiling captures that must stay small)")  # fmt: skip
     a = ap.parse_args()
     if a.warmup < 3:
         a.warmup = 3

@@ -3,13 +3,18 @@
 //
 // One CTA = 256 query rows of one (image, head), as two groups of 128 (MMA M = 128). Per 128-key
 // tile j:
-//   warp 0 (one thread)  TMA: Q once, then K_j and V_j into a two-stage ring
+//   warp 0 (one thread)  TMA: Q once, then K_j and V_j into separate four-stage rings (a K stage
+//                        frees as soon as S_j is computed, so keys stream several tiles ahead)
 //   warp 1 (one thread)  S_g = Q_g K_j^T  (M 128, N 128, K 64)       -> TMEM S_g
-//                        O_g = P_g V_j    (M 128, N 64,  K 128 keys) -> TMEM O_g, fresh per tile
+//                        O_g += P_g V_j   (M 128, N 64,  K 128 keys) -> TMEM O_g, A operand P_g
+//                                                                       read from TMEM
 //   warps 2-5 / 6-9      softmax for group A / B, one thread per query row (its TMEM lane): the
-//                        row's 128 scores are read twice from TMEM (max, then exp2), P goes to
-//                        shared memory as bf16 in the swizzled K-major layout the MMA reads, and
-//                        O_j is folded into a register accumulator with the running-max rescale.
+//                        row's 128 scores come into registers once, S_g is handed back for the
+//                        next tile's MMA, and P = exp2(s * scale - m) goes to TMEM as bf16 pairs.
+// The output accumulator stays in TMEM across tiles. The running row maximum m is only raised
+// (and O_g, l rescaled, in TMEM) when a tile's maximum exceeds it by more than 2^8; otherwise the
+// stale maximum stays, P values stay <= 2^8, and O / l is unchanged because O and l share the
+// reference maximum.
 // K and Q are K-major operands (head dim contiguous); V is an MN-major operand (head dim
 // contiguous along N, keys along K) straight from its TMA tile. Softmax in fp32 with exp2 on
 // log2(e)/sqrt(d)-scaled scores, P rounded to bf16 for P V, row sums from the fp32 P.
@@ -31,27 +36,33 @@ constexpr int kTcRows = 128;   // rows per group (MMA M)
 constexpr int kTcKeys = 128;   // keys per tile (MMA N of S, K of P V)
 constexpr int kTcHd = 64;
 constexpr int kTcTile = kTcRows * kTcHd * 2;   // 16 KB: a 128 x 64 bf16 tile
-constexpr int kTcThreads = 320;
+#ifndef SO101_ATTN_ISSUERS
+#define SO101_ATTN_ISSUERS 1
+#endif
+constexpr int kIssuers = SO101_ATTN_ISSUERS;     // MMA-issuing warps (1: both groups, 2: one each)
+constexpr int kTcThreads = 32 * (1 + kIssuers + 8);
+constexpr float kStaleMax = 8.f;               // log2 of the largest factor a stale maximum allows
+#ifndef SO101_ATTN_POLY_PAIRS
+#define SO101_ATTN_POLY_PAIRS 0
+#endif
+// Of every 16 score pairs, how many take exp2 from the polynomial (FMA pipe) instead of MUFU.
+constexpr int kPolyPairs = SO101_ATTN_POLY_PAIRS;
 
 // smem offsets (from a 1024-aligned base)
-constexpr int kOffQ = 0;                          // 2 groups x 16 KB
-constexpr int kOffK = kOffQ + 2 * kTcTile;        // 2 stages x 16 KB
-constexpr int kOffV = kOffK + 2 * kTcTile;        // 2 stages x 16 KB
-constexpr int kOffP = kOffV + 2 * kTcTile;        // 2 groups x 32 KB (two 64-key halves each)
-constexpr int kOffBar = kOffP + 4 * kTcTile;
+constexpr int kStages = 4;
+constexpr int kOffQ = 0;                              // 2 groups x 16 KB
+constexpr int kOffK = kOffQ + 2 * kTcTile;            // kStages x 16 KB
+constexpr int kOffV = kOffK + kStages * kTcTile;      // kStages x 16 KB
+constexpr int kOffBar = kOffV + kStages * kTcTile;
 constexpr int kTcSmem = kOffBar + 256 + 1024;
 
-// TMEM columns: S_A, S_B (128 each), O_A, O_B (64 each)
-constexpr uint32_t kColS = 0, kColO = 256;
+// TMEM columns: S_A, S_B (128 fp32 each), P_A, P_B (64 each: 128 bf16 keys in pairs), O_A, O_B (64)
+constexpr uint32_t kColS = 0, kColP = 256, kColO = 384;
 
 // Instruction descriptor: bf16 A/B, fp32 D, A K-major, B K-major (b_mn = 0) or MN-major (1).
 __host__ __device__ constexpr uint32_t idesc_attn(int n, int b_mn) {
   return (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(b_mn) << 16) |
          (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(128 >> 4) << 24);
-}
-
-__device__ __forceinline__ void fence_async_smem() {
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
 __device__ __forceinline__ float ex2(float x) {
@@ -66,20 +77,127 @@ __device__ __forceinline__ uint32_t bf16x2(float lo, float hi) {
   return *reinterpret_cast<const uint32_t*>(&h);
 }
 
+// (d0, d1) = (a0 * b + c, a1 * b + c) as one packed fp32x2 FMA.
+__device__ __forceinline__ void fma2(float& d0, float& d1, float a0, float a1, float b, float c) {
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\t"
+      "mov.b64 rb, {%4, %4};\n\t"
+      "mov.b64 rc, {%5, %5};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\t"
+      "mov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b), "f"(c));
+}
+
+// Packed fp32x2 arithmetic (sm_100): d = a * b + c and d = a + b on (x, y) pairs.
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\t"
+      "mov.b64 rb, {%4, %5};\n\t"
+      "mov.b64 rc, {%6, %7};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\t"
+      "mov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\t"
+      "mov.b64 rb, {%4, %5};\n\t"
+      "add.rn.f32x2 rd, ra, rb;\n\t"
+      "mov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+
+// 2^x for a pair, on the FMA and integer pipes instead of the MUFU unit (which the exp2 of the
+// other pairs keeps busy). x = j + f with j = rint(x) and |f| <= 1/2: adding 1.5 * 2^23 rounds x
+// to an integer held in the low mantissa bits of t; 2^f comes from a degree-3 polynomial (a
+// relative-error minimax fit on [-1/2, 1/2] made for this kernel, max relative error 7.5e-5, far
+// below the bf16 rounding P gets), and 2^j is added into its exponent field as (bits(t) << 23),
+// whose low bits are j. x is clamped to >= -126 so the exponent cannot wrap.
+__device__ __forceinline__ float2 exp2_poly2(float2 x) {
+  constexpr float kRound = 12582912.f;  // 1.5 * 2^23
+  x.x = fmaxf(x.x, -126.f);
+  x.y = fmaxf(x.y, -126.f);
+  const float2 t = fadd2(x, make_float2(kRound, kRound));
+  const float2 r = fadd2(t, make_float2(-kRound, -kRound));
+  const float2 f = fadd2(x, make_float2(-r.x, -r.y));
+  float2 q = ffma2(make_float2(5.517161265e-02f, 5.517161265e-02f), f, make_float2(2.426111251e-01f, 2.426111251e-01f));
+  q = ffma2(q, f, make_float2(6.932609677e-01f, 6.932609677e-01f));
+  q = ffma2(q, f, make_float2(9.999280572e-01f, 9.999280572e-01f));
+  return make_float2(__uint_as_float(__float_as_uint(q.x) + (__float_as_uint(t.x) << 23)),
+                     __uint_as_float(__float_as_uint(q.y) + (__float_as_uint(t.y) << 23)));
+}
+
+// (s0, s1) += (a0, a1) as one packed fp32x2 add.
+__device__ __forceinline__ void add2(float& s0, float& s1, float a0, float a1) {
+  asm("{\n\t.reg .b64 rs, ra;\n\t"
+      "mov.b64 rs, {%0, %1};\n\t"
+      "mov.b64 ra, {%2, %3};\n\t"
+      "add.rn.f32x2 rs, rs, ra;\n\t"
+      "mov.b64 {%0, %1}, rs;\n\t}"
+      : "+f"(s0), "+f"(s1)
+      : "f"(a0), "f"(a1));
+}
+
+// 32 lanes x 32 consecutive 32-bit columns: this thread's lane, columns [col, col+32).
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+
+// This thread's lane, columns [col, col+16) <- r.
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* r) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// D[tmem] (+)= A[tmem] * B[smem desc]: A (M 128 x K 16 bf16) in TMEM, two K elements per column.
+__device__ __forceinline__ void mma_f16_ta(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                           uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 __global__ void __launch_bounds__(kTcThreads, 1)
     attention_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                         const __grid_constant__ CUtensorMap tm_v, const AttnTcArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + kOffBar);
-  uint64_t* q_full = bar;           // [1]
-  uint64_t* kv_full = bar + 1;      // [2]
-  uint64_t* kv_empty = bar + 3;     // [2]
-  uint64_t* s_full = bar + 5;       // [2] per group
-  uint64_t* s_free = bar + 7;       // [2]
-  uint64_t* p_full = bar + 9;       // [2]
-  uint64_t* o_full = bar + 11;      // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 13);
+  uint64_t* q_full = bar;                       // [1]
+  uint64_t* k_full = bar + 1;                   // [kStages]
+  uint64_t* k_empty = k_full + kStages;         // [kStages]
+  uint64_t* v_full = k_empty + kStages;         // [kStages]
+  uint64_t* v_empty = v_full + kStages;         // [kStages]
+  uint64_t* s_full = v_empty + kStages;         // [2] per group: S_g written
+  uint64_t* s_free = s_full + 2;                // [2] per group: S_g read into registers
+  uint64_t* p_full = s_free + 2;                // [2] per group: P_g written (and O_g rescaled)
+  uint64_t* o_full = p_full + 2;                // [2] per group: P_g V accumulated into O_g
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_full + 2);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int head = blockIdx.y, img = blockIdx.z;
@@ -89,9 +207,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
+    for (int i = 0; i < kStages; ++i) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], kIssuers);  // one commit per issuer
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_empty[i], kIssuers);
+    }
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&kv_full[i], 1);
-      mbar_init(&kv_empty[i], 1);
       mbar_init(&s_full[i], 1);
       mbar_init(&s_free[i], 4);
       mbar_init(&p_full[i], 4);
@@ -115,163 +237,193 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       tma_prefetch_desc(&tm_k);
       tma_prefetch_desc(&tm_v);
       grid_dep_wait();
-      const uint64_t keep = policy_evict_last();
+      // Q is read once; K and V are read by the L / 256 CTAs of this (image, head), which run at
+      // the same time, so they need no protection beyond the normal policy
+      const uint64_t once = policy_evict_first(), keep = policy_evict_normal();
       const int xq = head * kTcHd;
       mbar_arrive_expect_tx(q_full, 2 * kTcTile);
-      tma_load_2d(smem + kOffQ, &tm_q, q_full, xq, row0, keep);
-      tma_load_2d(smem + kOffQ + kTcTile, &tm_q, q_full, xq, row0 + kTcRows, keep);
+      tma_load_2d(smem + kOffQ, &tm_q, q_full, xq, row0, once);
+      tma_load_2d(smem + kOffQ + kTcTile, &tm_q, q_full, xq, row0 + kTcRows, once);
       for (int j = 0; j < n_tiles; ++j) {
-        const int st = j & 1;
-        if (j >= 2 && !mbar_wait(&kv_empty[st], ((j >> 1) - 1) & 1u, a.status)) break;
-        mbar_arrive_expect_tx(&kv_full[st], 2 * kTcTile);
-        tma_load_2d(smem + kOffK + st * kTcTile, &tm_k, &kv_full[st], xq, key0 + j * kTcKeys, keep);
-        tma_load_2d(smem + kOffV + st * kTcTile, &tm_v, &kv_full[st], xq, key0 + j * kTcKeys, keep);
+        const int st = j % kStages;
+        const uint32_t back = static_cast<uint32_t>(j / kStages - 1) & 1u;  // phase of the use kStages ago
+        if (j >= kStages && !mbar_wait(&k_empty[st], back, a.status)) break;
+        mbar_arrive_expect_tx(&k_full[st], kTcTile);
+        tma_load_2d(smem + kOffK + st * kTcTile, &tm_k, &k_full[st], xq, key0 + j * kTcKeys, keep);
+        if (j >= kStages && !mbar_wait(&v_empty[st], back, a.status)) break;
+        mbar_arrive_expect_tx(&v_full[st], kTcTile);
+        tma_load_2d(smem + kOffV + st * kTcTile, &tm_v, &v_full[st], xq, key0 + j * kTcKeys, keep);
       }
     }
-  } else if (warp == 1) {
+  } else if (warp <= kIssuers) {
+    // MMA issue: one thread per issuing warp, for groups [g_lo, g_hi). An issuing thread stalls
+    // while the tensor pipe drains its MMAs; with one issuer per group (kIssuers = 2) the other
+    // group's barrier waits and issues proceed meanwhile.
     if (lane == 0) {
       constexpr uint32_t ID_S = idesc_attn(kTcKeys, 0);
       constexpr uint32_t ID_O = idesc_attn(kTcHd, 1);
-      bool ok = mbar_wait(q_full, 0, a.status);
-      for (int j = 0; j < n_tiles && ok; ++j) {
-        const int st = j & 1;
-        if (!mbar_wait(&kv_full[st], (j >> 1) & 1u, a.status)) break;
+      const int g_lo = kIssuers == 2 ? warp - 1 : 0, g_hi = kIssuers == 2 ? warp : 2;
+      // S_j(g) = Q_g K_j^T into TMEM S_g
+      auto issue_s = [&](int j, int g) {
+        const uint64_t qd = sw128_desc(smem_u32(smem + kOffQ + g * kTcTile));
+        const uint64_t kd = sw128_desc(smem_u32(smem + kOffK + (j % kStages) * kTcTile));
+#pragma unroll
+        for (int k = 0; k < kTcHd / 16; ++k)
+          mma_f16(tmem + kColS + g * kTcKeys, qd + 2 * k, kd + 2 * k, ID_S, k > 0 ? 1u : 0u);
+        mma_commit(&s_full[g]);
+      };
+      bool ok = mbar_wait(q_full, 0, a.status) && mbar_wait(&k_full[0], 0, a.status);
+      if (ok) {
         tc_fence_after();
-        const uint32_t kaddr = smem_u32(smem + kOffK + st * kTcTile);
-        const uint32_t vaddr = smem_u32(smem + kOffV + st * kTcTile);
-        for (int g = 0; g < 2; ++g) {
-          if (j >= 1 && !mbar_wait(&s_free[g], (j - 1) & 1u, a.status)) {
-            ok = false;
-            break;
+        for (int g = g_lo; g < g_hi; ++g) issue_s(0, g);
+        mma_commit(&k_empty[0]);  // the K stage is free once every issuer's S MMAs read it
+      }
+      for (int j = 0; j < n_tiles && ok; ++j) {
+        const int st = j % kStages;
+        if (j + 1 < n_tiles) {
+          const int sn = (j + 1) % kStages;
+          ok = mbar_wait(&k_full[sn], static_cast<uint32_t>((j + 1) / kStages) & 1u, a.status);
+          for (int g = g_lo; g < g_hi && ok; ++g) {
+            ok = mbar_wait(&s_free[g], j & 1u, a.status);
+            if (ok) {
+              tc_fence_after();
+              issue_s(j + 1, g);
+            }
           }
-          tc_fence_after();
-          const uint64_t qd = sw128_desc(smem_u32(smem + kOffQ + g * kTcTile));
-          const uint64_t kd = sw128_desc(kaddr);
-#pragma unroll
-          for (int k = 0; k < kTcHd / 16; ++k)
-            mma_f16(tmem + kColS + g * kTcKeys, qd + 2 * k, kd + 2 * k, ID_S, k > 0 ? 1u : 0u);
-          mma_commit(&s_full[g]);
+          if (!ok) break;
+          mma_commit(&k_empty[sn]);
         }
-        if (!ok) break;
-        for (int g = 0; g < 2; ++g) {
-          if (!mbar_wait(&p_full[g], j & 1u, a.status)) {
-            ok = false;
-            break;
-          }
+        if (!mbar_wait(&v_full[st], static_cast<uint32_t>(j / kStages) & 1u, a.status)) break;
+        const uint64_t vd = sw128_desc(smem_u32(smem + kOffV + st * kTcTile));
+        for (int g = g_lo; g < g_hi && ok; ++g) {
+          ok = mbar_wait(&p_full[g], j & 1u, a.status);
+          if (!ok) break;
           tc_fence_after();
-          const uint32_t paddr = smem_u32(smem + kOffP + g * 2 * kTcTile);
-          const uint64_t vd = sw128_desc(vaddr);
 #pragma unroll
-          for (int k = 0; k < kTcKeys / 16; ++k) {
-            // P: keys [16k, 16k+16) sit in the (k / 4)-th 64-key half, 32 bytes per step within it;
-            // V (MN-major): 16 keys = two 8-row groups = 2048 bytes per step
-            const uint64_t pd = sw128_desc(paddr + (k >> 2) * kTcTile) + 2 * (k & 3);
-            mma_f16(tmem + kColO + g * kTcHd, pd, vd + static_cast<uint64_t>(k) * (2048 >> 4), ID_O,
-                    k > 0 ? 1u : 0u);
-          }
+          for (int k = 0; k < kTcKeys / 16; ++k)  // 16 keys = 8 P columns; V: 16 key rows = 2048 bytes
+            mma_f16_ta(tmem + kColO + g * kTcHd, tmem + kColP + g * (kTcKeys / 2) + 8 * k,
+                       vd + static_cast<uint64_t>(k) * (2048 >> 4), ID_O, (j > 0 || k > 0) ? 1u : 0u);
           mma_commit(&o_full[g]);
         }
-        mma_commit(&kv_empty[st]);
+        mma_commit(&v_empty[st]);
       }
     }
   } else {
-    // ---------------- softmax: group g = (warp - 2) / 4, row r = quad * 32 + lane
+    // ---------------- softmax: group g = (warp - 1 - kIssuers) / 4, row r = quad * 32 + lane
     grid_dep_wait();
-    const int g = (warp - 2) >> 2;
+    const int g = (warp - 1 - kIssuers) >> 2;
     const int quad = warp & 3;
     const int r = quad * 32 + lane;
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(quad * 32) << 16);
     const uint32_t s_addr = lane_base + kColS + g * kTcKeys;
+    const uint32_t p_addr = lane_base + kColP + g * (kTcKeys / 2);
     const uint32_t o_addr = lane_base + kColO + g * kTcHd;
-    uint8_t* P = smem + kOffP + g * 2 * kTcTile;
+    const float sc = a.scale_log2;
     float m = -INFINITY, l = 0.f;
-    float acc[kTcHd];
-#pragma unroll
-    for (int d = 0; d < kTcHd; ++d) acc[d] = 0.f;
-    for (int j = 0; j < n_tiles; ++j) {
-      if (!mbar_wait(&s_full[g], j & 1u, a.status)) break;
+    bool ok = true;
+    for (int j = 0; j < n_tiles && ok; ++j) {
+      if (!mbar_wait(&s_full[g], j & 1u, a.status)) {
+        ok = false;
+        break;
+      }
       tc_fence_after();
-      // pass 1: the tile's row maximum
-      float tmax = -INFINITY;
+      uint32_t sv[kTcKeys];
 #pragma unroll
-      for (int c = 0; c < kTcKeys; c += 32) {
-        uint32_t v0[16], v1[16];
-        tmem_ld16(s_addr + c, v0);
-        tmem_ld16(s_addr + c + 16, v1);
-        tmem_ld_wait();
-#pragma unroll
-        for (int e = 0; e < 16; ++e) tmax = fmaxf(tmax, fmaxf(__uint_as_float(v0[e]), __uint_as_float(v1[e])));
-      }
-      const float m_new = fmaxf(m, tmax * a.scale_log2);
-      const float alpha = ex2(m - m_new);
-      // pass 2: P = exp2(s * scale - m_new) as bf16 into the swizzled K-major tile, row sums in fp32
-      float lsum = 0.f;
-#pragma unroll
-      for (int c = 0; c < kTcKeys; c += 32) {
-        uint32_t v0[16], v1[16];
-        tmem_ld16(s_addr + c, v0);
-        tmem_ld16(s_addr + c + 16, v1);
-        tmem_ld_wait();
-        uint32_t pk[16];
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const float p0 = ex2(fmaf(__uint_as_float(v0[2 * e]), a.scale_log2, -m_new));
-          const float p1 = ex2(fmaf(__uint_as_float(v0[2 * e + 1]), a.scale_log2, -m_new));
-          const float p2 = ex2(fmaf(__uint_as_float(v1[2 * e]), a.scale_log2, -m_new));
-          const float p3 = ex2(fmaf(__uint_as_float(v1[2 * e + 1]), a.scale_log2, -m_new));
-          lsum += (p0 + p1) + (p2 + p3);
-          pk[e] = bf16x2(p0, p1);
-          pk[8 + e] = bf16x2(p2, p3);
-        }
-        // keys c .. c+31 = four 16-byte chunks of row r in half c / 64, chunk (c % 64) / 8 + i
-        uint8_t* rowp = P + (c >> 6) * kTcTile + (r >> 3) * 1024 + (r & 7) * 128;
-        const int ch = (c & 63) >> 3;  // first of this row's four 16-byte chunks
-        *reinterpret_cast<uint4*>(rowp + (((ch + 0) ^ (r & 7)) << 4)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-        *reinterpret_cast<uint4*>(rowp + (((ch + 1) ^ (r & 7)) << 4)) = make_uint4(pk[4], pk[5], pk[6], pk[7]);
-        *reinterpret_cast<uint4*>(rowp + (((ch + 2) ^ (r & 7)) << 4)) = make_uint4(pk[8], pk[9], pk[10], pk[11]);
-        *reinterpret_cast<uint4*>(rowp + (((ch + 3) ^ (r & 7)) << 4)) = make_uint4(pk[12], pk[13], pk[14], pk[15]);
-      }
+      for (int c = 0; c < kTcKeys; c += 32) tmem_ld32(s_addr + c, sv + c);
+      tmem_ld_wait();
       tc_fence_before();
-      fence_async_smem();
       __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&s_free[g]);
-        mbar_arrive(&p_full[g]);
-      }
-      l = l * alpha + lsum;
-      m = m_new;
-      // O += alpha-rescaled previous + this tile's P V
-      if (!mbar_wait(&o_full[g], j & 1u, a.status)) break;
-      tc_fence_after();
+      if (lane == 0) mbar_arrive(&s_free[g]);  // the MMA may write S_{j+1} now
+      // row maximum over eight independent chains (short dependency chains keep the pipe busy)
+      float mx[8];
 #pragma unroll
-      for (int c = 0; c < kTcHd; c += 16) {
-        uint32_t ov[16];
-        tmem_ld16(o_addr + c, ov);
-        tmem_ld_wait();
+      for (int t = 0; t < 8; ++t) mx[t] = __uint_as_float(sv[t]);
 #pragma unroll
-        for (int e = 0; e < 16; ++e) acc[c + e] = fmaf(acc[c + e], alpha, __uint_as_float(ov[e]));
+      for (int e = 8; e < kTcKeys; e += 8)
+#pragma unroll
+        for (int t = 0; t < 8; ++t) mx[t] = fmaxf(mx[t], __uint_as_float(sv[e + t]));
+      const float m_tile =
+          fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7]))) * sc;
+      const bool raise = m_tile > m + kStaleMax;
+      const float alpha = raise ? ex2(m - m_tile) : 1.f;  // 0 on the first tile (m = -inf)
+      if (raise) m = m_tile;
+      const float neg_m = -m;
+      // P = exp2(s * scale - m) as bf16 pairs, in registers first: the previous tile's P V may
+      // still be reading P_g, and it runs while these exponentials are computed
+      uint32_t pk[kTcKeys / 2];
+      float ls[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // row sum over four packed chains
+#pragma unroll
+      for (int e = 0; e < kTcKeys; e += 2) {
+        float x0, x1;
+        fma2(x0, x1, __uint_as_float(sv[e]), __uint_as_float(sv[e + 1]), sc, neg_m);
+        float p0, p1;
+        if (((e >> 1) & 15) < kPolyPairs) {
+          const float2 pp = exp2_poly2(make_float2(x0, x1));
+          p0 = pp.x, p1 = pp.y;
+        } else {
+          p0 = ex2(x0), p1 = ex2(x1);
+        }
+        const int t = (e >> 1) & 3;
+        add2(ls[2 * t], ls[2 * t + 1], p0, p1);
+        pk[e >> 1] = bf16x2(p0, p1);
       }
+      const float s0 = (ls[0] + ls[2]) + (ls[4] + ls[6]), s1 = (ls[1] + ls[3]) + (ls[5] + ls[7]);
+      if (j > 0) {
+        // P_{j-1} V has landed: P_g may be overwritten and O_g is stable for a rescale
+        if (!mbar_wait(&o_full[g], (j - 1) & 1u, a.status)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+      }
+#pragma unroll
+      for (int c = 0; c < kTcKeys / 2; c += 16) tmem_st16(p_addr + c, pk + c);
+      if (j > 0 && __any_sync(0xffffffffu, raise)) {
+        // the row maximum rose by more than 2^8 somewhere in this warp: rescale O_g rows
+#pragma unroll
+        for (int c = 0; c < kTcHd; c += 32) {
+          uint32_t ov[32];
+          tmem_ld32(o_addr + c, ov);
+          tmem_ld_wait();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * alpha);
+          tmem_st16(o_addr + c, ov);
+          tmem_st16(o_addr + c + 16, ov + 16);
+        }
+      }
+      l = l * alpha + (s0 + s1);
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[g]);
     }
-    // write O / l for this row
-    const float inv = 1.f / l;
-    const long long orow = row0 + g * kTcRows + r;
-    if (a.o_type == SO101_BF16) {
-      uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.o) + orow * a.ldo + head * kTcHd);
+    // O / l for this row
+    if (ok && mbar_wait(&o_full[g], (n_tiles - 1) & 1u, a.status)) {
+      tc_fence_after();
+      uint32_t ov[kTcHd];
+      tmem_ld32(o_addr, ov);
+      tmem_ld32(o_addr + 32, ov + 32);
+      tmem_ld_wait();
+      const float inv = 1.f / l;
+      const long long orow = row0 + g * kTcRows + r;
+      if (a.o_type == SO101_BF16) {
+        uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.o) + orow * a.ldo + head * kTcHd);
 #pragma unroll
-      for (int q = 0; q < kTcHd / 8; ++q) {
-        const float* v = acc + 8 * q;
-        dst[q] = make_uint4(bf16x2(v[0] * inv, v[1] * inv), bf16x2(v[2] * inv, v[3] * inv),
-                            bf16x2(v[4] * inv, v[5] * inv), bf16x2(v[6] * inv, v[7] * inv));
-      }
-    } else {
-      uint4* dst = reinterpret_cast<uint4*>(static_cast<int8_t*>(a.o) + orow * a.ldo + head * kTcHd);
+        for (int q = 0; q < kTcHd / 8; ++q) {
+          const float* v = reinterpret_cast<const float*>(ov) + 8 * q;
+          dst[q] = make_uint4(bf16x2(v[0] * inv, v[1] * inv), bf16x2(v[2] * inv, v[3] * inv),
+                              bf16x2(v[4] * inv, v[5] * inv), bf16x2(v[6] * inv, v[7] * inv));
+        }
+      } else {
+        uint4* dst = reinterpret_cast<uint4*>(static_cast<int8_t*>(a.o) + orow * a.ldo + head * kTcHd);
 #pragma unroll
-      for (int q = 0; q < kTcHd / 16; ++q) {
-        const float* v = acc + 16 * q;
-        dst[q] = make_uint4(pack4_i8(v[0] * inv, v[1] * inv, v[2] * inv, v[3] * inv, a.o_qinv),
-                            pack4_i8(v[4] * inv, v[5] * inv, v[6] * inv, v[7] * inv, a.o_qinv),
-                            pack4_i8(v[8] * inv, v[9] * inv, v[10] * inv, v[11] * inv, a.o_qinv),
-                            pack4_i8(v[12] * inv, v[13] * inv, v[14] * inv, v[15] * inv, a.o_qinv));
+        for (int q = 0; q < kTcHd / 16; ++q) {
+          const float* v = reinterpret_cast<const float*>(ov) + 16 * q;
+          dst[q] = make_uint4(pack4_i8(v[0] * inv, v[1] * inv, v[2] * inv, v[3] * inv, a.o_qinv),
+                              pack4_i8(v[4] * inv, v[5] * inv, v[6] * inv, v[7] * inv, a.o_qinv),
+                              pack4_i8(v[8] * inv, v[9] * inv, v[10] * inv, v[11] * inv, a.o_qinv),
+                              pack4_i8(v[12] * inv, v[13] * inv, v[14] * inv, v[15] * inv, a.o_qinv));
+        }
       }
     }
   }

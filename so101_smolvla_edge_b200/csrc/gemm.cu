@@ -19,9 +19,10 @@
 //
 // gemm_persistent_kernel (normal tiling for large M, 1 CTA per SM, 320 threads)
 //   Each CTA loops over output tiles. Warp 0 streams A/B tiles through the ring, warp 1 issues the
-//   MMAs into one of two TMEM accumulators (2 x BN columns) and eight epilogue warps drain the other,
-//   so the epilogue of tile i overlaps the MMAs of tile i+1. Epilogue warp e reads lane quadrant
-//   (e + 2) % 4 and column half e / 4.
+//   MMAs into one of two TMEM accumulators (2 x BN columns) and sixteen epilogue warps drain the
+//   other, so the epilogue of tile i overlaps the MMAs of tile i+1. Epilogue warp e reads lane
+//   quadrant (e + 2) % 4 and column quarter e / 4 into registers in one go and releases the
+//   accumulator before its arithmetic.
 //
 // DUAL (SiLU gate): two weight tiles per stage (gate rows n and up rows N + n of the fused
 // [gate; up] matrix) into two accumulators; the epilogue writes silu(gate) * up.
@@ -609,9 +610,10 @@ __global__ void __launch_bounds__(128, 1)
 }
 
 // ================================================================ persistent, warp-specialized
-constexpr int kEpiWarps = 8;
+constexpr int kEpiWarps = 16;                         // four per SM sub-partition
+constexpr int kEpiCols = 256 / (kEpiWarps / 4);       // most columns one epilogue warp owns (BN 256)
 constexpr int kBarrierBytes = 256;                    // ring barriers, accumulator barriers, TMEM slot
-constexpr int kConstBytes = kEpiWarps * 3 * 128 * 4;  // column constants, BN <= 256
+constexpr int kConstBytes = kEpiWarps * 3 * kEpiCols * 4;  // column constants
 
 template <int BN, bool DUAL, bool I8>
 __global__ void __launch_bounds__(32 * (2 + kEpiWarps), 1)
@@ -733,26 +735,29 @@ __global__ void __launch_bounds__(32 * (2 + kEpiWarps), 1)
       }
     }
   } else {
-    // epilogue warps
+    // epilogue warps: warp e reads TMEM lane quadrant warp % 4 and column group e / 4 (COLS
+    // columns). It loads its whole slice of the accumulator into registers, hands the TMEM buffer
+    // back to the MMA warp, and only then runs the epilogue arithmetic and the stores.
     grid_dep_wait();
+    constexpr int G = kEpiWarps / 4;
+    constexpr int COLS = BN / G;
+    constexpr int CH = COLS / 16;
+    static_assert(COLS % 16 == 0 && COLS * NB <= 64, "epilogue slice must fit in registers");
     const int e = warp - 2;
     const int quad = warp & 3;
-    constexpr int HALF = BN / 2;
-    const int c_lo = (e / 4) * HALF;
+    const int c_lo = (e / 4) * COLS;
+    float* kc = consts + e * 3 * kEpiCols;
+    float* kb = kc + kEpiCols;
+    float* ku = kb + kEpiCols;
     int local = 0;
     for (int tile = blockIdx.x; tile < a.num_tiles; tile += gridDim.x, ++local) {
       const int buf = local & 1;
       const uint32_t use = static_cast<uint32_t>(local >> 1);
-      if (!mbar_wait(&acc_full[buf], use & 1u, a.status)) break;
-      tc_fence_after();
       const int p0 = (tile / a.tiles_q) * 128, q0 = (tile % a.tiles_q) * BN;
       const int p = p0 + quad * 32 + lane;
-      const uint32_t taddr = tmem + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(buf * NACC);
-      float* kc = consts + e * 3 * HALF;
-      float* kb = kc + HALF;
-      float* ku = kb + HALF;
+      // this tile's column constants, staged while the MMAs run
       __syncwarp();
-      for (int j = lane; j < HALF; j += 32) {
+      for (int j = lane; j < COLS; j += 32) {
         const int n = q0 + c_lo + j;
         const bool in = n < a.N;
         kc[j] = I8 ? (in ? a.x_scale * __ldg(a.w_scale + n) : 0.f) : 1.f;
@@ -760,27 +765,34 @@ __global__ void __launch_bounds__(32 * (2 + kEpiWarps), 1)
         ku[j] = (I8 && DUAL && in) ? a.x_scale * __ldg(a.w_scale + a.N + n) : 1.f;
       }
       __syncwarp();
-      float v[16], u[16];
-#pragma unroll 1
-      for (int c = c_lo; c < c_lo + HALF; c += 16) {
-        uint32_t r0[16], r1[16];
-        tmem_ld16(taddr + c, r0);
-        if (DUAL) tmem_ld16(taddr + BN + c, r1);
-        tmem_ld_wait();
-        if (a.vec_ok && p < a.M && q0 + c + 16 <= a.N) {
-          epilogue_row16_fast<DUAL, I8>(a, p, q0 + c, r0, r1, kc + (c - c_lo), kb + (c - c_lo), ku + (c - c_lo));
-        } else {
+      if (!mbar_wait(&acc_full[buf], use & 1u, a.status)) break;
+      tc_fence_after();
+      const uint32_t taddr = tmem + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(buf * NACC + c_lo);
+      uint32_t r0[CH][16], r1[DUAL ? CH : 1][16];
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            v[j] = acc_value<I8>(r0[j]);
-            u[j] = DUAL ? acc_value<I8>(r1[j]) : 0.f;
-          }
-          epilogue16<false, DUAL, I8>(a, p, q0 + c, v, u);
-        }
+      for (int c = 0; c < CH; ++c) {
+        tmem_ld16(taddr + 16 * c, r0[c]);
+        if constexpr (DUAL) tmem_ld16(taddr + BN + 16 * c, r1[c]);
       }
+      tmem_ld_wait();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[buf]);
+#pragma unroll
+      for (int c = 0; c < CH; ++c) {
+        const int q = q0 + c_lo + 16 * c;
+        if (a.vec_ok && p < a.M && q + 16 <= a.N) {
+          epilogue_row16_fast<DUAL, I8>(a, p, q, r0[c], r1[DUAL ? c : 0], kc + 16 * c, kb + 16 * c, ku + 16 * c);
+        } else {
+          float v[16], u[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            v[j] = acc_value<I8>(r0[c][j]);
+            u[j] = DUAL ? acc_value<I8>(r1[DUAL ? c : 0][j]) : 0.f;
+          }
+          epilogue16<false, DUAL, I8>(a, p, q, v, u);
+        }
+      }
     }
   }
 
@@ -1010,7 +1022,10 @@ extern "C" int so101_gemm_pick(int a_type, int64_t M, int64_t N, int64_t K, int 
     c.splits = s < 1 ? 1 : (s > max_s ? max_s : s);
   } else {
     c.swap = 0;
-    c.bn = (N >= 1024 && !dual) ? 256 : 128;
+    // 256-wide tiles halve the A-operand shared-memory reads per MMA (128 x 128 tiles need the
+    // full shared-memory bandwidth); take them whenever they still give every SM a tile.
+    const long long tiles256 = ((M + 127) / 128) * ((N + 255) / 256);
+    c.bn = (!dual && (N >= 1024 || (N >= 512 && tiles256 >= sms))) ? 256 : 128;
     if (N <= 128) c.bn = 64;
     const long long tiles = ((M + 127) / 128) * ((N + c.bn - 1) / c.bn);
     c.splits = 1;
