@@ -342,11 +342,20 @@ def run_ours(args) -> None:
     M, N, K = batch * s.n_cams * s.n_patches, s.vis_mlp, s.vis_dim
     pk, src = peaks()
     int8_peak = 2.0 * pk["bf16_tflops"]
-    roof = {"kernel": "gemm_tc_kernel<256,normal,int8> vis.0.fc1", "bound": "tensor",
+    roof = {"kernel": "gemm_persistent_kernel<256,0,1> vis.0.fc1 (W8A8, GELU, int8 out)", "bound": "tensor",
             "achieved": 2.0 * M * N * K / (kms * 1e-3) / 1e12, "peak": int8_peak, "unit": "TOP/s",
             "traffic": profile_traffic("vis.fc1"), "ms": kms,
             "peak_source": f"2 x {src} bf16 dense ({pk['bf16_tflops']} TF/s): int8 dense rate is twice bf16"}  # fmt: skip
     roof["frac"] = roof["achieved"] / roof["peak"]
+    # second family: SigLIP self-attention on tcgen05 (4 L^2 d flops per image and head)
+    fn, cargs = find_call(p.progs["vision"], "0.attn")
+    ams = time_call(fn, cargs, reps=10)
+    n_img, hd = batch * s.n_cams, s.vis_dim // s.vis_heads
+    aflops = 4.0 * n_img * s.vis_heads * s.n_patches**2 * hd
+    roof_attn = {"kernel": "attention_tc_kernel vis.0.attn", "bound": "tensor",
+                 "achieved": aflops / (ams * 1e-3) / 1e12, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+                 "traffic": profile_traffic("vis.attn"), "ms": ams, "peak_source": f"{src} bf16 dense"}  # fmt: skip
+    roof_attn["frac"] = roof_attn["achieved"] / roof_attn["peak"]
     launches = eng.launches()
     del eng
     torch.cuda.empty_cache()
@@ -401,6 +410,7 @@ def run_ours(args) -> None:
             "pdl": bool(args.pdl),
             "max_err_rad": err,
             "roofline": roof,
+            "roofline_attention": roof_attn,
             "latency": lat,
             "clocks": clk,
             "cpu_baseline": cpu,
