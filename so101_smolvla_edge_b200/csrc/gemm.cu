@@ -1018,8 +1018,18 @@ extern "C" int so101_gemm_pick(int a_type, int64_t M, int64_t N, int64_t K, int 
     const int tiles = static_cast<int>((N + 127) / 128);
     int s = sms / tiles;
     if (s > kMaxCluster) s = kMaxCluster;
-    const int max_s = kb / 2 > 0 ? kb / 2 : 1;  // at least two K blocks per split
+    const int max_s = kb / 3 > 0 ? kb / 3 : 1;  // at least three K blocks per split
     c.splits = s < 1 ? 1 : (s > max_s ? max_s : s);
+  } else if (M <= 256 && a_type == SO101_BF16 && !dual) {
+    // a few hundred rows (the prefix at batch 1): still weight streaming, tokens in 64-row tiles
+    // on MMA N, so each weight slab is read from HBM once and from L2 by the other token tiles
+    c.swap = 1;
+    c.bn = 64;
+    c.splits = kb >= 8 ? 4 : (kb >= 4 ? 2 : 1);
+  } else if (M <= 256 && a_type == SO101_BF16) {
+    c.swap = 0;
+    c.bn = 64;
+    c.splits = 1;
   } else {
     c.swap = 0;
     // 256-wide tiles halve the A-operand shared-memory reads per MMA (128 x 128 tiles need the

@@ -99,18 +99,27 @@ def test_config0_actions_within_north_star(config0_engine):
     assert max(errs) <= ACTION_TOL, errs
 
 
-def test_batched_equals_single():
-    """infer_batch over B observations agrees with B single-chunk engines."""
+def test_batched_matches_reference_and_single():
+    """infer_batch over B observations: every chunk within the action tolerance of the reference's
+    float32 chunk (the seeds with goldens) and of the single-chunk engine. The batched GEMMs have
+    B times the rows and may tile differently (rows on the MMA M or N side, other K splits), so
+    the two engines agree to rounding, not bit for bit."""
     from so101_smolvla_edge_b200.engine import Engine
 
-    b = case_bundle("small_absolute")
+    case = "small_absolute"
+    g = golden(case)
+    b = case_bundle(case)
     obs = [observation(b, s) for s in range(3)]
     single = Engine(b, warmup=1)
     batched = Engine(b, warmup=1, batch=3)
     got = batched.infer_batch([o[0] for o in obs], [o[1] for o in obs], [o[2] for o in obs])
     for i, (images, state, noise) in enumerate(obs):
         want = single.infer(images, state, noise)
-        assert np.abs(got[i] - want).max() <= 1e-3 * max(1.0, np.abs(want).max())
+        scale = max(1.0, np.abs(want).max())
+        assert np.abs(got[i] - want).max() <= ACTION_TOL * scale, i
+        if f"s{i}.actions" in g:
+            ref = g[f"s{i}.actions"]
+            assert np.abs(got[i] - ref).max() <= ACTION_TOL * max(1.0, np.abs(ref).max()), i
 
 
 def _int8_check(g, a, scale):
