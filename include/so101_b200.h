@@ -218,6 +218,46 @@ SO101_API int so101_gemm_static(int a_type, const void* x, int64_t ldx, const vo
  * streaming its weights while the previous kernel on the stream drains. */
 SO101_API int so101_set_pdl(int enable);
 
+/* ----------------------------------------------------------------- persistent expert step
+ * The action expert's layers for one denoising step of ONE observation (rows <= 64 action rows)
+ * as a single cooperative kernel: per layer RMSNorm -> q|k|v (RoPE on k, k/v written into the
+ * cache rows [prefix_len, prefix_len + rows)) -> attention -> o + residual -> RMSNorm -> SwiGLU
+ * gate/up -> down + residual, with grid barriers between the phases. It replaces the chain of
+ * per-op launches the reference's TritonPath.velocity makes for the 16 expert layers
+ * (pkg/model/smolvla_triton.py:106-130, the loop over layers); the reference has no fused
+ * counterpart. Requirements: head_dim 64, n_layers <= 16, exp_dim and mlp_dim multiples of 8,
+ * every pointer 16-byte aligned, bf16 weights, fp32 norm weights, fp32 e. */
+typedef struct so101_expert_layer {
+  const void* w_attn;     /* self: [q; k; v] rows (q_dim + 2 kv_dim) x exp_dim; cross: q rows q_dim x exp_dim */
+  const void* w_o;        /* exp_dim x q_dim */
+  const void* w_gate_up;  /* 2 mlp_dim x exp_dim: gate rows, then up rows */
+  const void* w_down;     /* exp_dim x mlp_dim */
+  const float* ln_in;     /* exp_dim */
+  const float* ln_post;   /* exp_dim */
+  void* k;                /* self: key cache, (prefix_len + rows) x kv_dim bf16; cross: prefix_len x kv_dim */
+  void* v;
+  int self_attn;
+} so101_expert_layer;
+
+typedef struct so101_expert_step {
+  int n_layers, rows, prefix_len, exp_dim, q_dim, kv_dim, n_heads, n_kv, head_dim, mlp_dim;
+  float eps;
+  so101_expert_layer layer[16];
+  float* e;                /* rows x exp_dim fp32 residual stream, updated in place */
+  void* q;                 /* rows x q_dim bf16 scratch */
+  void* attn;              /* rows x q_dim bf16 scratch */
+  void* act;               /* rows x mlp_dim bf16 scratch */
+  const float* cos_self;   /* rows x head_dim / 2: RoPE of the step's own positions */
+  const float* sin_self;
+  const float* cos_cross;  /* rows x head_dim / 2: RoPE of the cross-attention queries */
+  const float* sin_cross;
+  void* workspace;         /* so101_expert_step_workspace bytes; 16-byte aligned */
+  int64_t workspace_bytes;
+} so101_expert_step;
+
+SO101_API int so101_expert_step_workspace(const so101_expert_step* s, int64_t* bytes);
+SO101_API int so101_expert_step_run(const so101_expert_step* s, cudaStream_t stream);
+
 /* The CUDA error string behind this thread's most recent SO101_ERR_LAUNCH ("" if none). No
  * counterpart in the reference, whose TensorRT enqueue reports a bare failure. */
 SO101_API const char* so101_last_error(void);

@@ -57,6 +57,25 @@ class GemmConfig(C.Structure):
 
 P, I, I64, F, S = C.c_void_p, C.c_int, C.c_int64, C.c_float, C.c_void_p  # S: cudaStream_t
 
+EXPERT_MAX_LAYERS = 16
+
+
+class ExpertLayer(C.Structure):
+    """`so101_expert_layer`: one expert layer's weights, norms and K/V rows."""
+
+    _fields_ = [("w_attn", P), ("w_o", P), ("w_gate_up", P), ("w_down", P), ("ln_in", P),
+                ("ln_post", P), ("k", P), ("v", P), ("self_attn", C.c_int)]  # fmt: skip
+
+
+class ExpertStep(C.Structure):
+    """`so101_expert_step`: the persistent expert-step kernel's problem."""
+
+    _fields_ = [(n, C.c_int) for n in ("n_layers", "rows", "prefix_len", "exp_dim", "q_dim", "kv_dim",
+                                       "n_heads", "n_kv", "head_dim", "mlp_dim")] + [
+        ("eps", C.c_float), ("layer", ExpertLayer * EXPERT_MAX_LAYERS), ("e", P), ("q", P), ("attn", P),
+        ("act", P), ("cos_self", P), ("sin_self", P), ("cos_cross", P), ("sin_cross", P),
+        ("workspace", P), ("workspace_bytes", C.c_int64)]  # fmt: skip
+
 SIGNATURES = {
     "so101_gemm": [I, P, I64, P, I64, P, I64, I, I64, I64, I64, C.POINTER(Epilogue),
                    C.POINTER(GemmConfig), P, I64, P, I64, S],
@@ -78,6 +97,8 @@ SIGNATURES = {
     "so101_device_status": [],
     "so101_clear_device_status": [],
     "so101_set_pdl": [I],
+    "so101_expert_step_workspace": [C.POINTER(ExpertStep), C.POINTER(C.c_int64)],
+    "so101_expert_step_run": [C.POINTER(ExpertStep), S],
 }  # fmt: skip
 
 

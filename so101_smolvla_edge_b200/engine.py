@@ -87,6 +87,7 @@ class Engine:
         batch: int = 1,
         act_clip: dict[str, float] | str | Path | None = None,
         pdl: bool | None = None,
+        expert_step: str | None = None,
     ):
         self.device = dev = torch.device(device)
         if dev.type == "cuda" and dev.index is None:
@@ -123,7 +124,9 @@ class Engine:
         self.pdl = bool(pdl)
         ops.set_pdl(self.pdl)
         torch.cuda.set_device(dev)
-        self.path = B200Path(b, dev, self.batch, trt_precision, clip)
+        if expert_step is None:  # "fused": the persistent expert-step kernel; default the per-op chain
+            expert_step = os.environ.get("SO101_EXPERT_STEP", "auto")
+        self.path = B200Path(b, dev, self.batch, trt_precision, clip, expert_step)
         self.tp = self.path  # the reference's attribute for the custom-kernel path
         p = self.path
         self.img, self.state, self.noise, self.out = p.img, p.state, p.noise, p.out

@@ -107,7 +107,8 @@ class B200Path:
     """Weights, buffers and launch programs of one chunk (or B chunks) on one GPU."""
 
     def __init__(self, bundle: Bundle, device: torch.device, batch: int = 1,
-                 vision_precision: str = "bf16", act_clip: dict[str, float] | None = None):  # fmt: skip
+                 vision_precision: str = "bf16", act_clip: dict[str, float] | None = None,
+                 expert_step: str = "auto"):  # fmt: skip
         s = self.spec = bundle.spec
         why = unsupported(s)
         if why:
@@ -130,10 +131,13 @@ class B200Path:
         self.h_img, self.w_img = bundle.meta["image_hw"]
         self.state_dim, self.action_dim = bundle.meta["state_dim"], bundle.meta["action_dim"]
         self.repr = REPRS[bundle.meta["action_repr"]]
+        if expert_step not in ("auto", "fused", "ops"):
+            raise ValueError(f"expert_step must be 'auto', 'fused' or 'ops', not {expert_step!r}")
         self.ws = workspace(device)  # split-K partials and tickets exist before any capture
         self._amax: tuple[torch.Tensor, dict[str, int]] | None = None  # calibration hooks
         self._upload(bundle)
         self._alloc()
+        self.xs = self._expert_step(expert_step)
         self.progs = {"vision": Program("vision"), "prefix": Program("prefix"),
                       "denoise": Program("denoise")}  # fmt: skip
         self._build_vision(self.progs["vision"])
@@ -227,6 +231,45 @@ class B200Path:
         self.attn_e = z(B * H, s.q_dim, dtype=bf)
         self.mlp_e = z(B * H, s.exp_mlp, dtype=bf)
         self.v_buf = z(B * H, s.max_action)
+
+    def _expert_step(self, mode: str) -> L.ExpertStep | None:
+        """The persistent expert-step problem for one observation, or None (per-op launches).
+
+        "fused" requires it (one observation, shapes the library accepts); "auto" and "ops" use the
+        per-op launch chain, which is the faster of the two on B200 (0.78 ms against 1.36 ms per
+        denoising step at configs[0]: the persistent kernel's phases are chains of dependent
+        global-memory round trips plus a grid barrier, while consecutive per-op kernels overlap
+        their prologues through programmatic dependent launch)."""
+        s, w = self.spec, self.w
+        if mode in ("ops", "auto"):
+            return None
+        if self.B != 1 or s.n_layers > L.EXPERT_MAX_LAYERS:
+            raise ValueError("the fused expert step serves one observation of at most 16 layers")
+        H = self.H
+        xs = L.ExpertStep()
+        xs.n_layers, xs.rows, xs.prefix_len = s.n_layers, H, self.L
+        xs.exp_dim, xs.q_dim, xs.kv_dim = s.exp_dim, s.q_dim, s.kv_dim
+        xs.n_heads, xs.n_kv, xs.head_dim, xs.mlp_dim = s.n_heads, s.n_kv, s.head_dim, s.exp_mlp
+        xs.eps = s.rms_eps
+        for i in range(s.n_layers):
+            pre, y = f"exp.{i}.", xs.layer[i]
+            y.self_attn = int(s.is_self_attn(i))
+            y.w_attn = w[pre + ("qkv" if y.self_attn else "q")].data_ptr()
+            y.w_o, y.w_gate_up = w[pre + "o"].data_ptr(), w[pre + "gate_up"].data_ptr()
+            y.w_down = w[pre + "down"].data_ptr()
+            y.ln_in, y.ln_post = w[pre + "ln_in"].data_ptr(), w[pre + "ln_post"].data_ptr()
+            kt, vt = (self.ck[i], self.cv[i]) if y.self_attn else (self.kx[i], self.vx[i])
+            y.k, y.v = kt.data_ptr(), vt.data_ptr()
+        self.q_e = torch.zeros(H, s.q_dim, dtype=torch.bfloat16, device=self.dev)
+        xs.e, xs.q, xs.attn, xs.act = (self.e.data_ptr(), self.q_e.data_ptr(), self.attn_e.data_ptr(),
+                                       self.mlp_e.data_ptr())  # fmt: skip
+        xs.cos_self, xs.sin_self = w["cos_s"].data_ptr(), w["sin_s"].data_ptr()
+        xs.cos_cross, xs.sin_cross = w["cos_c"].data_ptr(), w["sin_c"].data_ptr()
+        need = C.c_int64()
+        L.check(self.lib.so101_expert_step_workspace(C.byref(xs), C.byref(need)), "expert_step_workspace")
+        self.xs_ws = torch.zeros(need.value, dtype=torch.uint8, device=self.dev)
+        xs.workspace, xs.workspace_bytes = self.xs_ws.data_ptr(), need.value
+        return xs
 
     # ------------------------------------------------------------------ launch helpers
     def _gemm(self, prog: Program, what: str, x: torch.Tensor, w: torch.Tensor, y: torch.Tensor, *,
@@ -392,7 +435,9 @@ class B200Path:
               w["act.time_out.w"].data_ptr(), s.exp_dim, w["act.time_out.b"].data_ptr(), None,
               self.e.data_ptr(), s.exp_dim, M, s.exp_dim, s.exp_dim, 0)  # fmt: skip
         e = self.e
-        for i in range(s.n_layers):
+        if self.xs is not None:
+            p.add(f"s{k}.expert_layers", self.lib.so101_expert_step_run, C.byref(self.xs), keep=(self.xs,))
+        for i in range(s.n_layers if self.xs is None else 0):
             pre = f"exp.{i}."
             self._rms(p, f"s{k}.{i}.ln_in", e, w[pre + "ln_in"], self.h_e, M)
             if s.is_self_attn(i):

@@ -187,3 +187,30 @@ def test_unsupported_models_raise():
         Engine(case_bundle("tiny_absolute"), warmup=0)
     with pytest.raises(ValueError):
         Engine(case_bundle("small_absolute"), dtype="fp32", warmup=0)
+
+
+@pytest.mark.parametrize("case", ["small64_absolute", "config0"])
+def test_fused_expert_step_matches_per_op_path(case):
+    """The persistent expert-step kernel (one cooperative launch per denoising step for all expert
+    layers) against the per-op launch chain and the reference's float32 chunk. Both are within the
+    action tolerance of the reference; they differ in the RMSNorm statistics' summation order and
+    the GEMMs' K splits, so they agree to rounding. Replays of the fused path are deterministic."""
+    from so101_smolvla_edge_b200.engine import Engine
+
+    g = golden(case)
+    b = config0_bundle() if case == "config0" else case_bundle(case)
+    fused = Engine(b, warmup=1, expert_step="fused")
+    per_op = Engine(b, warmup=1, expert_step="ops")
+    assert fused.path.xs is not None and per_op.path.xs is None
+    assert fused.launches() < per_op.launches()
+    for seed in (0, 1):
+        images, state, noise = observation(b, seed)
+        a = fused.infer(images, state, noise)
+        assert np.array_equal(a, fused.infer(images, state, noise)), "fused replays differ"
+        o = per_op.infer(images, state, noise)
+        ref = g["actions"][seed] if case == "config0" else g[f"s{seed}.actions"]
+        scale = max(1.0, np.abs(ref).max())
+        assert np.abs(a - ref).max() <= ACTION_TOL * scale, (seed, np.abs(a - ref).max())
+        assert np.abs(a - o).max() <= ACTION_TOL * scale, (seed, np.abs(a - o).max())
+    del fused, per_op
+    torch.cuda.empty_cache()
