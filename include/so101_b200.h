@@ -52,7 +52,22 @@ extern "C" {
  *   v += residual[(m % r_period) * ldr + n]    (residual != NULL; r_period 0 = no period)
  *   y[row(m) * ldy + n] = cast(v)              (I8: clamp(rint(v / y_qscale), -128, 127))
  * row(m) = (m / row_group) * row_stride + m % row_group when row_group > 0, else m.
- * y may alias residual (each element is read before it is written, by the same thread). */
+ * y may alias residual (each element is read before it is written, by the same thread).
+ *
+ * RMSNorm split between two GEMMs (the reference launches rms_norm before these GEMMs,
+ * pkg/model/smolvla_triton.py:87,101,114,126): rmsnorm(x) W^T = rstd[m] (x * w) W^T, so with the
+ * operand bf16(x * w) written by the producer of the residual stream x (y16, y16_scale = w),
+ *   rms_ss != NULL: first v *= rsqrt(sum_{s < rms_slots} rms_ss[m * rms_ld + s] / rms_n + rms_eps)
+ * (rms_slots <= 64, rms_ld a multiple of 4, rms_ss 16-byte aligned) where rms_ss holds sums of
+ * squares of the residual rows written by its producer:
+ *   stat_ss != NULL: stat_ss[m * stat_ld + slot] = sum of the final v^2 over one of the disjoint
+ *   feature ranges of row m, slots [0, so101_gemm_stat_slots(...)), summed in slot order
+ *   y16 != NULL: y16[row(m) * ld16 + n] = bf16(final v * y16_scale[n]), the next GEMM's operand
+ *   (y16_scale: the next norm's weight, fp32, 16-byte aligned; NULL: 1)
+ * stat_ss / y16 need the vectorised bf16 epilogues (so101_gemm_stat_slots says whether the plan
+ * has one), no GELU, an fp32 residual if any and N a multiple of 16. Zero fields mean "off".
+ * The weights stay as they are: scaling the activations rather than the weights by w rounds once
+ * per element, as the reference's rms_norm does. */
 typedef struct so101_epilogue {
   int epilogue;
   const float* bias;
@@ -66,6 +81,16 @@ typedef struct so101_epilogue {
   float y_qscale;
   int64_t row_group;
   int64_t row_stride;
+  const float* rms_ss;
+  int rms_slots;
+  int64_t rms_ld;
+  float rms_n;
+  float rms_eps;
+  float* stat_ss;
+  int64_t stat_ld;
+  void* y16;
+  int64_t ld16;
+  const float* y16_scale;
 } so101_epilogue;
 
 /* Tile configuration; zero-initialised fields mean "pick" (the heuristic of so101_gemm_pick). */
@@ -97,6 +122,11 @@ SO101_API int so101_gemm(int a_type, const void* x, int64_t ldx, const void* w, 
                const so101_epilogue* epi, const so101_gemm_config* cfg, void* workspace,
                int64_t workspace_bytes, int* tickets, int64_t n_tickets, cudaStream_t stream);
 
+/* How many statistics slots (stat_ss) the plan of this problem writes; SO101_ERR_ARG when its
+ * epilogue cannot produce them. No counterpart in the reference, whose RMSNorm is a GEMM prologue. */
+SO101_API int so101_gemm_stat_slots(int a_type, int64_t M, int64_t N, int64_t K, int epilogue,
+                                    const so101_gemm_config* cfg, int* slots);
+
 /* The configuration so101_gemm would pick for this problem on this device (cfg out). */
 SO101_API int so101_gemm_pick(int a_type, int64_t M, int64_t N, int64_t K, int epilogue,
                     so101_gemm_config* cfg);
@@ -125,6 +155,14 @@ SO101_API int so101_attention(const void* q, int64_t ldq, const void* k, int64_t
 SO101_API int so101_rms_norm(const void* x, int64_t ldx, int x_type, const float* w, void* y,
                    int64_t ldy, int y_type, int64_t rows, int64_t n, float eps,
                    cudaStream_t stream);
+
+/* Statistics of an fp32 residual stream for an RMSNorm finished in the consuming GEMM
+ * (so101_epilogue.rms_ss): per row the sum of squares of its n values into stat_ss[row * stat_ld]
+ * (one slot) and bf16(row * w) into y16 (ld16; w: the norm weight, 16-byte aligned, NULL: 1).
+ * Replaces the reference's rms_norm launch (pkg/kernels/norm.py:14-42) where no GEMM epilogue
+ * produced the statistics (the first norm of a pass). */
+SO101_API int so101_rms_stats(const float* x, int64_t ldx, int64_t rows, int64_t n, const float* w, void* y16,
+                              int64_t ld16, float* stat_ss, int64_t stat_ld, cudaStream_t stream);
 
 /* LayerNorm (fp32 statistics, fp32 affine) of x (rows x n) fp32 into y_type (SO101_BF16 or
  * SO101_I8 with y_qscale). shuffle > 1 writes the SmolVLM pixel shuffle of each image's

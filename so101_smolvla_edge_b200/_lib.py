@@ -41,6 +41,16 @@ class Epilogue(C.Structure):
         ("y_qscale", C.c_float),
         ("row_group", C.c_int64),
         ("row_stride", C.c_int64),
+        ("rms_ss", C.c_void_p),
+        ("rms_slots", C.c_int),
+        ("rms_ld", C.c_int64),
+        ("rms_n", C.c_float),
+        ("rms_eps", C.c_float),
+        ("stat_ss", C.c_void_p),
+        ("stat_ld", C.c_int64),
+        ("y16", C.c_void_p),
+        ("ld16", C.c_int64),
+        ("y16_scale", C.c_void_p),
     ]
 
 
@@ -97,6 +107,8 @@ SIGNATURES = {
     "so101_device_status": [],
     "so101_clear_device_status": [],
     "so101_set_pdl": [I],
+    "so101_gemm_stat_slots": [I, I64, I64, I64, I, C.POINTER(GemmConfig), C.POINTER(C.c_int)],
+    "so101_rms_stats": [P, I64, I64, I64, P, P, I64, P, I64, S],
     "so101_expert_step_workspace": [C.POINTER(ExpertStep), C.POINTER(C.c_int64)],
     "so101_expert_step_run": [C.POINTER(ExpertStep), S],
 }  # fmt: skip

@@ -59,7 +59,37 @@ struct GemmArgs {
   int vec_ok;
   int cluster_reduce;
   int* status;
+  // RMSNorm folded into the GEMM: v *= rsqrt(sum of rms_slots sums of squares / rms_n + rms_eps)
+  const float* rms_ss;
+  int rms_slots;
+  long long rms_ld;
+  float rms_n, rms_eps;
+  // producer side: per-slot sums of squares of the final rows, and a bf16 copy of the output
+  float* stat_ss;
+  long long stat_ld;
+  void* y16;
+  long long ld16;
+  const float* y16_scale;  // per output column (the next norm's weight), NULL: 1
 };
+
+// Per-token RMSNorm scale from the producer's sums of squares: token m's slots are contiguous
+// (row m of rms_ss, stride rms_ld, a multiple of 4, at most 64 slots); all of them are loaded at once
+// and summed in slot order.
+__device__ __forceinline__ float rms_scale(const GemmArgs& a, long long m) {
+  const float4* row = reinterpret_cast<const float4*>(a.rms_ss + m * a.rms_ld);
+  float4 v[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = 4 * i < a.rms_slots ? row[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const float x[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      if (4 * i + j < a.rms_slots) s += x[j];
+  }
+  return rsqrtf(s / a.rms_n + a.rms_eps);
+}
 
 __device__ __forceinline__ float load_elem(const void* p, long long i, int type) {
   if (type == SO101_F32) return static_cast<const float*>(p)[i];
@@ -72,8 +102,10 @@ __device__ __forceinline__ long long out_row(const GemmArgs& a, int m) {
 
 // Epilogue of one accumulator element (m, n); u is the up-projection accumulator for SILU_GATE.
 template <bool DUAL, bool I8>
-__device__ __forceinline__ void epilogue1(const GemmArgs& a, int m, int n, float v, float u) {
+__device__ __forceinline__ void epilogue1(const GemmArgs& a, int m, int n, float v, float u, float rs = 1.f) {
   if (m >= a.M || n >= a.N) return;
+  v *= rs;
+  u *= rs;
   float x = v;
   if (I8) x *= a.x_scale * __ldg(a.w_scale + n);
   if (a.bias) x += __ldg(a.bias + n);
@@ -101,7 +133,16 @@ __device__ __forceinline__ void epilogue1(const GemmArgs& a, int m, int n, float
 
 // Epilogue of 16 accumulator values sharing P index p, Q indices [qb, qb + 16).
 template <bool SWAP, bool DUAL, bool I8>
-__device__ __forceinline__ void epilogue16(const GemmArgs& a, int p, int qb, float (&v)[16], float (&u)[16]) {
+__device__ __forceinline__ void epilogue16(const GemmArgs& a, int p, int qb, float (&v)[16], float (&u)[16],
+                                          const float* rtab = nullptr, int rbase = 0) {
+  if (rtab) {  // RMSNorm scale of each element's token (q for SWAP, p otherwise)
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const float rs = rtab[(SWAP ? qb + j : p) - rbase];
+      v[j] *= rs;
+      u[j] *= rs;
+    }
+  }
   if (!SWAP) {
     const int m = p;
     if (m >= a.M) return;
@@ -188,9 +229,9 @@ __device__ __forceinline__ void epilogue16(const GemmArgs& a, int p, int qb, flo
 // shared memory: the dequantization scale (x_scale * w_scale[n], int8 only), the bias, and the
 // up-projection scale (int8 SiLU gate).
 template <bool DUAL, bool I8>
-__device__ __forceinline__ void epilogue_row16_fast(const GemmArgs& a, int m, int qb, const uint32_t (&r0)[16],
-                                                    const uint32_t (&r1)[16], const float* kc, const float* kb,
-                                                    const float* ku) {
+__device__ __forceinline__ float epilogue_row16_fast(const GemmArgs& a, int m, int qb, const uint32_t (&r0)[16],
+                                                     const uint32_t (&r1)[16], const float* kc, const float* kb,
+                                                     const float* ku, float rs = 1.f) {
   float v[16];
 #pragma unroll
   for (int j4 = 0; j4 < 4; ++j4) {
@@ -201,23 +242,24 @@ __device__ __forceinline__ void epilogue_row16_fast(const GemmArgs& a, int m, in
       const float ss[4] = {sc.x, sc.y, sc.z, sc.w};
 #pragma unroll
       for (int e = 0; e < 4; ++e)
-        v[4 * j4 + e] = fmaf(static_cast<float>(static_cast<int>(r0[4 * j4 + e])), ss[e], bb[e]);
+        v[4 * j4 + e] = fmaf(static_cast<float>(static_cast<int>(r0[4 * j4 + e])), ss[e] * rs, bb[e]);
     } else {
 #pragma unroll
-      for (int e = 0; e < 4; ++e) v[4 * j4 + e] = __uint_as_float(r0[4 * j4 + e]) + bb[e];
+      for (int e = 0; e < 4; ++e) v[4 * j4 + e] = fmaf(__uint_as_float(r0[4 * j4 + e]), rs, bb[e]);
     }
   }
   if constexpr (DUAL) {
 #pragma unroll
     for (int j4 = 0; j4 < 4; ++j4) {
-      float su[4] = {1.f, 1.f, 1.f, 1.f};
+      float su[4] = {rs, rs, rs, rs};
       if constexpr (I8) {
         const float4 sc = *reinterpret_cast<const float4*>(ku + 4 * j4);
-        su[0] = sc.x, su[1] = sc.y, su[2] = sc.z, su[3] = sc.w;
+        su[0] = sc.x * rs, su[1] = sc.y * rs, su[2] = sc.z * rs, su[3] = sc.w * rs;
       }
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        const float up = I8 ? static_cast<float>(static_cast<int>(r1[4 * j4 + e])) * su[e] : __uint_as_float(r1[4 * j4 + e]);
+        const float up = I8 ? static_cast<float>(static_cast<int>(r1[4 * j4 + e])) * su[e]
+                            : __uint_as_float(r1[4 * j4 + e]) * su[e];
         v[4 * j4 + e] = silu(v[4 * j4 + e]) * up;
       }
     }
@@ -271,6 +313,32 @@ __device__ __forceinline__ void epilogue_row16_fast(const GemmArgs& a, int m, in
         make_uint4(pack4_i8(v[0], v[1], v[2], v[3], inv), pack4_i8(v[4], v[5], v[6], v[7], inv),
                    pack4_i8(v[8], v[9], v[10], v[11], inv), pack4_i8(v[12], v[13], v[14], v[15], inv));
   }
+  float ssq = 0.f;
+  if (a.stat_ss) {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) ssq = fmaf(v[j], v[j], ssq);
+  }
+  if (a.y16) {
+    float c[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) c[j] = 1.f;
+    if (a.y16_scale) {
+      const float4* s4 = reinterpret_cast<const float4*>(a.y16_scale + qb);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float4 s = __ldg(s4 + j);
+        c[4 * j] = s.x, c[4 * j + 1] = s.y, c[4 * j + 2] = s.z, c[4 * j + 3] = s.w;
+      }
+    }
+    uint4 o[2];
+    __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(o);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) h[e] = __floats2bfloat162_rn(v[2 * e] * c[2 * e], v[2 * e + 1] * c[2 * e + 1]);
+    uint4* y4 = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.y16) + row * a.ld16 + qb);
+    y4[0] = o[0];
+    y4[1] = o[1];
+  }
+  return ssq;
 }
 
 template <bool I8>
@@ -398,6 +466,18 @@ __global__ void __launch_bounds__(128, 1)
   const int t = threadIdx.x;
   const uint32_t lane_addr = tmem + (static_cast<uint32_t>(warp * 32) << 16);
   const int p = p0 + t;
+  // epilogue scratch past the barriers: the RMSNorm scale of this tile's tokens, and the
+  // statistics reduction of the cluster path
+  float* rtab_s = reinterpret_cast<float*>(smem + stages * STAGE_BYTES + 256);
+  float* stat_red = rtab_s + 128;  // [BN][32]
+  const int rbase = SWAP ? q0 : p0;
+  const float* rtab = nullptr;
+  if (a.rms_ss) {
+    const int count = SWAP ? BN : 128;
+    if (t < count) rtab_s[t] = rbase + t < a.M ? rms_scale(a, rbase + t) : 1.f;
+    __syncthreads();
+    rtab = rtab_s;
+  }
   float v[16], u[16];
   if (a.splits == 1) {
 #pragma unroll 1
@@ -411,7 +491,7 @@ __global__ void __launch_bounds__(128, 1)
         v[j] = acc_value<I8>(r0[j]);
         u[j] = DUAL ? acc_value<I8>(r1[j]) : 0.f;
       }
-      epilogue16<SWAP, DUAL, I8>(a, p, q0 + c, v, u);
+      epilogue16<SWAP, DUAL, I8>(a, p, q0 + c, v, u, rtab, rbase);
     }
   } else if (a.cluster_reduce) {
     // stage this split's partial (column-major, lane contiguous) in the now idle stage ring
@@ -438,6 +518,10 @@ __global__ void __launch_bounds__(128, 1)
       // two items per pass, every load (partials, bias, residual) issued before any store: the
       // output may alias the residual, so the compiler could not reorder them itself
       const int total = nq * BN;
+      if (a.stat_ss) {
+        for (int i = t; i < BN * 32; i += 128) stat_red[i] = 0.f;
+        __syncthreads();
+      }
       for (int base = 0; base < total; base += 2 * 128) {
         float4 pv[2][kMaxSplitCluster], pu[2][DUAL ? kMaxSplitCluster : 1], bia[2], res[2];
         int ok[2], col[2], quad[2];
@@ -478,6 +562,11 @@ __global__ void __launch_bounds__(128, 1)
               if constexpr (DUAL) su.x += pu[it][sp].x, su.y += pu[it][sp].y, su.z += pu[it][sp].z, su.w += pu[it][sp].w;
             }
           }
+          if (rtab) {  // the token's RMSNorm scale
+            const float rs = rtab[col[it]];
+            sv.x *= rs, sv.y *= rs, sv.z *= rs, sv.w *= rs;
+            su.x *= rs, su.y *= rs, su.z *= rs, su.w *= rs;
+          }
           const int m = q0 + col[it], n = p0 + quad[it] * 4;
           if (n + 4 > a.N || (a.res && a.r_type != SO101_F32) || a.epilogue == SO101_EPI_GELU) {
             const float vv[4] = {sv.x, sv.y, sv.z, sv.w}, uu[4] = {su.x, su.y, su.z, su.w};
@@ -505,6 +594,24 @@ __global__ void __launch_bounds__(128, 1)
             for (int e = 0; e < 4; ++e)
               static_cast<int8_t*>(a.y)[yi + e] = static_cast<int8_t>(quant_i8_int(vv[e], a.y_qscale, a.y_qinv));
           }
+          if (a.y16) {
+            const float4 c = a.y16_scale ? __ldg(reinterpret_cast<const float4*>(a.y16_scale + n))
+                                         : make_float4(1.f, 1.f, 1.f, 1.f);
+            __nv_bfloat162 h[2] = {__floats2bfloat162_rn(x.x * c.x, x.y * c.y),
+                                   __floats2bfloat162_rn(x.z * c.z, x.w * c.w)};
+            *reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(a.y16) + out_row(a, m) * a.ld16 + n) =
+                *reinterpret_cast<uint2*>(h);
+          }
+          if (a.stat_ss) stat_red[col[it] * 32 + quad[it] - qlo] = (x.x * x.x + x.y * x.y) + (x.z * x.z + x.w * x.w);
+        }
+      }
+      if (a.stat_ss) {
+        // this rank's feature quads summed per token, in quad order: slot p_tile * S + rank
+        __syncthreads();
+        if (t < BN && q0 + t < a.M) {
+          float sum = 0.f;
+          for (int qq = 0; qq < nq; ++qq) sum += stat_red[t * 32 + qq];
+          a.stat_ss[static_cast<long long>(q0 + t) * a.stat_ld + p_tile * S + rank] = sum;
         }
       }
     } else {
@@ -533,7 +640,8 @@ __global__ void __launch_bounds__(128, 1)
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const int pp = p0 + quad * 4 + e;
-          epilogue1<DUAL, I8>(a, SWAP ? qq : pp, SWAP ? pp : qq, vv[e], uu[e]);
+          epilogue1<DUAL, I8>(a, SWAP ? qq : pp, SWAP ? pp : qq, vv[e], uu[e],
+                              rtab ? rtab[(SWAP ? qq : pp) - rbase] : 1.f);
         }
       }
     }
@@ -598,7 +706,7 @@ __global__ void __launch_bounds__(128, 1)
             }
           }
         }
-        epilogue16<SWAP, DUAL, I8>(a, p, q0 + c, v, u);
+        epilogue16<SWAP, DUAL, I8>(a, p, q0 + c, v, u, rtab, rbase);
       }
       if (t == 0) a.tickets[tile] = 0;
     }
@@ -765,6 +873,8 @@ __global__ void __launch_bounds__(32 * (2 + kEpiWarps), 1)
         ku[j] = (I8 && DUAL && in) ? a.x_scale * __ldg(a.w_scale + a.N + n) : 1.f;
       }
       __syncwarp();
+      // this row's RMSNorm scale (folded norm), from the producer's sums of squares
+      const float rs = (a.rms_ss && p < a.M) ? rms_scale(a, p) : 1.f;
       if (!mbar_wait(&acc_full[buf], use & 1u, a.status)) break;
       tc_fence_after();
       const uint32_t taddr = tmem + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(buf * NACC + c_lo);
@@ -778,21 +888,24 @@ __global__ void __launch_bounds__(32 * (2 + kEpiWarps), 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[buf]);
+      float ssq = 0.f;  // this row's sum of squares over the warp's columns (statistics output)
 #pragma unroll
       for (int c = 0; c < CH; ++c) {
         const int q = q0 + c_lo + 16 * c;
         if (a.vec_ok && p < a.M && q + 16 <= a.N) {
-          epilogue_row16_fast<DUAL, I8>(a, p, q, r0[c], r1[DUAL ? c : 0], kc + 16 * c, kb + 16 * c, ku + 16 * c);
+          ssq += epilogue_row16_fast<DUAL, I8>(a, p, q, r0[c], r1[DUAL ? c : 0], kc + 16 * c, kb + 16 * c, ku + 16 * c, rs);
         } else {
           float v[16], u[16];
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
-            v[j] = acc_value<I8>(r0[c][j]);
-            u[j] = DUAL ? acc_value<I8>(r1[DUAL ? c : 0][j]) : 0.f;
+            v[j] = acc_value<I8>(r0[c][j]) * rs;
+            u[j] = DUAL ? acc_value<I8>(r1[DUAL ? c : 0][j]) * rs : 0.f;
           }
           epilogue16<false, DUAL, I8>(a, p, q, v, u);
         }
       }
+      if (a.stat_ss && p < a.M)  // slot: (column tile, column group)
+        a.stat_ss[static_cast<long long>(p) * a.stat_ld + (tile % a.tiles_q) * G + e / 4] = ssq;
     }
   }
 
@@ -849,6 +962,7 @@ int stage_bytes(int bn, bool swap, bool dual) {
 }
 
 constexpr int kSmemBudget = 220 * 1024;
+constexpr int kTileScratch = (128 + 64 * 32) * 4;  // tile kernel epilogue scratch: rstd table, statistics
 constexpr int kMaxCluster = kMaxSplitCluster;
 
 enum Kind { kTile = 0, kPersistent = 1 };
@@ -898,7 +1012,7 @@ int plan_gemm(int a_type, long long M, long long N, long long K, int epi, const 
   if (pl->kind == kTile && pl->splits > 1 && pl->splits <= kMaxCluster && !(c.flags & SO101_GEMM_GLOBAL_SPLITK))
     pl->cluster = pl->splits;
   const int sb = stage_bytes(c.bn, c.swap, dual);
-  const int max_st = (kSmemBudget - 1024 - 256 - (pl->kind == kPersistent ? kConstBytes : 0)) / sb;
+  const int max_st = (kSmemBudget - 1024 - 256 - (pl->kind == kPersistent ? kConstBytes : kTileScratch)) / sb;
   if (c.stages <= 0) {
     int want = pl->kind == kPersistent ? 8 : pl->kb_per_split;
     if (want < 2) want = 2;
@@ -953,7 +1067,7 @@ template <int BN, bool SWAP, bool DUAL, bool I8>
 int launch_tile(const CUtensorMap& tx, const CUtensorMap& tw, const GemmArgs& a, const Plan& pl, cudaStream_t stream,
                 bool pdl) {
   static int configured = 0;
-  const int smem = pl.cfg.stages * stage_bytes(BN, SWAP, DUAL) + 1024 + 256;
+  const int smem = pl.cfg.stages * stage_bytes(BN, SWAP, DUAL) + 1024 + 256 + kTileScratch;
   return launch(gemm_tc_kernel<BN, SWAP, DUAL, I8>, tx, tw, a, dim3(pl.tiles_q, pl.tiles_p, pl.splits), 128, smem,
                 pl.cluster, pl.cfg.stages, stream, pdl, &configured);
 }
@@ -1063,6 +1177,26 @@ extern "C" int so101_gemm_workspace(int a_type, int64_t M, int64_t N, int64_t K,
   return SO101_OK;
 }
 
+// Statistics slots a producer plan writes (sums of squares over disjoint feature ranges per row),
+// or 0 when the plan cannot produce them: the cluster-reduced swap tiles (one slot per weight tile
+// and split) and the persistent kernel (one per column tile and epilogue column group).
+int stat_slots_of(const Plan& pl, bool dual, int a_type, long long N) {
+  if (dual || a_type != SO101_BF16) return 0;
+  if (pl.kind == kPersistent) return N % 16 == 0 ? pl.tiles_q * (kEpiWarps / 4) : 0;
+  if (pl.cfg.swap && pl.cluster > 1 && N % 4 == 0) return pl.tiles_p * pl.splits;
+  return 0;
+}
+
+extern "C" int so101_gemm_stat_slots(int a_type, int64_t M, int64_t N, int64_t K, int epilogue,
+                                     const so101_gemm_config* cfg, int* slots) {
+  if (!slots || M <= 0 || N <= 0 || K <= 0) return SO101_ERR_ARG;
+  Plan pl;
+  const int rc = plan_gemm(a_type, M, N, K, epilogue, cfg, &pl);
+  if (rc) return rc;
+  *slots = stat_slots_of(pl, epilogue == SO101_EPI_SILU_GATE, a_type, N);
+  return *slots > 0 ? SO101_OK : SO101_ERR_ARG;
+}
+
 extern "C" int so101_gemm(int a_type, const void* x, int64_t ldx, const void* w, int64_t ldw, void* y, int64_t ldy,
                           int y_type, int64_t M, int64_t N, int64_t K, const so101_epilogue* epi,
                           const so101_gemm_config* cfg, void* workspace, int64_t workspace_bytes, int* tickets,
@@ -1119,6 +1253,28 @@ extern "C" int so101_gemm(int a_type, const void* x, int64_t ldx, const void* w,
   a.tickets = tickets;
   a.cluster_reduce = pl.cluster > 1 ? 1 : 0;
   a.status = status_ptr();
+  a.rms_ss = epi->rms_ss;
+  a.rms_slots = epi->rms_slots;
+  a.rms_ld = epi->rms_ld;
+  a.rms_n = epi->rms_n;
+  a.rms_eps = epi->rms_eps;
+  a.stat_ss = epi->stat_ss;
+  a.stat_ld = epi->stat_ld;
+  a.y16 = epi->y16;
+  a.ld16 = epi->ld16;
+  a.y16_scale = epi->y16 ? epi->y16_scale : nullptr;
+  if (a.y16_scale && reinterpret_cast<uintptr_t>(a.y16_scale) % 16) return SO101_ERR_ARG;
+  if (a.rms_ss && (a.rms_slots < 1 || a.rms_slots > 64 || a.rms_ld < a.rms_slots || a.rms_ld % 4 ||
+                   reinterpret_cast<uintptr_t>(a.rms_ss) % 16 || !(a.rms_n > 0.f)))
+    return SO101_ERR_ARG;
+  if (a.stat_ss || a.y16) {
+    // statistics and the bf16 copy come from the vectorised epilogues only
+    if (a.stat_ss && (stat_slots_of(pl, dual, a_type, N) == 0 || a.stat_ld < stat_slots_of(pl, dual, a_type, N)))
+      return SO101_ERR_ARG;
+    if (a.y16 && (reinterpret_cast<uintptr_t>(a.y16) % 16 || a.ld16 % 8 || a.ld16 < N || N % 16)) return SO101_ERR_ARG;
+    if (epi->epilogue == SO101_EPI_GELU || (a.res && a.r_type != SO101_F32)) return SO101_ERR_ARG;
+    if (!pl.cfg.swap && pl.kind != kPersistent) return SO101_ERR_ARG;
+  }
   const int ysz = y_type == SO101_F32 ? 4 : y_type == SO101_BF16 ? 2 : 1;
   bool vec = reinterpret_cast<uintptr_t>(y) % 16 == 0 && (ldy * ysz) % 16 == 0;
   if (a.row_group > 0) vec = vec && (a.row_stride * ldy * ysz) % 16 == 0;
@@ -1127,6 +1283,7 @@ extern "C" int so101_gemm(int a_type, const void* x, int64_t ldx, const void* w,
     vec = vec && reinterpret_cast<uintptr_t>(a.res) % 16 == 0 && (a.ldr * rsz) % 16 == 0;
   }
   a.vec_ok = vec ? 1 : 0;
+  if ((a.stat_ss || a.y16) && !vec) return SO101_ERR_ARG;
 
   const bool i8 = a_type == SO101_I8;
   const long long w_rows = dual ? 2 * N : N;

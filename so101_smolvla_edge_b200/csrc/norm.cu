@@ -192,6 +192,28 @@ __global__ void rms_norm_vec_kernel(const float* __restrict__ x, long long ldx, 
   }
 }
 
+// Statistics for an RMSNorm applied in the consuming GEMM: per row, the sum of squares (slot 0 of
+// stat_ss, row stride stat_ld) and the bf16 row times the norm weight w (NULL: 1). One warp per row.
+__global__ void rms_stats_kernel(const float* __restrict__ x, long long ldx, long long rows, int n,
+                                 const float* __restrict__ w, __nv_bfloat16* __restrict__ y16, long long ld16,
+                                 float* __restrict__ stat, long long stat_ld) {
+  grid_dep_launch();
+  grid_dep_wait();
+  const long long row = static_cast<long long>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  float ss = 0.f;
+  for (int c = 4 * lane; c < n; c += 128) {
+    const float4 v = *reinterpret_cast<const float4*>(x + row * ldx + c);
+    ss += (v.x * v.x + v.y * v.y) + (v.z * v.z + v.w * v.w);
+    const float4 sc = w ? __ldg(reinterpret_cast<const float4*>(w + c)) : make_float4(1.f, 1.f, 1.f, 1.f);
+    __nv_bfloat162 h[2] = {__floats2bfloat162_rn(v.x * sc.x, v.y * sc.y), __floats2bfloat162_rn(v.z * sc.z, v.w * sc.w)};
+    *reinterpret_cast<uint2*>(y16 + row * ld16 + c) = *reinterpret_cast<uint2*>(h);
+  }
+  ss = warp_sum(ss);
+  if (lane == 0) stat[row * stat_ld] = ss;
+}
+
 // ------------------------------------------------------------------ RoPE + K/V cache write
 // grid (rows, batch); thread j < nkv * hd/2 rotates pair (d, d + hd/2) of kv head j / (hd/2) and
 // copies the two value columns at the same positions. The rotation is rounded per operation
@@ -311,6 +333,20 @@ extern "C" int so101_rms_norm(const void* x, int64_t ldx, int x_type, const floa
   }
   return launch_kernel(rms_norm_kernel, dim3(static_cast<unsigned>(blocks)), dim3(32 * rows_per_block), 0, stream,
                        x, ldx, x_type, w, y, ldy, y_type, rows, static_cast<int>(n), eps);
+}
+
+extern "C" int so101_rms_stats(const float* x, int64_t ldx, int64_t rows, int64_t n, const float* w, void* y16,
+                               int64_t ld16, float* stat_ss, int64_t stat_ld, cudaStream_t stream) {
+  if (!x || !y16 || !stat_ss || rows <= 0 || n <= 0 || n % 4 || n > (1 << 20)) return SO101_ERR_ARG;
+  if (reinterpret_cast<uintptr_t>(x) % 16 || ldx % 4 || reinterpret_cast<uintptr_t>(y16) % 8 || ld16 % 4 ||
+      reinterpret_cast<uintptr_t>(w) % 16 || stat_ld < 1 || ldx < n || ld16 < n)
+    return SO101_ERR_ARG;
+  const int rows_per_block = 4;
+  const long long blocks = (rows + rows_per_block - 1) / rows_per_block;
+  if (blocks > 0x7fffffffLL) return SO101_ERR_ARG;
+  return launch_kernel(rms_stats_kernel, dim3(static_cast<unsigned>(blocks)), dim3(32 * rows_per_block), 0, stream,
+                       x, ldx, rows, static_cast<int>(n), w, static_cast<__nv_bfloat16*>(y16), ld16, stat_ss,
+                       stat_ld);
 }
 
 extern "C" int so101_layer_norm(const float* x, int64_t ldx, const float* w, const float* b, void* y,

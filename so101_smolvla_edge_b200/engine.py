@@ -88,6 +88,7 @@ class Engine:
         act_clip: dict[str, float] | str | Path | None = None,
         pdl: bool | None = None,
         expert_step: str | None = None,
+        fold_norms: bool = True,
     ):
         self.device = dev = torch.device(device)
         if dev.type == "cuda" and dev.index is None:
@@ -126,7 +127,7 @@ class Engine:
         torch.cuda.set_device(dev)
         if expert_step is None:  # "fused": the persistent expert-step kernel; default the per-op chain
             expert_step = os.environ.get("SO101_EXPERT_STEP", "auto")
-        self.path = B200Path(b, dev, self.batch, trt_precision, clip, expert_step)
+        self.path = B200Path(b, dev, self.batch, trt_precision, clip, expert_step, fold_norms)
         self.tp = self.path  # the reference's attribute for the custom-kernel path
         p = self.path
         self.img, self.state, self.noise, self.out = p.img, p.state, p.noise, p.out

@@ -86,6 +86,8 @@ def linear(
     x_scale: float | None = None,
     w_scale: torch.Tensor | None = None,
     y_qscale: float | None = None,
+    rms: tuple[torch.Tensor, int, float] | None = None,
+    stat: tuple[torch.Tensor, torch.Tensor] | None = None,
 ) -> torch.Tensor:
     """Compute x (..., K) @ w (N, K).T with a fused epilogue on tcgen05.
 
@@ -94,6 +96,12 @@ def linear(
     be the residual itself. A float32 x is rounded to bf16 first, as `SmolVLA.lin` casts it.
     int8 operands: x and w int8 with `x_scale` (per tensor) and `w_scale` (N,) dequantizing the
     int32 accumulator. out_dtype int8 quantizes the result by `y_qscale`.
+
+    RMSNorm finished in the GEMM (not in the reference, which launches rms_norm before the GEMM):
+    rms=(ss, slots, eps) with x = bf16(residual stream * norm weight) scales row m by
+    rsqrt(sum(ss[m, :slots]) / K + eps). stat=(ss, x16[, norm_w]) makes this (residual) GEMM write
+    its rows' sums of squares into ss (`gemm_stat_slots` tells how many slots) and bf16(output *
+    norm_w) into x16, the next such GEMM's x.
     """
     _cuda(x, w, bias, residual, out)
     if silu_gate and (residual is not None or bias is not None or gelu):
@@ -130,6 +138,13 @@ def linear(
         out_scale=out_scale, w_scale=_ptr(w_scale), x_scale=x_scale or 0.0,
         y_qscale=y_qscale or 0.0, row_group=0, row_stride=0,
     )  # fmt: skip
+    if rms is not None:
+        ss, slots, eps = rms
+        epi.rms_ss, epi.rms_slots, epi.rms_ld, epi.rms_n, epi.rms_eps = ss.data_ptr(), slots, ss.stride(0), float(k), eps
+    if stat is not None:
+        ss, x16, nw = stat if len(stat) == 3 else (*stat, None)
+        epi.stat_ss, epi.stat_ld, epi.y16, epi.ld16 = ss.data_ptr(), ss.stride(0), x16.data_ptr(), x16.stride(0)
+        epi.y16_scale = _ptr(nw)
     cfg = None
     if config is not None:
         cfg = L.GemmConfig(*config)
@@ -142,6 +157,24 @@ def linear(
     )  # fmt: skip
     L.check(rc, "so101_gemm")
     return y.view(*x.shape[:-1], n)
+
+
+def gemm_stat_slots(m: int, n: int, k: int, config=None) -> int:
+    """Statistics slots a bf16 GEMM of this shape writes with `stat` (ValueError if none)."""
+    got = C.c_int()
+    cfg = L.GemmConfig(*config) if config is not None else None
+    L.check(L.lib().so101_gemm_stat_slots(L.BF16, m, n, k, L.EPI_NONE, C.byref(cfg) if cfg else None,
+                                          C.byref(got)), "gemm_stat_slots")  # fmt: skip
+    return got.value
+
+
+def rms_stats(x: torch.Tensor, x16: torch.Tensor, ss: torch.Tensor, w: torch.Tensor | None = None) -> None:
+    """Slot 0 of ss = per-row sums of squares of the fp32 rows x; x16 = bf16(x * w) (w: the norm
+    weight, fp32, None: 1)."""
+    _cuda(x, x16, ss)
+    L.check(L.lib().so101_rms_stats(x.data_ptr(), x.stride(0), x.shape[0], x.shape[1], _ptr(w), x16.data_ptr(),
+                                    x16.stride(0), ss.data_ptr(), ss.stride(0), _stream(x.device)),
+            "rms_stats")  # fmt: skip
 
 
 def attention(

@@ -34,6 +34,7 @@ from .ops import DTYPE, workspace
 from .spec import ModelSpec, vision_linear_names
 
 REPRS = {"absolute": 0, "delta": 1, "velocity": 2}
+STAT_SLOTS = 64  # statistics slots per row for the RMSNorm finished in a GEMM (so101_epilogue.rms_ss)
 
 
 def unsupported(spec: ModelSpec) -> str | None:
@@ -108,7 +109,7 @@ class B200Path:
 
     def __init__(self, bundle: Bundle, device: torch.device, batch: int = 1,
                  vision_precision: str = "bf16", act_clip: dict[str, float] | None = None,
-                 expert_step: str = "auto"):  # fmt: skip
+                 expert_step: str = "auto", fold_norms: bool = True):  # fmt: skip
         s = self.spec = bundle.spec
         why = unsupported(s)
         if why:
@@ -133,6 +134,7 @@ class B200Path:
         self.repr = REPRS[bundle.meta["action_repr"]]
         if expert_step not in ("auto", "fused", "ops"):
             raise ValueError(f"expert_step must be 'auto', 'fused' or 'ops', not {expert_step!r}")
+        self.fold = bool(fold_norms)  # RMSNorm split into the GEMMs around it (else an rms_norm launch each)
         self.ws = workspace(device)  # split-K partials and tickets exist before any capture
         self._amax: tuple[torch.Tensor, dict[str, int]] | None = None  # calibration hooks
         self._upload(bundle)
@@ -223,6 +225,7 @@ class B200Path:
         self.kx = [None if s.is_self_attn(i) else z(B, L_, kv, dtype=bf) for i in layers]
         self.vx = [None if s.is_self_attn(i) else z(B, L_, kv, dtype=bf) for i in layers]
         self.k_scratch = z(B * L_, kv, dtype=bf)
+        self.ss_t = z(B * L_, STAT_SLOTS)  # per-row sums of squares of the prefix residual stream
         # expert
         self.h0 = z(B * H, s.exp_dim)
         self.e = z(B * H, s.exp_dim)
@@ -231,6 +234,7 @@ class B200Path:
         self.attn_e = z(B * H, s.q_dim, dtype=bf)
         self.mlp_e = z(B * H, s.exp_mlp, dtype=bf)
         self.v_buf = z(B * H, s.max_action)
+        self.ss_e = z(B * H, STAT_SLOTS)  # per-row sums of squares of the expert residual stream
 
     def _expert_step(self, mode: str) -> L.ExpertStep | None:
         """The persistent expert-step problem for one observation, or None (per-op launches).
@@ -274,7 +278,12 @@ class B200Path:
     # ------------------------------------------------------------------ launch helpers
     def _gemm(self, prog: Program, what: str, x: torch.Tensor, w: torch.Tensor, y: torch.Tensor, *,
               bias=None, residual=None, r_period=0, gate=False, gelu=False, out_scale=1.0,
-              row_map=(0, 0), x_scale=0.0, w_scale=None, y_qscale=0.0, M=None) -> None:  # fmt: skip
+              row_map=(0, 0), x_scale=0.0, w_scale=None, y_qscale=0.0, M=None, rms=None,
+              stat=None) -> int:  # fmt: skip
+        """One GEMM launch. rms=(ss, slots): finish the RMSNorm of x in the GEMM (x = bf16(residual
+        stream * norm weight), row m scaled by its rstd from ss). stat=(ss, x16, norm_w): also
+        write the output rows' statistics and bf16(output * norm_w) for the next norm; returns the
+        slot count (a separate statistics launch when the GEMM's plan cannot produce them)."""
         m = x.shape[0] if M is None else M
         k = x.shape[1]
         n = w.shape[0] // 2 if gate else w.shape[0]
@@ -288,6 +297,19 @@ class B200Path:
             out_scale=out_scale, w_scale=None if w_scale is None else w_scale.data_ptr(),
             x_scale=x_scale, y_qscale=y_qscale, row_group=row_map[0], row_stride=row_map[1],
         )  # fmt: skip
+        if rms is not None:
+            ss, slots = rms
+            epi.rms_ss, epi.rms_slots, epi.rms_ld = ss.data_ptr(), slots, ss.stride(0)
+            epi.rms_n, epi.rms_eps = float(k), self.spec.rms_eps
+        slots_out = 0
+        if stat is not None:
+            ss, x16, nw = stat
+            got = C.c_int()
+            if self.lib.so101_gemm_stat_slots(a_type, m, n, k, epi.epilogue, None, C.byref(got)) == L.OK \
+                    and got.value <= ss.shape[1]:  # fmt: skip
+                slots_out = got.value
+                epi.stat_ss, epi.stat_ld = ss.data_ptr(), ss.stride(0)
+                epi.y16, epi.ld16, epi.y16_scale = x16.data_ptr(), x16.stride(0), nw.data_ptr()
         need, tick = C.c_int64(), C.c_int64()
         L.check(self.lib.so101_gemm_workspace(a_type, m, n, k, epi.epilogue, None, C.byref(need),
                                               C.byref(tick)), what)  # fmt: skip
@@ -297,6 +319,15 @@ class B200Path:
                  w.stride(0), y.data_ptr(), y.stride(0), DTYPE[y.dtype], m, n, k, C.byref(epi),
                  None, self.ws.partials.data_ptr(), self.ws.nbytes, self.ws.tickets.data_ptr(),
                  self.ws.tickets.numel(), keep=(epi,))  # fmt: skip
+        if stat is not None and slots_out == 0:
+            slots_out = self._stats(prog, f"{what}.stats", y, stat[2], stat[1], stat[0])
+        return slots_out
+
+    def _stats(self, prog, what, x, nw, x16, ss) -> int:
+        """Statistics (one slot) and bf16(x * nw) of the fp32 rows x, for the next norm's GEMM."""
+        prog.add(what, self.lib.so101_rms_stats, x.data_ptr(), x.stride(0), x.shape[0], x.shape[1],
+                 nw.data_ptr(), x16.data_ptr(), x16.stride(0), ss.data_ptr(), ss.stride(0))  # fmt: skip
+        return 1
 
     def _attn(self, prog, what, q, ldq, bq, k, ldk, bk, v, ldv, bv, o, ldo, bo, *, Lq, Lk, nq, nkv,
               hd, causal_from, q_offset=0, cos=None, sin=None, batch=1, o_qscale=0.0):  # fmt: skip
@@ -387,10 +418,15 @@ class B200Path:
               self.prefix.data_ptr(), s.text_dim, L_, tail, B)  # fmt: skip
         x = self.prefix
         esz = 2  # bf16 bytes
+        # RMSNorm in two halves: the residual GEMM before it writes bf16(x * w) and per-row sums of
+        # squares, the GEMM after it scales its rows by rstd (fold); else an rms_norm launch
+        fold = self.fold
+        slots = self._stats(p, "prefix.stats", x, w["txt.0.ln_in"], self.h_t, self.ss_t) if fold else 0
         for i in range(s.n_layers):
             t = f"txt.{i}."
-            self._rms(p, f"{i}.ln_in", x, w[t + "ln_in"], self.h_t, B * L_)
-            self._gemm(p, f"{i}.qkv", self.h_t, w[t + "qkv"], self.qkv_t)
+            if not fold:
+                self._rms(p, f"{i}.ln_in", x, w[t + "ln_in"], self.h_t, B * L_)
+            self._gemm(p, f"{i}.qkv", self.h_t, w[t + "qkv"], self.qkv_t, rms=(self.ss_t, slots) if fold else None)
             qkv_ptr = self.qkv_t.data_ptr()
             if s.is_self_attn(i):
                 k_ptr, v_ptr = self.ck[i].data_ptr(), self.cv[i].data_ptr()
@@ -415,10 +451,16 @@ class B200Path:
             self._attn(p, f"{i}.attn", qkv_ptr, qd, L_ * qd, k_ptr, ldk, bk, v_ptr, ldv, bv, self.attn_t,
                        s.q_dim, L_ * s.q_dim, Lq=L_, Lk=L_, nq=nq, nkv=nk, hd=hd, causal_from=L_ - 1,
                        cos=w["cos_p"], sin=w["sin_p"], batch=B)  # fmt: skip
-            self._gemm(p, f"{i}.o", self.attn_t, w[t + "o"], x, residual=x)
-            self._rms(p, f"{i}.ln_post", x, w[t + "ln_post"], self.h_t, B * L_)
-            self._gemm(p, f"{i}.gate_up", self.h_t, w[t + "gate_up"], self.mlp_t, gate=True)
-            self._gemm(p, f"{i}.down", self.mlp_t, w[t + "down"], x, residual=x)
+            if fold:
+                slots = self._gemm(p, f"{i}.o", self.attn_t, w[t + "o"], x, residual=x,
+                                   stat=(self.ss_t, self.h_t, w[t + "ln_post"]))  # fmt: skip
+            else:
+                self._gemm(p, f"{i}.o", self.attn_t, w[t + "o"], x, residual=x)
+                self._rms(p, f"{i}.ln_post", x, w[t + "ln_post"], self.h_t, B * L_)
+            self._gemm(p, f"{i}.gate_up", self.h_t, w[t + "gate_up"], self.mlp_t, gate=True,
+                       rms=(self.ss_t, slots) if fold else None)  # fmt: skip
+            nxt = (self.ss_t, self.h_t, w[f"txt.{i + 1}.ln_in"]) if fold else None
+            slots = self._gemm(p, f"{i}.down", self.mlp_t, w[t + "down"], x, residual=x, stat=nxt)
 
     # ------------------------------------------------------------------ denoising
     def _build_step(self, p: Program, k: int, x_in: torch.Tensor, x_out: torch.Tensor, dt: float) -> None:
@@ -437,11 +479,15 @@ class B200Path:
         e = self.e
         if self.xs is not None:
             p.add(f"s{k}.expert_layers", self.lib.so101_expert_step_run, C.byref(self.xs), keep=(self.xs,))
+        fold = self.fold and self.xs is None
+        slots = self._stats(p, f"s{k}.stats", e, w["exp.0.ln_in"], self.h_e, self.ss_e) if fold else 0
         for i in range(s.n_layers if self.xs is None else 0):
             pre = f"exp.{i}."
-            self._rms(p, f"s{k}.{i}.ln_in", e, w[pre + "ln_in"], self.h_e, M)
+            if not fold:
+                self._rms(p, f"s{k}.{i}.ln_in", e, w[pre + "ln_in"], self.h_e, M)
+            rms = (self.ss_e, slots) if fold else None
             if s.is_self_attn(i):
-                self._gemm(p, f"s{k}.{i}.qkv", self.h_e, w[pre + "qkv"], self.qkv_e)
+                self._gemm(p, f"s{k}.{i}.qkv", self.h_e, w[pre + "qkv"], self.qkv_e, rms=rms)
                 bk = (L_ + H) * kv
                 own = L_ * kv * 2  # bytes to the step's own rows
                 p.add(f"s{k}.{i}.rope_kv", self.lib.so101_rope_kv, self.qkv_e.data_ptr(), qd, nq, nk, hd,
@@ -453,15 +499,22 @@ class B200Path:
                            cos=w["cos_s"], sin=w["sin_s"], batch=B)  # fmt: skip
             else:
                 qv = self.qkv_e[:, : s.q_dim]
-                self._gemm(p, f"s{k}.{i}.q", self.h_e, w[pre + "q"], qv)
+                self._gemm(p, f"s{k}.{i}.q", self.h_e, w[pre + "q"], qv, rms=rms)
                 self._attn(p, f"s{k}.{i}.attn", self.qkv_e.data_ptr(), qd, H * qd, self.kx[i].data_ptr(),
                            kv, L_ * kv, self.vx[i].data_ptr(), kv, L_ * kv, self.attn_e, s.q_dim,
                            H * s.q_dim, Lq=H, Lk=L_, nq=nq, nkv=nk, hd=hd, causal_from=L_,
                            cos=w["cos_c"], sin=w["sin_c"], batch=B)  # fmt: skip
-            self._gemm(p, f"s{k}.{i}.o", self.attn_e, w[pre + "o"], e, residual=e)
-            self._rms(p, f"s{k}.{i}.ln_post", e, w[pre + "ln_post"], self.h_e, M)
-            self._gemm(p, f"s{k}.{i}.gate_up", self.h_e, w[pre + "gate_up"], self.mlp_e, gate=True)
-            self._gemm(p, f"s{k}.{i}.down", self.mlp_e, w[pre + "down"], e, residual=e)
+            if fold:
+                slots = self._gemm(p, f"s{k}.{i}.o", self.attn_e, w[pre + "o"], e, residual=e,
+                                   stat=(self.ss_e, self.h_e, w[pre + "ln_post"]))  # fmt: skip
+            else:
+                self._gemm(p, f"s{k}.{i}.o", self.attn_e, w[pre + "o"], e, residual=e)
+                self._rms(p, f"s{k}.{i}.ln_post", e, w[pre + "ln_post"], self.h_e, M)
+            self._gemm(p, f"s{k}.{i}.gate_up", self.h_e, w[pre + "gate_up"], self.mlp_e, gate=True,
+                       rms=(self.ss_e, slots) if fold else None)  # fmt: skip
+            # the last layer's output goes to the final norm of so101_expert_out (fp32, from e)
+            nxt = (self.ss_e, self.h_e, w[f"exp.{i + 1}.ln_in"]) if fold and i + 1 < s.n_layers else None
+            slots = self._gemm(p, f"s{k}.{i}.down", self.mlp_e, w[pre + "down"], e, residual=e, stat=nxt)
         p.add(f"s{k}.out+euler", self.lib.so101_expert_out, e.data_ptr(), s.exp_dim, w["exp.norm"].data_ptr(),
               s.rms_eps, w["act.out.w"].data_ptr(), w["act.out.b"].data_ptr(), x_out.data_ptr(),
               s.max_action, M, s.max_action, s.exp_dim, dt)  # fmt: skip

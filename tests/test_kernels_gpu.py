@@ -354,3 +354,83 @@ def test_layer_norm_and_pixel_shuffle():
     shuf = layer_norm(x, w, b, 1e-6, shuffle=4, tokens_per_image=1024)
     v = ln.reshape(2, 8, 4, 8, 4, 768).permute(0, 1, 3, 2, 4, 5).reshape(2 * 64, 768 * 16)
     assert (shuf.float() - v).abs().max() <= 2**-7 * v.abs().max()
+
+
+# ------------------------------------------------------------------ RMSNorm finished in the GEMM
+def _rms_ref(x, w, eps):
+    x = x.float()
+    return x * torch.rsqrt((x * x).mean(-1, keepdim=True) + eps) * w.float()
+
+
+def test_rms_stats_matches_torch():
+    from so101_smolvla_edge_b200.ops import rms_stats
+
+    x = rnd(137, 720)
+    nw = 1.0 + 0.1 * rnd(720, seed=3)
+    x16 = torch.empty(137, 720, device="cuda", dtype=torch.bfloat16)
+    ss = torch.zeros(137, 64, device="cuda")
+    rms_stats(x, x16, ss)
+    assert torch.equal(x16, x.bfloat16())
+    want = (x.double() ** 2).sum(1)
+    assert torch.allclose(ss[:, 0].double(), want, rtol=1e-5)
+    rms_stats(x, x16, ss, nw)
+    assert torch.equal(x16, (x * nw).bfloat16())
+    assert torch.allclose(ss[:, 0].double(), want, rtol=1e-5)
+
+
+@pytest.mark.parametrize("m,n,k,gate", [(50, 1600, 720, False), (50, 2048, 720, True), (241, 1600, 960, False),
+                                        (241, 2560, 960, True), (3200, 1600, 720, False), (3200, 2048, 720, True),
+                                        (10, 448, 128, False), (10, 160, 128, True), (16, 448, 320, False),
+                                        (16, 256, 320, True)])  # fmt: skip
+def test_rmsnorm_in_gemm(m, n, k, gate):
+    """rstd * (bf16(x * w) @ W^T) against float32 rmsnorm(x) * w @ W^T and against the two-launch
+    chain (rms_norm, then the GEMM): the swap tiles with and without a cluster split, the 64-wide
+    normal tiles and the persistent kernel all apply the scale; one bf16 rounding of x * w, as the
+    rms_norm launch rounds its output once."""
+    from so101_smolvla_edge_b200.ops import linear, rms_norm, rms_stats
+
+    eps = 1e-5
+    x = rnd(m, k, scale=2.0)
+    nw = 1.0 + 0.1 * rnd(k, seed=3)
+    w = rnd(2 * n if gate else n, k, dtype=torch.bfloat16, scale=k**-0.5, seed=1)
+    x16 = torch.empty(m, k, device="cuda", dtype=torch.bfloat16)
+    ss = torch.zeros(m, 64, device="cuda")
+    rms_stats(x, x16, ss, nw)
+    got = linear(x16, w, silu_gate=gate, rms=(ss, 1, eps))
+    want = gemm_ref(_rms_ref(x, nw, eps), w, silu_gate=gate)
+    chain = linear(rms_norm(x, nw, eps), w, silu_gate=gate)
+    scale = want.abs().max().item()
+    err = (got.float() - want).abs().max().item()
+    err_chain = (chain.float() - want).abs().max().item()
+    assert err <= 1e-2 * scale, err
+    assert err <= 2 * err_chain + 1e-3 * scale, (err, err_chain)
+
+
+@pytest.mark.parametrize("m,n,k", [(50, 720, 960), (50, 720, 2048), (241, 960, 2560), (3200, 720, 960)])
+def test_residual_gemm_statistics(m, n, k):
+    """A residual GEMM's statistics (sums of squares over disjoint column ranges) and bf16(output
+    * next norm weight) feed the next norm's GEMM: the slots sum to the rows' sums of squares,
+    bit-stable."""
+    from so101_smolvla_edge_b200.ops import gemm_stat_slots, linear
+
+    x = rnd(m, k, dtype=torch.bfloat16)
+    w = rnd(n, k, dtype=torch.bfloat16, scale=k**-0.5, seed=1)
+    e = rnd(m, n, seed=2)
+    nw = 1.0 + 0.1 * rnd(n, seed=3)
+    slots = gemm_stat_slots(m, n, k)
+    assert 1 <= slots <= 64
+    outs = []
+    for _ in range(2):
+        r = e.clone()
+        ss = torch.zeros(m, 64, device="cuda")
+        x16 = torch.zeros(m, n, device="cuda", dtype=torch.bfloat16)
+        linear(x, w, residual=r, out=r, stat=(ss, x16, nw))
+        outs.append((r, ss, x16))
+    r, ss, x16 = outs[0]
+    assert torch.equal(r, outs[1][0]) and torch.equal(ss, outs[1][1])
+    ok, err = close(r, gemm_ref(x, w, residual=e), torch.float32)
+    assert ok, err
+    assert torch.equal(x16, (r * nw).bfloat16())
+    want = (r.double() ** 2).sum(1)
+    assert torch.allclose(ss[:, :slots].double().sum(1), want, rtol=1e-4)
+    assert torch.count_nonzero(ss[:, slots:]) == 0
