@@ -108,6 +108,8 @@ typedef struct so101_gemm_config {
 #define SO101_GEMM_GLOBAL_SPLITK 1     /* reduce split-K partials through the workspace       */
 #define SO101_GEMM_PERSISTENT 2        /* tokens on M, no split: always the persistent kernel */
 #define SO101_GEMM_ONE_TILE_PER_CTA 4  /* tokens on M: never the persistent kernel            */
+#define SO101_GEMM_PAIR 8              /* tokens on M, no split, bn 128/256: CTA-pair tiles    */
+                                       /* (256 x bn per two SMs, cta_group::2 MMAs)           */
 
 /* y (M x N) = epilogue(x (M x K) @ w (N x K)^T) on tcgen05 tensor cores, TMA-fed.
  * Replaces kernels/gemm.py:48-96 (so101_gemm) and :350-398 (linear), the cuBLAS F.linear calls of

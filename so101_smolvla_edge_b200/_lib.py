@@ -54,7 +54,7 @@ class Epilogue(C.Structure):
     ]
 
 
-GEMM_GLOBAL_SPLITK, GEMM_PERSISTENT, GEMM_ONE_TILE_PER_CTA = 1, 2, 4
+GEMM_GLOBAL_SPLITK, GEMM_PERSISTENT, GEMM_ONE_TILE_PER_CTA, GEMM_PAIR = 1, 2, 4, 8
 
 
 class GemmConfig(C.Structure):

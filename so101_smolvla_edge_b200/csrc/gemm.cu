@@ -228,11 +228,13 @@ __device__ __forceinline__ void epilogue16(const GemmArgs& a, int p, int qb, flo
 // fully inside N with vector-aligned rows. kc / kb / ku hold this chunk's per-column constants in
 // shared memory: the dequantization scale (x_scale * w_scale[n], int8 only), the bias, and the
 // up-projection scale (int8 SiLU gate).
+// Values of 16 consecutive output columns of one row before the residual: dequantization scale,
+// bias, RMSNorm row scale, SiLU gate or GELU, out_scale. Shared by the row-per-lane stores below and
+// the transposed stores of the CTA-pair kernel, so both round identically.
 template <bool DUAL, bool I8>
-__device__ __forceinline__ float epilogue_row16_fast(const GemmArgs& a, int m, int qb, const uint32_t (&r0)[16],
-                                                     const uint32_t (&r1)[16], const float* kc, const float* kb,
-                                                     const float* ku, float rs = 1.f) {
-  float v[16];
+__device__ __forceinline__ void epilogue_values16(const GemmArgs& a, const uint32_t (&r0)[16], const uint32_t (&r1)[16],
+                                                  const float* kc, const float* kb, const float* ku, float rs,
+                                                  float (&v)[16]) {
 #pragma unroll
   for (int j4 = 0; j4 < 4; ++j4) {
     const float4 bi = *reinterpret_cast<const float4*>(kb + 4 * j4);
@@ -271,6 +273,14 @@ __device__ __forceinline__ float epilogue_row16_fast(const GemmArgs& a, int m, i
 #pragma unroll
     for (int j = 0; j < 16; ++j) v[j] *= a.out_scale;
   }
+}
+
+template <bool DUAL, bool I8>
+__device__ __forceinline__ float epilogue_row16_fast(const GemmArgs& a, int m, int qb, const uint32_t (&r0)[16],
+                                                     const uint32_t (&r1)[16], const float* kc, const float* kb,
+                                                     const float* ku, float rs = 1.f) {
+  float v[16];
+  epilogue_values16<DUAL, I8>(a, r0, r1, kc, kb, ku, rs, v);
   const long long row = out_row(a, m);
   if (a.res) {
     const long long rrow = a.r_period > 0 ? m % a.r_period : row;
@@ -341,6 +351,38 @@ __device__ __forceinline__ float epilogue_row16_fast(const GemmArgs& a, int m, i
   return ssq;
 }
 
+// Residual, output, bf16 copy and sum of squares of 4 consecutive columns [n, n + 4) of row m
+// (vector path: n + 4 <= N, aligned rows), from values as epilogue_values16 leaves them.
+__device__ __forceinline__ float epilogue_store4(const GemmArgs& a, int m, int n, float4 x) {
+  const long long row = out_row(a, m);
+  if (a.res) {
+    const long long rrow = a.r_period > 0 ? m % a.r_period : row;
+    if (a.r_type == SO101_F32) {
+      const float4 r = *reinterpret_cast<const float4*>(static_cast<const float*>(a.res) + rrow * a.ldr + n);
+      x.x += r.x, x.y += r.y, x.z += r.z, x.w += r.w;
+    } else {
+      const uint2 r = *reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(a.res) + rrow * a.ldr + n);
+      const float2 f0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&r.x));
+      const float2 f1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&r.y));
+      x.x += f0.x, x.y += f0.y, x.z += f1.x, x.w += f1.y;
+    }
+  }
+  if (a.y_type == SO101_F32) {
+    *reinterpret_cast<float4*>(static_cast<float*>(a.y) + row * a.ldy + n) = x;
+  } else if (a.y_type == SO101_BF16) {
+    __nv_bfloat162 h[2] = {__floats2bfloat162_rn(x.x, x.y), __floats2bfloat162_rn(x.z, x.w)};
+    *reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(a.y) + row * a.ldy + n) = *reinterpret_cast<uint2*>(h);
+  } else {
+    *reinterpret_cast<uint32_t*>(static_cast<int8_t*>(a.y) + row * a.ldy + n) = pack4_i8(x.x, x.y, x.z, x.w, a.y_qinv);
+  }
+  if (a.y16) {
+    const float4 c = a.y16_scale ? __ldg(reinterpret_cast<const float4*>(a.y16_scale + n)) : make_float4(1.f, 1.f, 1.f, 1.f);
+    __nv_bfloat162 h[2] = {__floats2bfloat162_rn(x.x * c.x, x.y * c.y), __floats2bfloat162_rn(x.z * c.z, x.w * c.w)};
+    *reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(a.y16) + row * a.ld16 + n) = *reinterpret_cast<uint2*>(h);
+  }
+  return (x.x * x.x + x.y * x.y) + (x.z * x.z + x.w * x.w);
+}
+
 template <bool I8>
 __device__ __forceinline__ float acc_value(uint32_t r) {
   return I8 ? i32_to_f32(static_cast<int>(r)) : __uint_as_float(r);
@@ -368,10 +410,15 @@ __global__ void __launch_bounds__(128, 1)
   uint64_t* accum = empty + stages;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
   int* last_flag = reinterpret_cast<int*>(tmem_slot + 1);
+  // epilogue scratch past the barriers: the RMSNorm scale of this tile's tokens, and the
+  // statistics reduction of the cluster path
+  float* rtab_s = reinterpret_cast<float*>(smem + stages * STAGE_BYTES + 256);
+  float* stat_red = rtab_s + 128;  // [BN][32]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int q_tile = blockIdx.x, p_tile = blockIdx.y, split = blockIdx.z;
   const int p0 = p_tile * 128, q0 = q_tile * BN;
+  const int rbase = SWAP ? q0 : p0;
   const int kb0 = split * a.kb_per_split;
   const int kb1 = min(kb0 + a.kb_per_split, a.kb_total);
   const int nkb = kb1 - kb0;
@@ -457,6 +504,12 @@ __global__ void __launch_bounds__(128, 1)
     grid_dep_wait();
   } else {
     grid_dep_wait();
+    if (a.rms_ss && warp >= 2) {
+      // the tokens' RMSNorm scales, while the MMAs run (the producer's statistics are complete
+      // once the previous grid is)
+      const int count = SWAP ? BN : 128;
+      for (int i = threadIdx.x - 64; i < count; i += 64) rtab_s[i] = rbase + i < a.M ? rms_scale(a, rbase + i) : 1.f;
+    }
   }
   __syncwarp();
 
@@ -466,16 +519,9 @@ __global__ void __launch_bounds__(128, 1)
   const int t = threadIdx.x;
   const uint32_t lane_addr = tmem + (static_cast<uint32_t>(warp * 32) << 16);
   const int p = p0 + t;
-  // epilogue scratch past the barriers: the RMSNorm scale of this tile's tokens, and the
-  // statistics reduction of the cluster path
-  float* rtab_s = reinterpret_cast<float*>(smem + stages * STAGE_BYTES + 256);
-  float* stat_red = rtab_s + 128;  // [BN][32]
-  const int rbase = SWAP ? q0 : p0;
   const float* rtab = nullptr;
   if (a.rms_ss) {
-    const int count = SWAP ? BN : 128;
-    if (t < count) rtab_s[t] = rbase + t < a.M ? rms_scale(a, rbase + t) : 1.f;
-    __syncthreads();
+    __syncthreads();  // rtab_s, written by warps 2-3 during the main loop
     rtab = rtab_s;
   }
   float v[16], u[16];
@@ -722,6 +768,10 @@ constexpr int kEpiWarps = 16;                         // four per SM sub-partiti
 constexpr int kEpiCols = 256 / (kEpiWarps / 4);       // most columns one epilogue warp owns (BN 256)
 constexpr int kBarrierBytes = 256;                    // ring barriers, accumulator barriers, TMEM slot
 constexpr int kConstBytes = kEpiWarps * 3 * kEpiCols * 4;  // column constants
+// CTA-pair epilogue: per warp a 32-row x 16-column transpose buffer, rows 20 floats apart so that
+// both the row-per-lane writes and the column-group reads are free of bank conflicts
+constexpr int kOutStride = 20;
+constexpr int kOutBytes = kEpiWarps * 32 * kOutStride * 4;
 
 template <int BN, bool DUAL, bool I8>
 __global__ void __launch_bounds__(32 * (2 + kEpiWarps), 1)
@@ -914,6 +964,265 @@ __global__ void __launch_bounds__(32 * (2 + kEpiWarps), 1)
   if (warp == 1) tmem_dealloc(tmem, TMEM_COLS);
 }
 
+// ================================================================ CTA pair, persistent
+// Two CTAs of a cluster share each 256 x BN output tile (tokens on M). CTA r stages token rows
+// [p0 + 128 r, +128) of x and weight rows [q0 + r BN/2, +BN/2) of w in its own shared memory; the
+// even CTA issues M = 256 cta_group::2 MMAs over both CTAs' operands, and each CTA's TMEM receives
+// its 128 rows x BN columns of the accumulator (two buffers). Per SM that streams 128 x K + BN/2 x K
+// operand bytes per 128 x BN outputs instead of 128 x K + BN x K: the large GEMMs are bound by the
+// L2 -> SM read rate, not by the tensor pipe. Both CTAs' stage loads complete on the even CTA's
+// stage barrier (cta_group::2 TMA), which expects both halves' bytes; commits reach both CTAs'
+// barriers (multicast commit); the odd CTA's epilogue warps release a TMEM buffer with remote
+// arrives on the even CTA's barrier. Epilogue as the persistent kernel's.
+template <int BN, bool DUAL, bool I8>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(32 * (2 + kEpiWarps), 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
+                     const GemmArgs a, const int stages) {
+  constexpr int HB = BN / 2;  // weight rows per CTA
+  constexpr int A_BYTES = 128 * 128;
+  constexpr int B_BYTES = HB * 128;
+  constexpr int NB = DUAL ? 2 : 1;
+  constexpr int STAGE_BYTES = A_BYTES + NB * B_BYTES;
+  constexpr int NACC = BN * NB;
+  constexpr uint32_t TMEM_COLS = 2 * NACC <= 128 ? 128 : 2 * NACC <= 256 ? 256 : 512;
+  constexpr uint32_t IDESC = I8 ? idesc_i8(256, BN) : idesc_bf16(256, BN);
+  constexpr int KB_ELEMS = I8 ? 128 : 64;
+  static_assert(2 * NACC <= 512, "two accumulators must fit in TMEM");
+  static_assert(B_BYTES % 1024 == 0, "swizzled B halves start on 1024-byte boundaries");
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + stages * STAGE_BYTES);
+  uint64_t* empty = full + stages;
+  uint64_t* acc_full = empty + stages;  // [2]
+  uint64_t* acc_empty = acc_full + 2;   // [2], the even CTA's counts both CTAs' epilogue warps
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  float* consts = reinterpret_cast<float*>(smem + stages * STAGE_BYTES + kBarrierBytes);
+  float* stage_out = reinterpret_cast<float*>(smem + stages * STAGE_BYTES + kBarrierBytes + kConstBytes);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < stages; ++s) {
+      mbar_init(&full[s], 1);  // used in the even CTA only
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 2 * kEpiWarps);
+    }
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // both CTAs' barriers exist before any remote arrive or multicast commit
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int kb_total = a.kb_total;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tm_x);
+      tma_prefetch_desc(&tm_w);
+      const uint64_t pol_w = policy_evict_last();
+      const uint64_t pol_x = policy_evict_first();
+      bool waited = false, ok = true;
+      int it = 0;
+      for (int tile = pair; tile < a.num_tiles && ok; tile += npairs) {
+        const int p0 = (tile / a.tiles_q) * 256 + static_cast<int>(rank) * 128;
+        const int q0 = (tile % a.tiles_q) * BN + static_cast<int>(rank) * HB;
+        for (int kb = 0; kb < kb_total; ++kb, ++it) {
+          const int s = it % stages;
+          const uint32_t round = static_cast<uint32_t>(it / stages);
+          if (it >= stages && !mbar_wait(&empty[s], (round - 1) & 1u, a.status)) {
+            ok = false;
+            break;
+          }
+          uint8_t* st = smem + s * STAGE_BYTES;
+          if (leader) mbar_arrive_expect_tx(&full[s], 2 * STAGE_BYTES);
+          const uint32_t bar = mapa_shared(smem_u32(&full[s]), 0);
+          const int kx = kb * KB_ELEMS;
+#pragma unroll
+          for (int t = 0; t < NB; ++t) tma_load_2d_pair(st + A_BYTES + t * B_BYTES, &tm_w, bar, kx, q0 + t * a.N, pol_w);
+          if (!waited) {
+            grid_dep_wait();
+            waited = true;
+          }
+          tma_load_2d_pair(st, &tm_x, bar, kx, p0, pol_x);
+        }
+      }
+      if (!waited) grid_dep_wait();
+      grid_dep_launch();
+      // every commit the even CTA sends to this CTA's stage barriers has landed before exit
+      for (int j = it - stages; j < it && ok; ++j) {
+        if (j < 0) continue;
+        ok = mbar_wait(&empty[j % stages], static_cast<uint32_t>(j / stages) & 1u, a.status);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+      int it = 0, local = 0;
+      bool ok = true;
+      for (int tile = pair; tile < a.num_tiles && ok; tile += npairs, ++local) {
+        const int buf = local & 1;
+        const uint32_t use = static_cast<uint32_t>(local >> 1);
+        if (local >= 2 && !mbar_wait(&acc_empty[buf], (use - 1) & 1u, a.status)) break;
+        tc_fence_after();
+        const uint32_t d = tmem + static_cast<uint32_t>(buf * NACC);
+        for (int kb = 0; kb < kb_total; ++kb, ++it) {
+          const int s = it % stages;
+          const uint32_t round = static_cast<uint32_t>(it / stages);
+          if (!mbar_wait(&full[s], round & 1u, a.status)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t base = smem_u32(smem + s * STAGE_BYTES);
+          const uint64_t a0 = sw128_desc(base);
+          const uint64_t b0 = sw128_desc(base + A_BYTES);
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const uint32_t acc = (kb > 0 || k > 0) ? 1u : 0u;
+            if (I8)
+              mma_i8_pair(d, a0 + 2 * k, b0 + 2 * k, IDESC, acc);
+            else
+              mma_f16_pair(d, a0 + 2 * k, b0 + 2 * k, IDESC, acc);
+            if (DUAL) {
+              const uint64_t b1 = sw128_desc(base + A_BYTES + B_BYTES);
+              if (I8)
+                mma_i8_pair(d + BN, a0 + 2 * k, b1 + 2 * k, IDESC, acc);
+              else
+                mma_f16_pair(d + BN, a0 + 2 * k, b1 + 2 * k, IDESC, acc);
+            }
+          }
+          mma_commit_pair(&empty[s]);
+        }
+        if (ok) mma_commit_pair(&acc_full[buf]);
+      }
+    }
+  } else {
+    grid_dep_wait();
+    constexpr int G = kEpiWarps / 4;
+    constexpr int COLS = BN / G;
+    constexpr int CH = COLS / 16;
+    static_assert(COLS % 16 == 0 && COLS * NB <= 64, "epilogue slice must fit in registers");
+    const int e = warp - 2;
+    const int quad = warp & 3;
+    const int c_lo = (e / 4) * COLS;
+    float* kc = consts + e * 3 * kEpiCols;
+    float* kb = kc + kEpiCols;
+    float* ku = kb + kEpiCols;
+    const uint32_t release_addr = mapa_shared(smem_u32(acc_empty), 0);
+    int local = 0;
+    for (int tile = pair; tile < a.num_tiles; tile += npairs, ++local) {
+      const int buf = local & 1;
+      const uint32_t use = static_cast<uint32_t>(local >> 1);
+      const int p0 = (tile / a.tiles_q) * 256 + static_cast<int>(rank) * 128, q0 = (tile % a.tiles_q) * BN;
+      const int p = p0 + quad * 32 + lane;
+      __syncwarp();
+      for (int j = lane; j < COLS; j += 32) {
+        const int n = q0 + c_lo + j;
+        const bool in = n < a.N;
+        kc[j] = I8 ? (in ? a.x_scale * __ldg(a.w_scale + n) : 0.f) : 1.f;
+        kb[j] = (a.bias && in) ? __ldg(a.bias + n) : 0.f;
+        ku[j] = (I8 && DUAL && in) ? a.x_scale * __ldg(a.w_scale + a.N + n) : 1.f;
+      }
+      __syncwarp();
+      const float rs = (a.rms_ss && p < a.M) ? rms_scale(a, p) : 1.f;
+      if (!mbar_wait(&acc_full[buf], use & 1u, a.status)) break;
+      tc_fence_after();
+      const uint32_t taddr = tmem + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(buf * NACC + c_lo);
+      // Accumulator chunk by chunk (16 columns; the next chunk's TMEM load in flight while this one
+      // is processed); the buffer goes back to the MMA warp once its last chunk is in registers.
+      // Values per row (lane); stores either per row (one 16-byte piece of 32 rows: plain int8
+      // output) or through the warp's transpose buffer, each store covering 8 rows x 16 columns
+      // (lanes 8 apart share a row): fp32 / bf16 outputs, residuals and bf16 copies.
+      const bool transpose = a.y_type != SO101_I8 || a.res || a.y16 || a.stat_ss;
+      float* wb = stage_out + e * 32 * kOutStride;
+      const int prow0 = p0 + quad * 32, c4 = lane >> 3;
+      float ssq4[4] = {0.f, 0.f, 0.f, 0.f};
+      float ssq = 0.f;
+      // (SiLU gate: two accumulators per chunk, so no load ahead, to stay within the registers)
+      uint32_t ra[16], rb[16];
+      tmem_ld16(taddr, ra);
+      if constexpr (DUAL) tmem_ld16(taddr + BN, rb);
+      tmem_ld_wait(ra, rb);
+#pragma unroll
+      for (int c = 0; c < CH; ++c) {
+        uint32_t na[16], nb[16];
+        if (c + 1 < CH) {
+          if constexpr (!DUAL) tmem_ld16(taddr + 16 * (c + 1), na);
+        } else {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_remote(release_addr + static_cast<uint32_t>(buf * 8));
+        }
+        const int q = q0 + c_lo + 16 * c;
+        if (a.vec_ok && q + 16 <= a.N) {
+          if (transpose) {
+            float v[16];
+            epilogue_values16<DUAL, I8>(a, ra, rb, kc + 16 * c, kb + 16 * c, ku + 16 * c, rs, v);
+            float4* w4 = reinterpret_cast<float4*>(wb + lane * kOutStride);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) w4[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+            __syncwarp();
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const int rl = i * 8 + (lane & 7);
+              const float4 x = *reinterpret_cast<const float4*>(wb + rl * kOutStride + c4 * 4);
+              if (prow0 + rl < a.M) ssq4[i] += epilogue_store4(a, prow0 + rl, q + c4 * 4, x);
+            }
+            __syncwarp();
+          } else if (p < a.M) {
+            ssq += epilogue_row16_fast<DUAL, I8>(a, p, q, ra, rb, kc + 16 * c, kb + 16 * c, ku + 16 * c, rs);
+          }
+        } else if (p < a.M) {
+          float v[16], u[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            v[j] = acc_value<I8>(ra[j]) * rs;
+            u[j] = DUAL ? acc_value<I8>(rb[j]) * rs : 0.f;
+          }
+          epilogue16<false, DUAL, I8>(a, p, q, v, u);
+        }
+        if (c + 1 < CH) {
+          if constexpr (DUAL) {
+            tmem_ld16(taddr + 16 * (c + 1), na);
+            tmem_ld16(taddr + BN + 16 * (c + 1), nb);
+          }
+          tmem_ld_wait(na, nb);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) ra[j] = na[j], rb[j] = nb[j];
+        }
+      }
+      if (a.stat_ss) {  // statistics take the transposed stores
+        // row i * 8 + (lane & 7): its four column groups sit in lanes 8 apart
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          float t = ssq4[i];
+          t += __shfl_xor_sync(0xffffffffu, t, 8);
+          t += __shfl_xor_sync(0xffffffffu, t, 16);
+          const int m = prow0 + i * 8 + lane;
+          if (lane < 8 && m < a.M) a.stat_ss[static_cast<long long>(m) * a.stat_ld + (tile % a.tiles_q) * G + e / 4] = t;
+        }
+      }
+      (void)ssq;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // neither CTA frees TMEM while the pair's MMAs or epilogues may still use it
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc_pair(tmem, TMEM_COLS);
+}
+
 // ============================================================================ host side
 namespace {
 
@@ -956,16 +1265,16 @@ int sm_count() {
   return n;
 }
 
-int stage_bytes(int bn, bool swap, bool dual) {
+int stage_bytes(int bn, bool swap, bool dual, bool pair = false) {
   const int na = (swap && dual) ? 2 : 1, nb = (!swap && dual) ? 2 : 1;
-  return na * 128 * 128 + nb * bn * 128;
+  return na * 128 * 128 + nb * (pair ? bn / 2 : bn) * 128;
 }
 
 constexpr int kSmemBudget = 220 * 1024;
 constexpr int kTileScratch = (128 + 64 * 32) * 4;  // tile kernel epilogue scratch: rstd table, statistics
 constexpr int kMaxCluster = kMaxSplitCluster;
 
-enum Kind { kTile = 0, kPersistent = 1 };
+enum Kind { kTile = 0, kPersistent = 1, kPair = 2 };
 
 struct Plan {
   so101_gemm_config cfg;
@@ -1000,24 +1309,30 @@ int plan_gemm(int a_type, long long M, long long N, long long K, int epi, const 
   pl->kb_per_split = ceil_div(pl->kb_total, splits);
   pl->splits = ceil_div(pl->kb_total, pl->kb_per_split);  // no empty split
   c.splits = pl->splits;
-  pl->tiles_p = c.swap ? ceil_div(N, 128) : ceil_div(M, 128);
+  const bool pair = (c.flags & SO101_GEMM_PAIR) && !c.swap && pl->splits == 1 &&
+                    (c.bn == 256 || c.bn == 128);
+  pl->tiles_p = c.swap ? ceil_div(N, 128) : ceil_div(M, pair ? 256 : 128);
   pl->tiles_q = c.swap ? ceil_div(M, c.bn) : ceil_div(N, c.bn);
   pl->nacc = c.bn * (dual ? 2 : 1);
   const long long tiles = static_cast<long long>(pl->tiles_p) * pl->tiles_q;
   pl->kind = kTile;
-  if (!c.swap && pl->splits == 1 && !(c.flags & SO101_GEMM_ONE_TILE_PER_CTA) &&
-      ((c.flags & SO101_GEMM_PERSISTENT) || tiles >= sm_count()))
+  if (pair)
+    pl->kind = kPair;
+  else if (!c.swap && pl->splits == 1 && !(c.flags & SO101_GEMM_ONE_TILE_PER_CTA) &&
+           ((c.flags & SO101_GEMM_PERSISTENT) || tiles >= sm_count()))
     pl->kind = kPersistent;
+  if (!pair) c.flags &= ~SO101_GEMM_PAIR;
   pl->cluster = 1;
   if (pl->kind == kTile && pl->splits > 1 && pl->splits <= kMaxCluster && !(c.flags & SO101_GEMM_GLOBAL_SPLITK))
     pl->cluster = pl->splits;
-  const int sb = stage_bytes(c.bn, c.swap, dual);
-  const int max_st = (kSmemBudget - 1024 - 256 - (pl->kind == kPersistent ? kConstBytes : kTileScratch)) / sb;
+  const bool pers = pl->kind == kPersistent || pl->kind == kPair;
+  const int sb = stage_bytes(c.bn, c.swap, dual, pair);
+  const int max_st = (kSmemBudget - 1024 - 256 - (pers ? kConstBytes : kTileScratch) - (pair ? kOutBytes : 0)) / sb;
   if (c.stages <= 0) {
-    int want = pl->kind == kPersistent ? 8 : pl->kb_per_split;
+    int want = pers ? (pair ? 12 : 8) : pl->kb_per_split;
     if (want < 2) want = 2;
     c.stages = want < max_st ? want : max_st;
-    if (c.stages > 8) c.stages = 8;
+    if (c.stages > (pair ? 12 : 8)) c.stages = pair ? 12 : 8;
   }
   if (c.stages < 2 || c.stages > max_st) return SO101_ERR_ARG;
   if (pl->cluster > 1 && c.stages * sb < pl->nacc * 128 * 4) {
@@ -1084,6 +1399,34 @@ int launch_persistent(const CUtensorMap& tx, const CUtensorMap& tw, const GemmAr
                 pl.cfg.stages, stream, pdl, &configured);
 }
 
+// One cluster of two CTAs per SM pair, as many clusters as can be resident at once.
+template <int BN, bool DUAL, bool I8>
+int launch_pair(const CUtensorMap& tx, const CUtensorMap& tw, const GemmArgs& a, const Plan& pl, cudaStream_t stream,
+                bool pdl) {
+  static int configured = 0;
+  static int max_clusters = 0;
+  const int smem = pl.cfg.stages * stage_bytes(BN, false, DUAL, true) + 1024 + kBarrierBytes + kConstBytes + kOutBytes;
+  auto kern = gemm_pair_kernel<BN, DUAL, I8>;
+  if (configured == 0) {
+    const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBudget);
+    if (e != cudaSuccess) return launch_error(e);
+    configured = 1;
+  }
+  if (max_clusters == 0) {
+    cudaLaunchConfig_t q = {};
+    q.gridDim = dim3(2 * (sm_count() / 2), 1, 1);
+    q.blockDim = dim3(32 * (2 + kEpiWarps), 1, 1);
+    q.dynamicSmemBytes = kSmemBudget;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &q) != cudaSuccess || n < 1) n = sm_count() / 2;
+    max_clusters = n;
+  }
+  const long long tiles = static_cast<long long>(pl.tiles_p) * pl.tiles_q;
+  const int pairs = static_cast<int>(tiles < max_clusters ? tiles : max_clusters);
+  return launch(kern, tx, tw, a, dim3(2 * pairs, 1, 1), 32 * (2 + kEpiWarps), smem, 1, pl.cfg.stages, stream, pdl,
+                &configured);
+}
+
 template <bool SWAP, bool DUAL, bool I8>
 int launch_bn(const CUtensorMap& tx, const CUtensorMap& tw, const GemmArgs& a, const Plan& pl, cudaStream_t stream,
               bool pdl) {
@@ -1096,6 +1439,12 @@ int launch_bn(const CUtensorMap& tx, const CUtensorMap& tw, const GemmArgs& a, c
     }
   } else {
     const bool pers = pl.kind == kPersistent;
+    if (pl.kind == kPair) {
+      if (pl.cfg.bn == 128) return launch_pair<128, DUAL, I8>(tx, tw, a, pl, stream, pdl);
+      if constexpr (!DUAL)
+        if (pl.cfg.bn == 256) return launch_pair<256, DUAL, I8>(tx, tw, a, pl, stream, pdl);
+      return SO101_ERR_ARG;
+    }
     switch (pl.cfg.bn) {
       case 64:
         return pers ? launch_persistent<64, DUAL, I8>(tx, tw, a, pl, stream, pdl)
@@ -1182,7 +1531,7 @@ extern "C" int so101_gemm_workspace(int a_type, int64_t M, int64_t N, int64_t K,
 // and split) and the persistent kernel (one per column tile and epilogue column group).
 int stat_slots_of(const Plan& pl, bool dual, int a_type, long long N) {
   if (dual || a_type != SO101_BF16) return 0;
-  if (pl.kind == kPersistent) return N % 16 == 0 ? pl.tiles_q * (kEpiWarps / 4) : 0;
+  if (pl.kind == kPersistent || pl.kind == kPair) return N % 16 == 0 ? pl.tiles_q * (kEpiWarps / 4) : 0;
   if (pl.cfg.swap && pl.cluster > 1 && N % 4 == 0) return pl.tiles_p * pl.splits;
   return 0;
 }
@@ -1273,7 +1622,7 @@ extern "C" int so101_gemm(int a_type, const void* x, int64_t ldx, const void* w,
       return SO101_ERR_ARG;
     if (a.y16 && (reinterpret_cast<uintptr_t>(a.y16) % 16 || a.ld16 % 8 || a.ld16 < N || N % 16)) return SO101_ERR_ARG;
     if (epi->epilogue == SO101_EPI_GELU || (a.res && a.r_type != SO101_F32)) return SO101_ERR_ARG;
-    if (!pl.cfg.swap && pl.kind != kPersistent) return SO101_ERR_ARG;
+    if (!pl.cfg.swap && pl.kind != kPersistent && pl.kind != kPair) return SO101_ERR_ARG;
   }
   const int ysz = y_type == SO101_F32 ? 4 : y_type == SO101_BF16 ? 2 : 1;
   bool vec = reinterpret_cast<uintptr_t>(y) % 16 == 0 && (ldy * ysz) % 16 == 0;
@@ -1289,7 +1638,7 @@ extern "C" int so101_gemm(int a_type, const void* x, int64_t ldx, const void* w,
   const long long w_rows = dual ? 2 * N : N;
   CUtensorMap tx, tw;
   const int x_box = pl.cfg.swap ? pl.cfg.bn : 128;
-  const int w_box = pl.cfg.swap ? 128 : pl.cfg.bn;
+  const int w_box = pl.cfg.swap ? 128 : (pl.kind == kPair ? pl.cfg.bn / 2 : pl.cfg.bn);
   rc = make_map(&tx, x, i8, K, M, ldx, x_box);
   if (rc) return rc;
   rc = make_map(&tw, w, i8, K, w_rows, ldw, w_box);

@@ -13,6 +13,10 @@ This is `src/so101_smolvla_edge/model/engine.py`'s `Engine` (constructor options
     vision    "cuda" (and the reference's "torch" / "trt") run the vision tower on the B200
               kernels in `trt_precision` "bf16" or "int8" (W8A8, with activation clips).
 
+    compile   "autotune" times the GEMM plans of every GEMM with many token rows (persistent or
+              CTA-pair tiles, 128 or 256 wide) and keeps the fastest (`Engine.tuning` reports
+              them); other values are accepted and ignored. SO101_AUTOTUNE=1 does the same.
+
 There is no CPU fallback: without a CUDA device or without the library, construction raises.
 `batch=B` sizes every buffer for B observations; `infer_batch` runs them as one graph replay.
 """
@@ -104,7 +108,7 @@ class Engine:
             raise ValueError(f"vision must be one of {VISIONS}, not {vision!r}")
         if trt_precision not in ("bf16", "int8"):
             raise ValueError(f"trt_precision must be 'bf16' or 'int8', not {trt_precision!r}")
-        if compile:
+        if compile and compile != "autotune":
             log.info("compile=%r ignored: the B200 path is hand-written kernels in a CUDA graph", compile)
         self.vision_precision = trt_precision
         clip = None
@@ -130,6 +134,11 @@ class Engine:
         self.path = B200Path(b, dev, self.batch, trt_precision, clip, expert_step, fold_norms)
         self.tp = self.path  # the reference's attribute for the custom-kernel path
         p = self.path
+        self.tuning = None
+        if compile == "autotune" or os.environ.get("SO101_AUTOTUNE", "0") == "1":
+            # the reference autotunes its prefix GEMMs here (pkg/model/engine.py:219-233); this
+            # path times its own GEMM plans for every large GEMM and rebuilds with the fastest
+            self.tuning = p.autotune()
         self.img, self.state, self.noise, self.out = p.img, p.state, p.noise, p.out
         self._host_img = torch.zeros(p.img.shape, dtype=torch.uint8).pin_memory()
         self._host_state = torch.zeros(p.state.shape, dtype=torch.float32).pin_memory()

@@ -35,6 +35,12 @@ from .spec import ModelSpec, vision_linear_names
 
 REPRS = {"absolute": 0, "delta": 1, "velocity": 2}
 STAT_SLOTS = 64  # statistics slots per row for the RMSNorm finished in a GEMM (so101_epilogue.rms_ss)
+# Plans `B200Path.autotune` times for a GEMM with many token rows (so101_gemm_config: swap, bn,
+# splits, stages, flags): the library's pick, the persistent kernel and the CTA pair at two tile
+# widths. None of them splits K, so the choice never changes the accumulation order.
+TUNE_CANDIDATES = (None, (0, 256, 1, 0, L.GEMM_PERSISTENT), (0, 128, 1, 0, L.GEMM_PERSISTENT),
+                   (0, 256, 1, 0, L.GEMM_PAIR), (0, 128, 1, 0, L.GEMM_PAIR))  # fmt: skip
+TUNE_MIN_ROWS = 1024  # fewer rows: weight-streaming tiles, whose pick is kept
 
 
 def unsupported(spec: ModelSpec) -> str | None:
@@ -140,11 +146,51 @@ class B200Path:
         self._upload(bundle)
         self._alloc()
         self.xs = self._expert_step(expert_step)
+        self.tuned: dict[tuple, tuple | None] = {}  # GEMM signature -> plan chosen by autotune
+        self._build_all()
+
+    def _build_all(self) -> None:
+        self._sites: dict[tuple, tuple[str, tuple]] = {}  # GEMM signature -> (name, launch args)
         self.progs = {"vision": Program("vision"), "prefix": Program("prefix"),
                       "denoise": Program("denoise")}  # fmt: skip
         self._build_vision(self.progs["vision"])
         self._build_prefix(self.progs["prefix"])
         self._build_denoise(self.progs["denoise"])
+
+    def autotune(self, reps: int = 5) -> dict[str, dict]:
+        """Time every candidate plan (TUNE_CANDIDATES) of each distinct GEMM with many token rows
+        on this GPU, on its first launch site's own buffers, and rebuild the programs with the
+        fastest. The B200 counterpart of the reference's autotuned GEMMs (`compile="autotune"`,
+        pkg/model/engine.py:219-233, and `scripts/tune_gemm.py`). Rebuilding matters: a residual
+        GEMM's plan sets how many statistics slots the next norm's GEMM reads. Overwrites the
+        work buffers (the next chunk recomputes them). Returns {site: {"plan", "ms"}}."""
+        stream = torch.cuda.current_stream(self.dev).cuda_stream
+        report: dict[str, dict] = {}
+        for key, (what, args) in self._sites.items():
+            times: dict[tuple | None, float] = {}
+            for cand in TUNE_CANDIDATES:
+                cfg = None if cand is None else L.GemmConfig(*cand)
+                a = list(args)
+                a[12] = None if cfg is None else C.byref(cfg)
+                need, tick = C.c_int64(), C.c_int64()
+                if self.lib.so101_gemm_workspace(a[0], a[8], a[9], a[10], key[4], a[12], C.byref(need),
+                                                 C.byref(tick)) != L.OK or need.value > self.ws.nbytes:  # fmt: skip
+                    continue
+                if self.lib.so101_gemm(*a, stream) != L.OK:  # a plan this epilogue cannot take
+                    continue
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                for _ in range(reps):
+                    L.check(self.lib.so101_gemm(*a, stream), f"autotune {what}")
+                e1.record()
+                e1.synchronize()
+                times[cand] = e0.elapsed_time(e1) / reps
+            best = min(times, key=times.get)
+            self.tuned[key] = best
+            report[what] = {"plan": best, "ms": {str(c): t for c, t in times.items()}}
+        torch.cuda.synchronize(self.dev)
+        self._build_all()
+        return report
 
     # ------------------------------------------------------------------ weights and buffers
     def _upload(self, b: Bundle) -> None:
@@ -288,6 +334,12 @@ class B200Path:
         k = x.shape[1]
         n = w.shape[0] // 2 if gate else w.shape[0]
         a_type = L.I8 if w.dtype == torch.int8 else L.BF16
+        key = (a_type, m, n, k, L.EPI_SILU_GATE if gate else (L.EPI_GELU if gelu else L.EPI_NONE), DTYPE[y.dtype],
+               -1 if residual is None else DTYPE[residual.dtype], bias is not None, rms is not None,
+               stat is not None)  # fmt: skip
+        plan = self.tuned.get(key)
+        cfg = None if plan is None else L.GemmConfig(*plan)
+        cfg_ref = None if cfg is None else C.byref(cfg)
         epi = L.Epilogue(
             epilogue=L.EPI_SILU_GATE if gate else (L.EPI_GELU if gelu else L.EPI_NONE),
             bias=None if bias is None else bias.data_ptr(),
@@ -305,20 +357,22 @@ class B200Path:
         if stat is not None:
             ss, x16, nw = stat
             got = C.c_int()
-            if self.lib.so101_gemm_stat_slots(a_type, m, n, k, epi.epilogue, None, C.byref(got)) == L.OK \
+            if self.lib.so101_gemm_stat_slots(a_type, m, n, k, epi.epilogue, cfg_ref, C.byref(got)) == L.OK \
                     and got.value <= ss.shape[1]:  # fmt: skip
                 slots_out = got.value
                 epi.stat_ss, epi.stat_ld = ss.data_ptr(), ss.stride(0)
                 epi.y16, epi.ld16, epi.y16_scale = x16.data_ptr(), x16.stride(0), nw.data_ptr()
         need, tick = C.c_int64(), C.c_int64()
-        L.check(self.lib.so101_gemm_workspace(a_type, m, n, k, epi.epilogue, None, C.byref(need),
+        L.check(self.lib.so101_gemm_workspace(a_type, m, n, k, epi.epilogue, cfg_ref, C.byref(need),
                                               C.byref(tick)), what)  # fmt: skip
         if need.value > self.ws.nbytes or tick.value > self.ws.tickets.numel():
             raise RuntimeError(f"{what}: split-K workspace too small ({need.value} bytes)")
-        prog.add(what, self.lib.so101_gemm, a_type, x.data_ptr(), x.stride(0), w.data_ptr(),
-                 w.stride(0), y.data_ptr(), y.stride(0), DTYPE[y.dtype], m, n, k, C.byref(epi),
-                 None, self.ws.partials.data_ptr(), self.ws.nbytes, self.ws.tickets.data_ptr(),
-                 self.ws.tickets.numel(), keep=(epi,))  # fmt: skip
+        args = (a_type, x.data_ptr(), x.stride(0), w.data_ptr(), w.stride(0), y.data_ptr(), y.stride(0),
+                DTYPE[y.dtype], m, n, k, C.byref(epi), cfg_ref, self.ws.partials.data_ptr(), self.ws.nbytes,
+                self.ws.tickets.data_ptr(), self.ws.tickets.numel())  # fmt: skip
+        prog.add(what, self.lib.so101_gemm, *args, keep=(epi, cfg))
+        if m >= TUNE_MIN_ROWS and key not in self._sites:
+            self._sites[key] = (what, args)
         if stat is not None and slots_out == 0:
             slots_out = self._stats(prog, f"{what}.stats", y, stat[2], stat[1], stat[0])
         return slots_out

@@ -214,3 +214,23 @@ def test_fused_expert_step_matches_per_op_path(case):
         assert np.abs(a - o).max() <= ACTION_TOL * scale, (seed, np.abs(a - o).max())
     del fused, per_op
     torch.cuda.empty_cache()
+
+
+def test_autotuned_engine_matches_reference():
+    """compile="autotune" (the reference's autotuned GEMMs) times the GEMM plans of every large
+    GEMM and rebuilds the programs with the fastest: configs[0]'s vision GEMMs (3072 rows) are
+    tuned, the chunk stays within the action tolerance of the reference's float32 chunk and within
+    rounding of the untuned engine (the plans never split K; only the statistics' summation order
+    of a re-tiled residual GEMM can move)."""
+    from so101_smolvla_edge_b200.engine import Engine
+
+    g = golden("config0")
+    b = config0_bundle()
+    tuned = Engine(b, warmup=1, compile="autotune")
+    assert tuned.tuning and all(v["ms"] for v in tuned.tuning.values())
+    images, state, noise = observation(b, 0)
+    a = tuned.infer(images, state, noise)
+    assert np.array_equal(a, tuned.infer(images, state, noise))
+    assert np.abs(a - g["actions"][0]).max() <= ACTION_TOL
+    del tuned
+    torch.cuda.empty_cache()

@@ -137,10 +137,11 @@ def test_silu_gate_tiles(swap, bn, split, flags):
 
 @pytest.mark.parametrize("m,n,k", [(3072, 2304, 768), (3072, 768, 3072), (1000, 5120, 960), (300, 720, 200)])
 @pytest.mark.parametrize("epi", ["gelu", "residual", "silu_gate"])
-@pytest.mark.parametrize("flags", [2, 4])
+@pytest.mark.parametrize("flags", [2, 4, 8])
 def test_persistent_matches_one_tile_per_cta(m, n, k, epi, flags):
-    """The persistent kernel (flags 2) and one tile per CTA (flags 4) both match the reference,
-    including tile counts that are not a multiple of the grid."""
+    """The persistent kernel (flags 2), one tile per CTA (flags 4) and the CTA-pair kernel (flags 8:
+    256-row tiles over two SMs, cta_group::2) all match the reference, including tile counts that
+    are not a multiple of the grid and pair tiles whose second CTA lies wholly past the last row."""
     from so101_smolvla_edge_b200.ops import linear
 
     x = rnd(m, k, dtype=torch.bfloat16)
@@ -173,7 +174,7 @@ def test_strided_input_view():
 
 
 @pytest.mark.parametrize("m,k,n", [(3072, 768, 2304), (3072, 3072, 768), (192, 12288, 960), (50, 768, 64)])
-@pytest.mark.parametrize("flags", [0, 2, 4])
+@pytest.mark.parametrize("flags", [0, 2, 4, 8])
 def test_int8_gemm_is_the_fake_quant_product(m, k, n, flags):
     """W8A8: int8 x and w with per-tensor / per-channel scales give the float product of the
     dequantized operands (exact int32 accumulation)."""
@@ -406,8 +407,9 @@ def test_rmsnorm_in_gemm(m, n, k, gate):
     assert err <= 2 * err_chain + 1e-3 * scale, (err, err_chain)
 
 
-@pytest.mark.parametrize("m,n,k", [(50, 720, 960), (50, 720, 2048), (241, 960, 2560), (3200, 720, 960)])
-def test_residual_gemm_statistics(m, n, k):
+@pytest.mark.parametrize("m,n,k,config", [(50, 720, 960, None), (50, 720, 2048, None), (241, 960, 2560, None),
+                                          (3200, 720, 960, None), (3200, 720, 960, (0, 256, 1, 0, 8))])
+def test_residual_gemm_statistics(m, n, k, config):
     """A residual GEMM's statistics (sums of squares over disjoint column ranges) and bf16(output
     * next norm weight) feed the next norm's GEMM: the slots sum to the rows' sums of squares,
     bit-stable."""
@@ -417,14 +419,14 @@ def test_residual_gemm_statistics(m, n, k):
     w = rnd(n, k, dtype=torch.bfloat16, scale=k**-0.5, seed=1)
     e = rnd(m, n, seed=2)
     nw = 1.0 + 0.1 * rnd(n, seed=3)
-    slots = gemm_stat_slots(m, n, k)
+    slots = gemm_stat_slots(m, n, k, config)
     assert 1 <= slots <= 64
     outs = []
     for _ in range(2):
         r = e.clone()
         ss = torch.zeros(m, 64, device="cuda")
         x16 = torch.zeros(m, n, device="cuda", dtype=torch.bfloat16)
-        linear(x, w, residual=r, out=r, stat=(ss, x16, nw))
+        linear(x, w, residual=r, out=r, stat=(ss, x16, nw), config=config)
         outs.append((r, ss, x16))
     r, ss, x16 = outs[0]
     assert torch.equal(r, outs[1][0]) and torch.equal(ss, outs[1][1])
