@@ -295,6 +295,29 @@ def test_siglip_attention_batched(out):
     assert torch.equal(got, again)
 
 
+@pytest.mark.parametrize("case", ["expert_self", "expert_cross", "prefix", "five_heads_per_kv"])
+def test_attention_gqa_batched(case):
+    """The batched prefix and expert shapes (hundreds of CTAs, grouped query heads over shared kv
+    heads, prefix-LM and causal masks, RoPE on q) against the float32 reference for a sample of the
+    batch; replays are equal."""
+    from so101_smolvla_edge_b200.ops import attention
+
+    B, hd = 48, 64
+    nq, nkv, lq, lk, cf, qo = {"expert_self": (15, 5, 50, 291, 241, 241), "expert_cross": (15, 5, 50, 241, 241, 0),
+                               "prefix": (15, 5, 241, 241, 240, 0), "five_heads_per_kv": (5, 1, 50, 178, 128, 128)}[case]
+    q = rnd(B, lq, nq * hd, dtype=torch.bfloat16, scale=2.0)
+    k = rnd(B, lk, nkv * hd, dtype=torch.bfloat16, seed=1)
+    v = rnd(B, lk, nkv * hd, dtype=torch.bfloat16, seed=2)
+    cos, sin = rope_tables(torch.arange(qo, qo + lq, device="cuda"), hd, 10000.0)
+    got = attention(q, k, v, nq, nkv, cos=cos, sin=sin, causal_from=cf, q_offset=qo)
+    vis = visibility(lq, lk, cf, qo)
+    for b in range(0, B, 7):
+        want = attention_ref(q[b], k[b], v[b], nq, nkv, vis, cos, sin)
+        err = (got[b].float() - want).abs()
+        assert err.max() <= 0.02 * want.abs().max() and err.mean() <= 2e-3 * want.abs().mean() + 1e-4, (b, float(err.max()))
+    assert torch.equal(got, attention(q, k, v, nq, nkv, cos=cos, sin=sin, causal_from=cf, q_offset=qo))
+
+
 def test_attention_batched_and_strided():
     """A batch of independent problems with k and v as views into the fused qkv rows."""
     from so101_smolvla_edge_b200.ops import attention
