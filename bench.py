@@ -357,10 +357,10 @@ def run_ours(args) -> None:
     pk, src = peaks()
     int8_peak = 2.0 * pk["bf16_tflops"]
     plans = {k: v["plan"] for k, v in (eng.tuning or {}).items()}
-    roof = {"kernel": f"{gemm_kernel_name(plans.get('vis.0.fc1'), M, N, K)} vis.0.fc1 (W8A8, GELU, int8 out)",
-            "bound": "tensor",
+    kname = gemm_kernel_name(plans.get("vis.0.fc1"), M, N, K)
+    roof = {"kernel": f"{kname} vis.0.fc1 (W8A8, GELU, int8 out)", "bound": "tensor",
             "achieved": 2.0 * M * N * K / (kms * 1e-3) / 1e12, "peak": int8_peak, "unit": "TOP/s",
-            "traffic": profile_traffic("vis.fc1"), "ms": kms,
+            "traffic": profile_traffic("vis.fc1/" + kname.split("<")[0]), "ms": kms,
             "peak_source": f"2 x {src} bf16 dense ({pk['bf16_tflops']} TF/s): int8 dense rate is twice bf16"}  # fmt: skip
     roof["frac"] = roof["achieved"] / roof["peak"]
     # second family: SigLIP self-attention on tcgen05 (4 L^2 d flops per image and head)

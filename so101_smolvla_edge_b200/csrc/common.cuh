@@ -403,14 +403,66 @@ __device__ __forceinline__ float gelu_tanh_fast(float x) {
   return fmaf(h, t, h);
 }
 
+// Packed fp32x2 arithmetic (sm_100): two independent round-to-nearest fp32 operations per
+// instruction on (x, y) pairs, so results equal the scalar ones bit for bit.
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\t"
+      "mov.b64 rb, {%4, %5};\n\t"
+      "mov.b64 rc, {%6, %7};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\t"
+      "mov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\t"
+      "mov.b64 rb, {%4, %5};\n\t"
+      "add.rn.f32x2 rd, ra, rb;\n\t"
+      "mov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+
+__device__ __forceinline__ float2 fmul2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\t"
+      "mov.b64 rb, {%4, %5};\n\t"
+      "mul.rn.f32x2 rd, ra, rb;\n\t"
+      "mov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+
+// gelu_tanh_fast on a pair, packed; same operations in the same order, same results.
+__device__ __forceinline__ float2 gelu_tanh_fast2(float2 x) {
+  const float2 p = ffma2(fmul2(x, x), make_float2(0.7978845608028654f * 0.044715f, 0.7978845608028654f * 0.044715f),
+                         make_float2(0.7978845608028654f, 0.7978845608028654f));
+  const float2 a = fmul2(x, p);
+  const float2 t = make_float2(tanh_fast(a.x), tanh_fast(a.y));
+  const float2 h = fmul2(make_float2(0.5f, 0.5f), x);
+  return ffma2(h, t, h);
+}
+
 // Four values to packed int8 (clamp(round_half_even(v * inv), -128, 127)): the clamped product
 // plus 1.5 * 2^23 holds the rounded integer in the low byte of its bit pattern.
 __device__ __forceinline__ uint32_t pack4_i8(float a, float b, float c, float d, float inv) {
-  const uint32_t qa = __float_as_uint(fminf(fmaxf(a * inv, -128.f), 127.f) + 12582912.0f);
-  const uint32_t qb = __float_as_uint(fminf(fmaxf(b * inv, -128.f), 127.f) + 12582912.0f);
-  const uint32_t qc = __float_as_uint(fminf(fmaxf(c * inv, -128.f), 127.f) + 12582912.0f);
-  const uint32_t qd = __float_as_uint(fminf(fmaxf(d * inv, -128.f), 127.f) + 12582912.0f);
-  return __byte_perm(__byte_perm(qa, qb, 0x0040), __byte_perm(qc, qd, 0x0040), 0x5410);
+  const float2 m01 = fmul2(make_float2(a, b), make_float2(inv, inv));
+  const float2 m23 = fmul2(make_float2(c, d), make_float2(inv, inv));
+  const float2 r01 = fadd2(make_float2(fminf(fmaxf(m01.x, -128.f), 127.f), fminf(fmaxf(m01.y, -128.f), 127.f)),
+                           make_float2(12582912.0f, 12582912.0f));
+  const float2 r23 = fadd2(make_float2(fminf(fmaxf(m23.x, -128.f), 127.f), fminf(fmaxf(m23.y, -128.f), 127.f)),
+                           make_float2(12582912.0f, 12582912.0f));
+  return __byte_perm(__byte_perm(__float_as_uint(r01.x), __float_as_uint(r01.y), 0x0040),
+                     __byte_perm(__float_as_uint(r23.x), __float_as_uint(r23.y), 0x0040), 0x5410);
 }
 
 // SiLU through sigmoid(x) = (1 + tanh(x / 2)) / 2.

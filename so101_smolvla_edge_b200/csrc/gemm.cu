@@ -235,22 +235,35 @@ template <bool DUAL, bool I8>
 __device__ __forceinline__ void epilogue_values16(const GemmArgs& a, const uint32_t (&r0)[16], const uint32_t (&r1)[16],
                                                   const float* kc, const float* kb, const float* ku, float rs,
                                                   float (&v)[16]) {
+  // packed fp32x2 throughout (the epilogue is instruction-bound); rs differs from 1 only with a
+  // folded RMSNorm, and multiplying by 1 is exact, so that multiply is skipped without it
+  const bool scaled = a.rms_ss != nullptr;
+  const float2 rs2 = make_float2(rs, rs);
+  float2 x[8];
 #pragma unroll
   for (int j4 = 0; j4 < 4; ++j4) {
     const float4 bi = *reinterpret_cast<const float4*>(kb + 4 * j4);
-    const float bb[4] = {bi.x, bi.y, bi.z, bi.w};
+    float2 s01, s23, x01, x23;
     if constexpr (I8) {
       const float4 sc = *reinterpret_cast<const float4*>(kc + 4 * j4);
-      const float ss[4] = {sc.x, sc.y, sc.z, sc.w};
-#pragma unroll
-      for (int e = 0; e < 4; ++e)
-        v[4 * j4 + e] = fmaf(static_cast<float>(static_cast<int>(r0[4 * j4 + e])), ss[e] * rs, bb[e]);
+      s01 = make_float2(sc.x, sc.y);
+      s23 = make_float2(sc.z, sc.w);
+      if (scaled) {
+        s01 = fmul2(s01, rs2);
+        s23 = fmul2(s23, rs2);
+      }
+      x01 = make_float2(static_cast<float>(static_cast<int>(r0[4 * j4])), static_cast<float>(static_cast<int>(r0[4 * j4 + 1])));
+      x23 = make_float2(static_cast<float>(static_cast<int>(r0[4 * j4 + 2])), static_cast<float>(static_cast<int>(r0[4 * j4 + 3])));
     } else {
-#pragma unroll
-      for (int e = 0; e < 4; ++e) v[4 * j4 + e] = fmaf(__uint_as_float(r0[4 * j4 + e]), rs, bb[e]);
+      s01 = s23 = rs2;
+      x01 = make_float2(__uint_as_float(r0[4 * j4]), __uint_as_float(r0[4 * j4 + 1]));
+      x23 = make_float2(__uint_as_float(r0[4 * j4 + 2]), __uint_as_float(r0[4 * j4 + 3]));
     }
+    x[2 * j4] = ffma2(x01, s01, make_float2(bi.x, bi.y));
+    x[2 * j4 + 1] = ffma2(x23, s23, make_float2(bi.z, bi.w));
   }
   if constexpr (DUAL) {
+    // the SiLU gate stays scalar: packed it measured slower (the pair packing costs moves here)
 #pragma unroll
     for (int j4 = 0; j4 < 4; ++j4) {
       float su[4] = {rs, rs, rs, rs};
@@ -258,21 +271,26 @@ __device__ __forceinline__ void epilogue_values16(const GemmArgs& a, const uint3
         const float4 sc = *reinterpret_cast<const float4*>(ku + 4 * j4);
         su[0] = sc.x * rs, su[1] = sc.y * rs, su[2] = sc.z * rs, su[3] = sc.w * rs;
       }
+      float g[4] = {x[2 * j4].x, x[2 * j4].y, x[2 * j4 + 1].x, x[2 * j4 + 1].y};
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const float up = I8 ? static_cast<float>(static_cast<int>(r1[4 * j4 + e])) * su[e]
                             : __uint_as_float(r1[4 * j4 + e]) * su[e];
-        v[4 * j4 + e] = silu(v[4 * j4 + e]) * up;
+        g[e] = silu(g[e]) * up;
       }
+      x[2 * j4] = make_float2(g[0], g[1]);
+      x[2 * j4 + 1] = make_float2(g[2], g[3]);
     }
   } else if (a.epilogue == SO101_EPI_GELU) {
 #pragma unroll
-    for (int j = 0; j < 16; ++j) v[j] = gelu_tanh_fast(v[j]);
+    for (int j = 0; j < 8; ++j) x[j] = gelu_tanh_fast2(x[j]);
   }
   if (a.out_scale != 1.f) {
 #pragma unroll
-    for (int j = 0; j < 16; ++j) v[j] *= a.out_scale;
+    for (int j = 0; j < 8; ++j) x[j] = fmul2(x[j], make_float2(a.out_scale, a.out_scale));
   }
+#pragma unroll
+  for (int j = 0; j < 8; ++j) v[2 * j] = x[j].x, v[2 * j + 1] = x[j].y;
 }
 
 template <bool DUAL, bool I8>
@@ -289,7 +307,9 @@ __device__ __forceinline__ float epilogue_row16_fast(const GemmArgs& a, int m, i
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const float4 r = r4[j];
-        v[4 * j] += r.x, v[4 * j + 1] += r.y, v[4 * j + 2] += r.z, v[4 * j + 3] += r.w;
+        const float2 s01 = fadd2(make_float2(v[4 * j], v[4 * j + 1]), make_float2(r.x, r.y));
+        const float2 s23 = fadd2(make_float2(v[4 * j + 2], v[4 * j + 3]), make_float2(r.z, r.w));
+        v[4 * j] = s01.x, v[4 * j + 1] = s01.y, v[4 * j + 2] = s23.x, v[4 * j + 3] = s23.y;
       }
     } else {
       const uint4* r4 = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(a.res) + rrow * a.ldr + qb);
@@ -359,7 +379,9 @@ __device__ __forceinline__ float epilogue_store4(const GemmArgs& a, int m, int n
     const long long rrow = a.r_period > 0 ? m % a.r_period : row;
     if (a.r_type == SO101_F32) {
       const float4 r = *reinterpret_cast<const float4*>(static_cast<const float*>(a.res) + rrow * a.ldr + n);
-      x.x += r.x, x.y += r.y, x.z += r.z, x.w += r.w;
+      const float2 s01 = fadd2(make_float2(x.x, x.y), make_float2(r.x, r.y));
+      const float2 s23 = fadd2(make_float2(x.z, x.w), make_float2(r.z, r.w));
+      x = make_float4(s01.x, s01.y, s23.x, s23.y);
     } else {
       const uint2 r = *reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(a.res) + rrow * a.ldr + n);
       const float2 f0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&r.x));

@@ -154,6 +154,90 @@ __global__ void __launch_bounds__(LF_THREADS) linear_f32_kernel(const float* __r
   }
 }
 
+// Many rows (the batched action / time MLP): 128 x 64 outputs per 256-thread CTA, each thread 8
+// rows x 4 columns in registers. Both tiles sit k-major in shared memory (x is transposed as it is
+// stored), so one k step is three 16-byte broadcast loads for 32 FMAs; the next k block's global
+// loads are in registers during the current block's FMAs. Every output still accumulates over k in
+// order with fmaf, so results equal linear_f32_kernel's bit for bit.
+constexpr int LT_BM = 128, LT_BN = 64, LT_BK = 16, LT_THREADS = 256;
+
+__global__ void __launch_bounds__(LT_THREADS) linear_f32_tiled_kernel(const float* __restrict__ x, long long ldx,
+                                                                      const float* __restrict__ w, long long ldw,
+                                                                      const float* __restrict__ bias,
+                                                                      const float* __restrict__ bias2,
+                                                                      float* __restrict__ y, long long ldy, int M,
+                                                                      int N, int K, int act) {
+  grid_dep_launch();
+  grid_dep_wait();
+  __shared__ __align__(16) float xs[2][LT_BK][LT_BM + 4];
+  __shared__ __align__(16) float ws[2][LT_BK][LT_BN + 4];
+  const int m0 = blockIdx.y * LT_BM, n0 = blockIdx.x * LT_BN;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int tr = (warp >> 1) * 4 + (lane >> 3);  // rows m0 + 8 tr .. +8
+  const int tc = (warp & 1) * 8 + (lane & 7);    // columns n0 + 4 tc .. +4
+  float4 rx[2], rw;
+  auto gload = [&](int k0) {
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int c = tid + i * LT_THREADS, r = c >> 2, k = k0 + (c & 3) * 4;
+      rx[i] = (m0 + r < M && k < K) ? __ldg(reinterpret_cast<const float4*>(x + static_cast<long long>(m0 + r) * ldx + k))
+                                    : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    const int r = tid >> 2, k = k0 + (tid & 3) * 4;
+    rw = (n0 + r < N && k < K) ? __ldg(reinterpret_cast<const float4*>(w + static_cast<long long>(n0 + r) * ldw + k))
+                               : make_float4(0.f, 0.f, 0.f, 0.f);
+  };
+  auto sstore = [&](int st) {
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int c = tid + i * LT_THREADS, r = c >> 2, kq = (c & 3) * 4;
+      xs[st][kq][r] = rx[i].x, xs[st][kq + 1][r] = rx[i].y, xs[st][kq + 2][r] = rx[i].z, xs[st][kq + 3][r] = rx[i].w;
+    }
+    const int r = tid >> 2, kq = (tid & 3) * 4;
+    ws[st][kq][r] = rw.x, ws[st][kq + 1][r] = rw.y, ws[st][kq + 2][r] = rw.z, ws[st][kq + 3][r] = rw.w;
+  };
+  float acc[8][4];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+  const int nk = (K + LT_BK - 1) / LT_BK;
+  gload(0);
+  sstore(0);
+  __syncthreads();
+  for (int kc = 0; kc < nk; ++kc) {
+    const int st = kc & 1;
+    if (kc + 1 < nk) gload((kc + 1) * LT_BK);
+#pragma unroll
+    for (int kk = 0; kk < LT_BK; ++kk) {
+      const float4 a0 = *reinterpret_cast<const float4*>(&xs[st][kk][tr * 8]);
+      const float4 a1 = *reinterpret_cast<const float4*>(&xs[st][kk][tr * 8 + 4]);
+      const float4 b = *reinterpret_cast<const float4*>(&ws[st][kk][tc * 4]);
+      const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+      const float bv[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+    }
+    if (kc + 1 < nk) sstore(st ^ 1);  // that buffer was last read before the previous barrier
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int m = m0 + tr * 8 + i;
+    if (m >= M) continue;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int n = n0 + tc * 4 + j;
+      if (n >= N) continue;
+      float v = acc[i][j];
+      if (bias) v += bias[n];
+      if (bias2) v += bias2[n];
+      if (act == 2) v = v / (1.0f + expf(-v));  // SiLU of the output, full fp32 accuracy
+      y[static_cast<long long>(m) * ldy + n] = v;
+    }
+  }
+}
+
 // ------------------------------------------------------------------ expert head + Euler step
 // One block per row m: h = rms_norm(e[m]) in shared memory, then each warp computes output
 // columns n = warp, warp + 8, ... as warp-reduced dot products; x_t[m, n] += dt * (h . w_n + b_n).
@@ -279,6 +363,13 @@ extern "C" int so101_linear_f32(const float* x, int64_t ldx, const float* w, int
   if (!x || !w || !y || M <= 0 || N <= 0 || K <= 0 || ldx < K || ldw < K || ldy < N) return SO101_ERR_ARG;
   if (K % 4 || ldx % 4 || ldw % 4 || reinterpret_cast<uintptr_t>(x) % 16 || reinterpret_cast<uintptr_t>(w) % 16)
     return SO101_ERR_ARG;
+  if (M >= 512) {  // enough rows for register-blocked 128 x 64 tiles
+    const long long ty = (M + LT_BM - 1) / LT_BM, tx = (N + LT_BN - 1) / LT_BN;
+    if (ty > 65535 || tx > 0x7fffffffLL) return SO101_ERR_ARG;
+    return launch_kernel(linear_f32_tiled_kernel, dim3(static_cast<unsigned>(tx), static_cast<unsigned>(ty)),
+                         dim3(LT_THREADS), 0, stream, x, ldx, w, ldw, bias, bias2, y, ldy, static_cast<int>(M),
+                         static_cast<int>(N), static_cast<int>(K), act);
+  }
   const long long gy = (M + LF_BM - 1) / LF_BM, gx = (N + LF_BN - 1) / LF_BN;
   if (gy > 65535 || gx > 0x7fffffffLL) return SO101_ERR_ARG;
   return launch_kernel(linear_f32_kernel, dim3(dim3(static_cast<unsigned>(gx), static_cast<unsigned>(gy))), dim3(LF_THREADS), 0, stream,

@@ -159,6 +159,21 @@ def linear(
     return y.view(*x.shape[:-1], n)
 
 
+def linear_f32(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None, bias2: torch.Tensor | None = None,
+               silu: bool = False) -> torch.Tensor:
+    """y = x @ w.T (+ bias + bias2), then SiLU when `silu`, all in float32 on CUDA cores: the
+    action / time MLP of the velocity (pkg/model/smolvla.py:282-285). Sequential fmaf over k for
+    every output, so any row tiling gives the same bits."""
+    _cuda(x, w, bias, bias2)
+    m, k = x.shape
+    n = w.shape[0]
+    y = torch.empty(m, n, dtype=torch.float32, device=x.device)
+    L.check(L.lib().so101_linear_f32(x.data_ptr(), x.stride(0), w.data_ptr(), w.stride(0), _ptr(bias), _ptr(bias2),
+                                     y.data_ptr(), y.stride(0), m, n, k, 2 if silu else 0, _stream(x.device)),
+            "linear_f32")  # fmt: skip
+    return y
+
+
 def gemm_stat_slots(m: int, n: int, k: int, config=None) -> int:
     """Statistics slots a bf16 GEMM of this shape writes with `stat` (ValueError if none)."""
     got = C.c_int()

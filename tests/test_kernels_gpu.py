@@ -380,6 +380,27 @@ def test_layer_norm_and_pixel_shuffle():
     assert (shuf.float() - v).abs().max() <= 2**-7 * v.abs().max()
 
 
+@pytest.mark.parametrize("silu", [False, True])
+def test_linear_f32_tiles_agree_bit_for_bit(silu):
+    """The fp32 action/time MLP linear: many rows take the register-blocked 128 x 64 tiles, few rows
+    the latency kernel; both accumulate every output over k in order, so the first rows of a
+    3200-row call equal a 50-row call bit for bit, and both match float64 within fp32 rounding."""
+    from so101_smolvla_edge_b200.ops import linear_f32
+
+    x = rnd(3200, 720)
+    w = rnd(720, 720, scale=720**-0.5, seed=1)
+    b, b2 = rnd(720, seed=2), rnd(720, seed=3)
+    big = linear_f32(x, w, b, b2, silu=silu)
+    small = linear_f32(x[:50].contiguous(), w, b, b2, silu=silu)
+    assert torch.equal(big[:50], small)
+    want = x.double() @ w.double().T + b.double() + b2.double()
+    if silu:
+        want = want * torch.sigmoid(want)
+    assert (big.double() - want).abs().max() <= 1e-4 * want.abs().max()
+    odd = linear_f32(x[:1000, :32].contiguous(), w[:77, :32].contiguous())  # ragged tiles, short K
+    assert torch.allclose(odd.double(), x[:1000, :32].double() @ w[:77, :32].double().T, rtol=1e-5, atol=1e-5)
+
+
 # ------------------------------------------------------------------ RMSNorm finished in the GEMM
 def _rms_ref(x, w, eps):
     x = x.float()
