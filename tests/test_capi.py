@@ -98,3 +98,18 @@ def test_other_entry_points_validate_arguments(lib):
     assert lib.so101_preprocess(fake, 1, 10, 10, 10, 10, 100, 16, fake, L.BF16, 0.0, None) == L.ERR_ARG
     assert lib.so101_linear_f32(fake, 3, fake, 3, None, None, fake, 3, 2, 3, 3, 0, None) == L.ERR_ARG
     assert lib.so101_finish(fake, 8, fake, 6, fake, fake, fake, fake, fake, fake, fake, 6, 10, 3, 1, None) == L.ERR_ARG
+
+
+def test_tune_gemm_candidates():
+    """The plan sweep (the counterpart of the reference's scripts/tune_gemm.py) offers the pick,
+    weight-streaming swap tiles for few rows (not for int8, which has no swap tiles) and the
+    token-tile kernels (one tile per CTA with K splits, persistent, CTA pair) for many rows."""
+    from so101_smolvla_edge_b200 import _lib as L
+    from so101_smolvla_edge_b200.tune_gemm import SHAPES, candidates
+
+    few = candidates(50, dual=False, int8=False)
+    assert few[0] is None and any(c and c[0] == 1 for c in few)
+    many = candidates(3072, dual=True, int8=True)
+    assert not any(c and c[0] == 1 for c in many)
+    assert any(c and c[4] == L.GEMM_PAIR for c in many) and all(c is None or c[1] <= 128 for c in many)
+    assert set(SHAPES) == {"expert", "prefix", "vision"}
