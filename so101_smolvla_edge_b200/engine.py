@@ -27,6 +27,7 @@ import json
 import logging
 import os
 import time
+from concurrent.futures import ThreadPoolExecutor
 from pathlib import Path
 
 import numpy as np
@@ -144,6 +145,11 @@ class Engine:
         self._host_state = torch.zeros(p.state.shape, dtype=torch.float32).pin_memory()
         self._host_noise = torch.zeros(p.noise.shape, dtype=torch.float32).pin_memory()
         self._host_out = torch.zeros(p.out.shape, dtype=torch.float32).pin_memory()
+        # batched staging: observation groups copied into pinned memory by helper threads (numpy
+        # copies release the GIL), each group's H2D issued as soon as its copy is done
+        self._stage_groups = [(g * self.batch // n, (g + 1) * self.batch // n)
+                              for n in [min(8, self.batch, os.cpu_count() or 1)] for g in range(n)]  # fmt: skip
+        self._pool = ThreadPoolExecutor(len(self._stage_groups)) if len(self._stage_groups) > 1 else None
         self.dt = -1.0 / s.n_steps
         self.timing = Timing()
         self._stages = [self._vision, self._prefix, self._denoise]
@@ -193,13 +199,24 @@ class Engine:
 
     # ------------------------------------------------------------------ staging
     def _stage(self, images, states, noises) -> None:
-        """Host observations -> pinned buffers -> device (async on the current stream)."""
+        """Host observations -> pinned buffers -> device (async on the current stream). The
+        previous call synchronized its stream, so the pinned buffers are free to overwrite."""
         B, C_ = self.batch, len(self.cams)
         hi = self._host_img.numpy()
-        for bi in range(B):
-            for ci, c in enumerate(self.cams):
-                hi[bi * C_ + ci] = images[bi][c]
-        self.img.copy_(self._host_img, non_blocking=True)
+
+        def fill(b0: int, b1: int) -> None:
+            for bi in range(b0, b1):
+                for ci, c in enumerate(self.cams):
+                    hi[bi * C_ + ci] = images[bi][c]
+
+        if self._pool is None:
+            fill(0, B)
+            self.img.copy_(self._host_img, non_blocking=True)
+        else:
+            futures = [self._pool.submit(fill, b0, b1) for b0, b1 in self._stage_groups]
+            for (b0, b1), f in zip(self._stage_groups, futures, strict=True):
+                f.result()
+                self.img[b0 * C_ : b1 * C_].copy_(self._host_img[b0 * C_ : b1 * C_], non_blocking=True)
         self._host_state.numpy()[:] = np.asarray(states, np.float32).reshape(B, self.state_dim)
         self.state.copy_(self._host_state, non_blocking=True)
         if noises is None:
