@@ -200,22 +200,33 @@ __device__ __forceinline__ void attention_body(const AttnArgs& a, int split, int
         mma_bf16_16816(s[2 * t2 + 1], qf[kk], b2, b3);
       }
     }
-    // scale, mask, row max
+    // scale, mask, row max. A tile whose keys all precede causal_from and Lk is visible to every
+    // query (most of the prefix and expert tiles): no per-element mask there, same values.
     const int j0 = (t_begin + tile) * BN;
     float mx0 = -INFINITY, mx1 = -INFINITY;
+    if (j0 + BN <= a.Lk && j0 + BN <= a.causal_from) {
 #pragma unroll
-    for (int t = 0; t < BN / 8; ++t) {
+      for (int t = 0; t < BN / 8; ++t) {
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const long long j = j0 + t * 8 + (lane & 3) * 2 + (e & 1);
-        const long long i = e < 2 ? r0 : r1;
-        const bool vis = j < a.Lk && (j < a.causal_from || j <= i + a.q_offset);
-        const float x = vis ? s[t][e] * a.scale_log2 : -INFINITY;
-        s[t][e] = x;
-        if (e < 2)
-          mx0 = fmaxf(mx0, x);
-        else
-          mx1 = fmaxf(mx1, x);
+        for (int e = 0; e < 4; ++e) s[t][e] *= a.scale_log2;
+        mx0 = fmaxf(mx0, fmaxf(s[t][0], s[t][1]));
+        mx1 = fmaxf(mx1, fmaxf(s[t][2], s[t][3]));
+      }
+    } else {
+#pragma unroll
+      for (int t = 0; t < BN / 8; ++t) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const long long j = j0 + t * 8 + (lane & 3) * 2 + (e & 1);
+          const long long i = e < 2 ? r0 : r1;
+          const bool vis = j < a.Lk && (j < a.causal_from || j <= i + a.q_offset);
+          const float x = vis ? s[t][e] * a.scale_log2 : -INFINITY;
+          s[t][e] = x;
+          if (e < 2)
+            mx0 = fmaxf(mx0, x);
+          else
+            mx1 = fmaxf(mx1, x);
+        }
       }
     }
     mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
