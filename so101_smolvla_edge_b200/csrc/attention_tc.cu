@@ -65,11 +65,6 @@ __host__ __device__ constexpr uint32_t idesc_attn(int n, int b_mn) {
          (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(128 >> 4) << 24);
 }
 
-__device__ __forceinline__ float ex2(float x) {
-  float y;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
 
 // Two floats rounded to bf16 (nearest even) and packed, the first in the low half.
 __device__ __forceinline__ uint32_t bf16x2(float lo, float hi) {

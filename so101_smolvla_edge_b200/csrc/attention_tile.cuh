@@ -236,15 +236,15 @@ __device__ __forceinline__ void attention_body(const AttnArgs& a, int split, int
     const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
     const float base0 = mn0 == -INFINITY ? 0.f : mn0;
     const float base1 = mn1 == -INFINITY ? 0.f : mn1;
-    const float al0 = exp2f(m0 - base0), al1 = exp2f(m1 - base1);
+    const float al0 = ex2(m0 - base0), al1 = ex2(m1 - base1);
     m0 = mn0;
     m1 = mn1;
     float ps0 = 0.f, ps1 = 0.f;
     uint32_t pf[BN / 16][4];
 #pragma unroll
     for (int t = 0; t < BN / 8; ++t) {
-      const float p0 = exp2f(s[t][0] - base0), p1 = exp2f(s[t][1] - base0);
-      const float p2 = exp2f(s[t][2] - base1), p3 = exp2f(s[t][3] - base1);
+      const float p0 = ex2(s[t][0] - base0), p1 = ex2(s[t][1] - base0);
+      const float p2 = ex2(s[t][2] - base1), p3 = ex2(s[t][3] - base1);
       ps0 += p0 + p1;
       ps1 += p2 + p3;
       pf[t / 2][(t & 1) * 2 + 0] = pack_bf16(p0, p1);

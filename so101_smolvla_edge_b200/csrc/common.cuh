@@ -442,6 +442,13 @@ __device__ __forceinline__ float2 fmul2(float2 a, float2 b) {
   return d;
 }
 
+// 2^x on the MUFU unit (PTX ex2.approx.ftz: subnormal inputs and results flush to zero).
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 // gelu_tanh_fast on a pair, packed; same operations in the same order, same results.
 __device__ __forceinline__ float2 gelu_tanh_fast2(float2 x) {
   const float2 p = ffma2(fmul2(x, x), make_float2(0.7978845608028654f * 0.044715f, 0.7978845608028654f * 0.044715f),
