@@ -96,7 +96,8 @@ typedef struct so101_epilogue {
 /* Tile configuration; zero-initialised fields mean "pick" (the heuristic of so101_gemm_pick). */
 typedef struct so101_gemm_config {
   int swap;    /* 1: weights on the MMA M side (few token rows), 0: tokens on the M side */
-  int bn;      /* MMA N: 16, 32, 48, 64 (swap) or 64, 128, 256 (tokens on M)             */
+  int bn;      /* MMA N: 16, 32, 48, 64 (swap) or 64, 128, 256, 192 (tokens on M; 192:   */
+               /* persistent kernel only, no SiLU gate)                                  */
   int splits;  /* K splits, reduced in split order (deterministic)                        */
   int stages;  /* shared-memory pipeline depth (0: chosen from the problem)               */
   int flags;   /* SO101_GEMM_* bits                                                       */

@@ -1323,8 +1323,8 @@ int plan_gemm(int a_type, long long M, long long N, long long K, int epi, const 
     if (c.bn != 16 && c.bn != 32 && c.bn != 48 && c.bn != 64) return SO101_ERR_ARG;
     if (a_type == SO101_I8) return SO101_ERR_ARG;
   } else {
-    if (c.bn != 64 && c.bn != 128 && c.bn != 256) return SO101_ERR_ARG;
-    if (dual && c.bn == 256) return SO101_ERR_ARG;
+    if (c.bn != 64 && c.bn != 128 && c.bn != 192 && c.bn != 256) return SO101_ERR_ARG;
+    if (dual && c.bn >= 192) return SO101_ERR_ARG;
   }
   pl->kb_total = ceil_div(K, kb_elems);
   const int splits = c.splits > pl->kb_total ? pl->kb_total : c.splits;
@@ -1344,6 +1344,7 @@ int plan_gemm(int a_type, long long M, long long N, long long K, int epi, const 
            ((c.flags & SO101_GEMM_PERSISTENT) || tiles >= sm_count()))
     pl->kind = kPersistent;
   if (!pair) c.flags &= ~SO101_GEMM_PAIR;
+  if (c.bn == 192 && pl->kind != kPersistent) return SO101_ERR_ARG;
   pl->cluster = 1;
   if (pl->kind == kTile && pl->splits > 1 && pl->splits <= kMaxCluster && !(c.flags & SO101_GEMM_GLOBAL_SPLITK))
     pl->cluster = pl->splits;
@@ -1474,6 +1475,10 @@ int launch_bn(const CUtensorMap& tx, const CUtensorMap& tw, const GemmArgs& a, c
       case 128:
         return pers ? launch_persistent<128, DUAL, I8>(tx, tw, a, pl, stream, pdl)
                     : launch_tile<128, SWAP, DUAL, I8>(tx, tw, a, pl, stream, pdl);
+      case 192:  // persistent only: N = 720 in four tiles, 48 columns per epilogue warp
+        if constexpr (!DUAL)
+          if (pers) return launch_persistent<192, DUAL, I8>(tx, tw, a, pl, stream, pdl);
+        break;
       case 256:
         if constexpr (!DUAL)
           return pers ? launch_persistent<256, DUAL, I8>(tx, tw, a, pl, stream, pdl)
