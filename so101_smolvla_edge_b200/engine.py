@@ -27,6 +27,7 @@ import json
 import logging
 import os
 import time
+import weakref
 from concurrent.futures import ThreadPoolExecutor
 from pathlib import Path
 
@@ -150,6 +151,8 @@ class Engine:
         self._stage_groups = [(g * self.batch // n, (g + 1) * self.batch // n)
                               for n in [min(8, self.batch, os.cpu_count() or 1)] for g in range(n)]  # fmt: skip
         self._pool = ThreadPoolExecutor(len(self._stage_groups)) if len(self._stage_groups) > 1 else None
+        if self._pool is not None:  # the helper threads end with the engine
+            weakref.finalize(self, self._pool.shutdown, wait=False)
         self.dt = -1.0 / s.n_steps
         self.timing = Timing()
         self._stages = [self._vision, self._prefix, self._denoise]
