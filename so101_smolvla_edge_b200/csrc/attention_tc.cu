@@ -49,12 +49,18 @@ constexpr float kStaleMax = 8.f;               // log2 of the largest factor a s
 constexpr int kPolyPairs = SO101_ATTN_POLY_PAIRS;
 
 // smem offsets (from a 1024-aligned base)
-constexpr int kStages = 4;
+#ifndef SO101_ATTN_STAGES
+#define SO101_ATTN_STAGES 4
+#endif
+constexpr int kStages = SO101_ATTN_STAGES;  // K and V ring depth (16 KB per stage each)
 constexpr int kOffQ = 0;                              // 2 groups x 16 KB
 constexpr int kOffK = kOffQ + 2 * kTcTile;            // kStages x 16 KB
 constexpr int kOffV = kOffK + kStages * kTcTile;      // kStages x 16 KB
 constexpr int kOffBar = kOffV + kStages * kTcTile;
-constexpr int kTcSmem = kOffBar + 256 + 1024;
+constexpr int kBarBytes = 512;  // q_full, 4 x kStages ring barriers, 8 group barriers, TMEM slot
+static_assert((1 + 4 * kStages + 8) * 8 + 4 <= kBarBytes, "barrier region");
+constexpr int kTcSmem = kOffBar + kBarBytes + 1024;
+static_assert(kTcSmem <= 232448, "227 KB of shared memory per CTA");
 
 // TMEM columns: S_A, S_B (128 fp32 each), P_A, P_B (64 each: 128 bf16 keys in pairs), O_A, O_B (64)
 constexpr uint32_t kColS = 0, kColP = 256, kColO = 384;
