@@ -153,6 +153,20 @@ SO101_API int so101_attention(const void* q, int64_t ldq, const void* k, int64_t
                     const float* cos, const float* sin, int batch, int64_t bq, int64_t bk,
                     int64_t bv, int64_t bo, cudaStream_t stream);
 
+/* so101_attention where keys j >= own_from (and their values) are the current step's own rows,
+ * read from row j - own_from of k_own / v_own (row stride ld_own, batch stride b_own: the fused
+ * q|k|v output) instead of k / v, and rotated on chip by k_cos / k_sin (row j - own_from, hd/2
+ * columns) exactly as so101_rope_kv rotates cache rows. Replaces the rope_kv launch that writes the
+ * expert's own rows into the K/V cache before each self-attention (kernels/rope.py:17-66 followed
+ * by kernels/attention.py:27-120). hd 64; k_own, v_own 16-byte aligned. */
+SO101_API int so101_attention_rows(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v,
+                                   int64_t ldv, void* o, int64_t ldo, int o_type, float o_qscale, int64_t Lq,
+                                   int64_t Lk, int nq, int nkv, int hd, int64_t causal_from, int64_t q_offset,
+                                   const float* cos, const float* sin, int batch, int64_t bq, int64_t bk,
+                                   int64_t bv, int64_t bo, const void* k_own, const void* v_own, int64_t ld_own,
+                                   int64_t b_own, int64_t own_from, const float* k_cos, const float* k_sin,
+                                   cudaStream_t stream);
+
 /* y (rows x n) = x * rsqrt(mean(x^2) + eps) * w, statistics in fp32, one rounding to y_type.
  * x_type SO101_F32 or SO101_BF16. Replaces kernels/norm.py:14-42 and model/smolvla.py:72-74. */
 SO101_API int so101_rms_norm(const void* x, int64_t ldx, int x_type, const float* w, void* y,

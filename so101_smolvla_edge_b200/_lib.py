@@ -94,6 +94,8 @@ SIGNATURES = {
                              C.POINTER(C.c_int64)],
     "so101_attention": [P, I64, P, I64, P, I64, P, I64, I, F, I64, I64, I, I, I, I64, I64, P, P, I,
                         I64, I64, I64, I64, S],
+    "so101_attention_rows": [P, I64, P, I64, P, I64, P, I64, I, F, I64, I64, I, I, I, I64, I64, P, P, I,
+                             I64, I64, I64, I64, P, P, I64, I64, I64, P, P, S],
     "so101_rms_norm": [P, I64, I, P, P, I64, I, I64, I64, F, S],
     "so101_layer_norm": [P, I64, P, P, P, I64, I, F, I64, I64, F, I, I64, S],
     "so101_rope_kv": [P, I64, I, I, I, P, P, P, I64, P, I64, I64, I, I64, I64, I64, S],

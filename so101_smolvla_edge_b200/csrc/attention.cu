@@ -47,11 +47,20 @@ int attention_tc_launch(const void* q, long long ldq, const void* k, long long l
 
 using namespace so101;
 
-extern "C" int so101_attention(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v, int64_t ldv,
-                               void* o, int64_t ldo, int o_type, float o_qscale, int64_t Lq, int64_t Lk, int nq,
-                               int nkv, int hd, int64_t causal_from, int64_t q_offset, const float* cos,
-                               const float* sin, int batch, int64_t bq, int64_t bk, int64_t bv, int64_t bo,
-                               cudaStream_t stream) {
+namespace {
+
+struct OwnRows {
+  const void* k;
+  const void* v;
+  int64_t ld, b, from;
+  const float* cos;
+  const float* sin;
+};
+
+int attention_impl(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v, int64_t ldv, void* o,
+                   int64_t ldo, int o_type, float o_qscale, int64_t Lq, int64_t Lk, int nq, int nkv, int hd,
+                   int64_t causal_from, int64_t q_offset, const float* cos, const float* sin, int batch, int64_t bq,
+                   int64_t bk, int64_t bv, int64_t bo, const OwnRows& own, cudaStream_t stream) {
   if (!q || !k || !v || !o || Lq <= 0 || Lk <= 0 || nq <= 0 || nkv <= 0 || nq % nkv || batch <= 0) return SO101_ERR_ARG;
   if (hd != 32 && hd != 64 && hd != 128) return SO101_ERR_ARG;
   if ((cos == nullptr) != (sin == nullptr)) return SO101_ERR_ARG;
@@ -66,7 +75,14 @@ extern "C" int so101_attention(const void* q, int64_t ldq, const void* k, int64_
   // q rows and the rotary tables are read in 16-byte pieces
   if (reinterpret_cast<uintptr_t>(q) % 16 || (ldq * 2) % 16 || (bq * 2) % 16) return SO101_ERR_ARG;
   if (cos && (reinterpret_cast<uintptr_t>(cos) % 16 || reinterpret_cast<uintptr_t>(sin) % 16)) return SO101_ERR_ARG;
-  if (attention_tc_eligible(q, ldq, k, ldk, v, ldv, Lq, Lk, nq, nkv, hd, causal_from, cos, bq, bk, bv, o_type) &&
+  if (own.k) {  // the step's own keys and values from the fused qkv rows, keys rotated on chip
+    if (!own.v || !own.cos || !own.sin || own.from < 0 || own.from > Lk || hd != 64) return SO101_ERR_ARG;
+    if (reinterpret_cast<uintptr_t>(own.k) % 16 || reinterpret_cast<uintptr_t>(own.v) % 16 || (own.ld * 2) % 16 ||
+        (own.b * 2) % 16)
+      return SO101_ERR_ARG;
+  }
+  if (!own.k &&
+      attention_tc_eligible(q, ldq, k, ldk, v, ldv, Lq, Lk, nq, nkv, hd, causal_from, cos, bq, bk, bv, o_type) &&
       ldo % 8 == 0 && bo == Lq * ldo && reinterpret_cast<uintptr_t>(o) % 16 == 0)
     return attention_tc_launch(q, ldq, k, ldk, v, ldv, o, ldo, o_type, o_qscale, Lq, nq, batch, stream);
   AttnArgs a;
@@ -93,6 +109,13 @@ extern "C" int so101_attention(const void* q, int64_t ldq, const void* k, int64_
   a.cos = cos;
   a.sin = sin;
   a.scale_log2 = static_cast<float>(1.4426950408889634 / sqrt(static_cast<double>(hd)));
+  a.k_own = static_cast<const __nv_bfloat16*>(own.k);
+  a.v_own = static_cast<const __nv_bfloat16*>(own.v);
+  a.ld_own = own.ld;
+  a.b_own = own.b;
+  a.own_from = own.from;
+  a.k_cos = own.cos;
+  a.k_sin = own.sin;
   // few CTAs (the expert's 50 queries, the 241-row prefix): split the key tiles over a cluster
   {
     long long last = causal_from - 1;
@@ -115,4 +138,27 @@ extern "C" int so101_attention(const void* q, int64_t ldq, const void* k, int64_
     case 64: return launch_attention<64>(a, batch, stream);
     default: return launch_attention<128>(a, batch, stream);
   }
+}
+
+}  // namespace
+
+extern "C" int so101_attention(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v, int64_t ldv,
+                               void* o, int64_t ldo, int o_type, float o_qscale, int64_t Lq, int64_t Lk, int nq,
+                               int nkv, int hd, int64_t causal_from, int64_t q_offset, const float* cos,
+                               const float* sin, int batch, int64_t bq, int64_t bk, int64_t bv, int64_t bo,
+                               cudaStream_t stream) {
+  return attention_impl(q, ldq, k, ldk, v, ldv, o, ldo, o_type, o_qscale, Lq, Lk, nq, nkv, hd, causal_from, q_offset,
+                        cos, sin, batch, bq, bk, bv, bo, OwnRows{}, stream);
+}
+
+extern "C" int so101_attention_rows(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v, int64_t ldv,
+                                    void* o, int64_t ldo, int o_type, float o_qscale, int64_t Lq, int64_t Lk, int nq,
+                                    int nkv, int hd, int64_t causal_from, int64_t q_offset, const float* cos,
+                                    const float* sin, int batch, int64_t bq, int64_t bk, int64_t bv, int64_t bo,
+                                    const void* k_own, const void* v_own, int64_t ld_own, int64_t b_own,
+                                    int64_t own_from, const float* k_cos, const float* k_sin, cudaStream_t stream) {
+  if (!k_own) return SO101_ERR_ARG;
+  return attention_impl(q, ldq, k, ldk, v, ldv, o, ldo, o_type, o_qscale, Lq, Lk, nq, nkv, hd, causal_from, q_offset,
+                        cos, sin, batch, bq, bk, bv, bo, OwnRows{k_own, v_own, ld_own, b_own, own_from, k_cos, k_sin},
+                        stream);
 }

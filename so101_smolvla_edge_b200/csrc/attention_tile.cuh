@@ -32,6 +32,14 @@ struct AttnArgs {
   const float* sin;
   float scale_log2;
   int kv_splits;  // > 1: the key tiles are split over a cluster of this many CTAs
+  // Keys j >= own_from read row j - own_from of k_own / v_own (the step's own rows, straight from
+  // the fused qkv output, batch stride b_own) instead of k / v; those keys are rotated by
+  // k_cos / k_sin (row j - own_from) once they are in shared memory. k_own == nullptr: off.
+  const __nv_bfloat16* k_own = nullptr;
+  const __nv_bfloat16* v_own = nullptr;
+  long long ld_own = 0, b_own = 0, own_from = 0;
+  const float* k_cos = nullptr;
+  const float* k_sin = nullptr;
 };
 
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
@@ -91,6 +99,9 @@ __device__ __forceinline__ void attention_body(const AttnArgs& a, int split, int
   const __nv_bfloat16* Q = a.q + bi * a.bq + static_cast<long long>(h) * HD;
   const __nv_bfloat16* K = a.k + bi * a.bk + static_cast<long long>(kvh) * HD;
   const __nv_bfloat16* V = a.v + bi * a.bv + static_cast<long long>(kvh) * HD;
+  const bool own = a.k_own != nullptr;
+  const __nv_bfloat16* K_own = own ? a.k_own + bi * a.b_own + static_cast<long long>(kvh) * HD : nullptr;
+  const __nv_bfloat16* V_own = own ? a.v_own + bi * a.b_own + static_cast<long long>(kvh) * HD : nullptr;
 
   // last key any query of this block can see -> number of key tiles
   long long last = a.causal_from - 1;
@@ -110,8 +121,11 @@ __device__ __forceinline__ void attention_body(const AttnArgs& a, int split, int
       const int j = j0 + r;
       const bool ok = j < a.Lk;
       const long long jj = ok ? j : 0;
-      cp_async16(smem_u32(sK + buf * BN * LDS + r * LDS + cc * 8), K + jj * a.ldk + cc * 8, ok ? 16 : 0);
-      cp_async16(smem_u32(sV + buf * BN * LDS + r * LDS + cc * 8), V + jj * a.ldv + cc * 8, ok ? 16 : 0);
+      const bool mine = own && jj >= a.own_from;
+      const __nv_bfloat16* ks = mine ? K_own + (jj - a.own_from) * a.ld_own : K + jj * a.ldk;
+      const __nv_bfloat16* vs = mine ? V_own + (jj - a.own_from) * a.ld_own : V + jj * a.ldv;
+      cp_async16(smem_u32(sK + buf * BN * LDS + r * LDS + cc * 8), ks + cc * 8, ok ? 16 : 0);
+      cp_async16(smem_u32(sV + buf * BN * LDS + r * LDS + cc * 8), vs + cc * 8, ok ? 16 : 0);
     }
     cp_async_commit();
   };
@@ -182,6 +196,25 @@ __device__ __forceinline__ void attention_body(const AttnArgs& a, int split, int
       cp_async_wait<0>();
     }
     __syncthreads();
+    {
+      // the step's own keys in this tile, rotated in place as the RoPE K/V cache kernel would
+      // have written them (per-operation rounding, one rounding to bf16)
+      const long long j0 = static_cast<long long>(t_begin + tile) * BN;
+      if (own && j0 + BN > a.own_from) {
+        const int r_lo = static_cast<int>(a.own_from > j0 ? a.own_from - j0 : 0);
+        const int r_hi = static_cast<int>(a.Lk - j0 < BN ? a.Lk - j0 : BN);
+        __nv_bfloat16* kt = sK + buf * BN * LDS;
+        for (int idx = tid; idx < (r_hi - r_lo) * HALF; idx += 128) {
+          const int r = r_lo + idx / HALF, d = idx % HALF;
+          const long long jr = j0 + r - a.own_from;
+          const float k1 = __bfloat162float(kt[r * LDS + d]), k2 = __bfloat162float(kt[r * LDS + d + HALF]);
+          const float c = a.k_cos[jr * HALF + d], sn = a.k_sin[jr * HALF + d];
+          kt[r * LDS + d] = __float2bfloat16_rn(__fsub_rn(__fmul_rn(k1, c), __fmul_rn(k2, sn)));
+          kt[r * LDS + d + HALF] = __float2bfloat16_rn(__fadd_rn(__fmul_rn(k2, c), __fmul_rn(k1, sn)));
+        }
+        __syncthreads();
+      }
+    }
     const __nv_bfloat16* k_s = sK + buf * BN * LDS;
     const __nv_bfloat16* v_s = sV + buf * BN * LDS;
 

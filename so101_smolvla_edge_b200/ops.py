@@ -206,6 +206,7 @@ def attention(
     out: torch.Tensor | None = None,
     out_dtype: torch.dtype = torch.bfloat16,
     out_qscale: float | None = None,
+    own: tuple | None = None,
 ) -> torch.Tensor:
     """Attention of q's heads over k and v, written as (Lq, n_heads * hd).
 
@@ -213,7 +214,9 @@ def attention(
     so it can be a slice of the fused qkv output; k and v are (Lk, n_kv * hd). A leading batch
     dimension on all three runs independent problems. cos and sin (Lq, hd / 2) rotate q; None
     means no RoPE. Key j is visible to query i iff j < causal_from or j <= i + q_offset; None
-    means every key is visible.
+    means every key is visible. own=(k_own, v_own, own_from, k_cos, k_sin): keys j >= own_from and
+    their values come from row j - own_from of k_own / v_own (e.g. the fused qkv rows), the keys
+    rotated by k_cos / k_sin as the RoPE cache write would (so101_attention_rows).
     """
     _cuda(q, k, v, out)
     batched = q.dim() == 3
@@ -232,13 +235,21 @@ def attention(
         cos = cos.reshape(lq, hd // 2).float().contiguous()
         sin = sin.reshape(lq, hd // 2).float().contiguous()
     ck = lk if causal_from is None else causal_from
-    rc = L.lib().so101_attention(
-        qb.data_ptr(), qb.stride(1), kb.data_ptr(), kb.stride(1), vb.data_ptr(), vb.stride(1),
-        ob.data_ptr(), ob.stride(1), DTYPE[ob.dtype], out_qscale or 0.0, lq, lk, n_heads, n_kv, hd,
-        ck, q_offset, _ptr(cos), _ptr(sin), bsz, qb.stride(0), kb.stride(0), vb.stride(0),
-        ob.stride(0), _stream(q.device),
-    )  # fmt: skip
-    L.check(rc, "so101_attention")
+    args = (qb.data_ptr(), qb.stride(1), kb.data_ptr(), kb.stride(1), vb.data_ptr(), vb.stride(1),
+            ob.data_ptr(), ob.stride(1), DTYPE[ob.dtype], out_qscale or 0.0, lq, lk, n_heads, n_kv, hd,
+            ck, q_offset, _ptr(cos), _ptr(sin), bsz, qb.stride(0), kb.stride(0), vb.stride(0),
+            ob.stride(0))  # fmt: skip
+    if own is None:
+        L.check(L.lib().so101_attention(*args, _stream(q.device)), "so101_attention")
+    else:
+        k_own, v_own, own_from, k_cos, k_sin = own
+        ko = k_own if k_own.dim() == 3 else k_own[None]
+        vo = v_own if v_own.dim() == 3 else v_own[None]
+        if ko.stride(1) != vo.stride(1) or ko.stride(0) != vo.stride(0):
+            raise ValueError("k_own and v_own need the same strides (views of one fused buffer)")
+        L.check(L.lib().so101_attention_rows(*args, ko.data_ptr(), vo.data_ptr(), ko.stride(1), ko.stride(0),
+                                             own_from, k_cos.data_ptr(), k_sin.data_ptr(), _stream(q.device)),
+                "so101_attention_rows")  # fmt: skip
     return out
 
 

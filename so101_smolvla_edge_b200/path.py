@@ -388,12 +388,19 @@ class B200Path:
         return 1
 
     def _attn(self, prog, what, q, ldq, bq, k, ldk, bk, v, ldv, bv, o, ldo, bo, *, Lq, Lk, nq, nkv,
-              hd, causal_from, q_offset=0, cos=None, sin=None, batch=1, o_qscale=0.0):  # fmt: skip
+              hd, causal_from, q_offset=0, cos=None, sin=None, batch=1, o_qscale=0.0, own=None):  # fmt: skip
+        """One attention launch; own=(k_own, v_own, ld, batch stride, own_from, k_cos, k_sin) reads
+        keys and values from own_from on from the fused qkv rows and rotates those keys on chip."""
         o_type = L.I8 if o.dtype == torch.int8 else L.BF16
-        prog.add(what, self.lib.so101_attention, q, ldq, k, ldk, v, ldv, o.data_ptr() if
-                 isinstance(o, torch.Tensor) else o, ldo, o_type, o_qscale, Lq, Lk, nq, nkv, hd,
-                 causal_from, q_offset, None if cos is None else cos.data_ptr(),
-                 None if sin is None else sin.data_ptr(), batch, bq, bk, bv, bo)  # fmt: skip
+        args = (q, ldq, k, ldk, v, ldv, o.data_ptr() if isinstance(o, torch.Tensor) else o, ldo, o_type, o_qscale,
+                Lq, Lk, nq, nkv, hd, causal_from, q_offset, None if cos is None else cos.data_ptr(),
+                None if sin is None else sin.data_ptr(), batch, bq, bk, bv, bo)  # fmt: skip
+        if own is None:
+            prog.add(what, self.lib.so101_attention, *args)
+        else:
+            k_own, v_own, ld_own, b_own, own_from, k_cos, k_sin = own
+            prog.add(what, self.lib.so101_attention_rows, *args, k_own, v_own, ld_own, b_own, own_from,
+                     k_cos.data_ptr(), k_sin.data_ptr())  # fmt: skip
 
     def _rms(self, prog, what, x, w, y, rows):
         s = self.spec
@@ -547,14 +554,19 @@ class B200Path:
             if s.is_self_attn(i):
                 self._gemm(p, f"s{k}.{i}.qkv", self.h_e, w[pre + "qkv"], self.qkv_e, rms=rms)
                 bk = (L_ + H) * kv
-                own = L_ * kv * 2  # bytes to the step's own rows
-                p.add(f"s{k}.{i}.rope_kv", self.lib.so101_rope_kv, self.qkv_e.data_ptr(), qd, nq, nk, hd,
-                      w["cos_s"].data_ptr(), w["sin_s"].data_ptr(), self.ck[i].data_ptr() + own, kv,
-                      self.cv[i].data_ptr() + own, kv, H, B, H * qd, bk, bk)  # fmt: skip
+                own = None
+                if hd == 64:  # the step's own keys and values straight from the fused qkv rows
+                    k_own = self.qkv_e.data_ptr() + nq * hd * 2
+                    own = (k_own, k_own + nk * hd * 2, qd, H * qd, L_, w["cos_s"], w["sin_s"])
+                else:  # RoPE and the K/V cache rows in a separate launch
+                    off = L_ * kv * 2  # bytes to the step's own rows
+                    p.add(f"s{k}.{i}.rope_kv", self.lib.so101_rope_kv, self.qkv_e.data_ptr(), qd, nq, nk, hd,
+                          w["cos_s"].data_ptr(), w["sin_s"].data_ptr(), self.ck[i].data_ptr() + off, kv,
+                          self.cv[i].data_ptr() + off, kv, H, B, H * qd, bk, bk)  # fmt: skip
                 self._attn(p, f"s{k}.{i}.attn", self.qkv_e.data_ptr(), qd, H * qd, self.ck[i].data_ptr(),
                            kv, bk, self.cv[i].data_ptr(), kv, bk, self.attn_e, s.q_dim, H * s.q_dim,
                            Lq=H, Lk=L_ + H, nq=nq, nkv=nk, hd=hd, causal_from=L_, q_offset=L_,
-                           cos=w["cos_s"], sin=w["sin_s"], batch=B)  # fmt: skip
+                           cos=w["cos_s"], sin=w["sin_s"], batch=B, own=own)  # fmt: skip
             else:
                 qv = self.qkv_e[:, : s.q_dim]
                 self._gemm(p, f"s{k}.{i}.q", self.h_e, w[pre + "q"], qv, rms=rms)

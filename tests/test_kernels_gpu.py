@@ -319,6 +319,29 @@ def test_attention_gqa_batched(case):
     assert torch.equal(got, attention(q, k, v, nq, nkv, cos=cos, sin=sin, causal_from=cf, q_offset=qo))
 
 
+@pytest.mark.parametrize("batch", [1, 16])
+def test_attention_own_rows_equal_rope_cache_then_attention(batch):
+    """so101_attention_rows (the step's own keys and values read from the fused qkv rows, the keys
+    rotated on chip) gives the same bits as rope_kv writing them into the K/V cache followed by
+    attention over the cache: the action expert's self-attention. The cache's own rows hold
+    unrelated values for the fused call, so they are shown not to be read."""
+    from so101_smolvla_edge_b200.ops import attention, rope_kv
+
+    L_, H, nq, nk, hd = 241, 50, 15, 5, 64
+    qd = (nq + 2 * nk) * hd
+    qkv = rnd(batch, H, qd, dtype=torch.bfloat16, scale=2.0)
+    cache_k = rnd(batch, L_ + H, nk * hd, dtype=torch.bfloat16, seed=1)
+    cache_v = rnd(batch, L_ + H, nk * hd, dtype=torch.bfloat16, seed=2)
+    cos, sin = rope_tables(torch.arange(L_, L_ + H, device="cuda"), hd, 10000.0)
+    q = qkv[:, :, : nq * hd]
+    own = (qkv[:, :, nq * hd : (nq + nk) * hd], qkv[:, :, (nq + nk) * hd :], L_, cos, sin)
+    got = attention(q, cache_k, cache_v, nq, nk, cos=cos, sin=sin, causal_from=L_, q_offset=L_, own=own)
+    for b in range(batch):
+        rope_kv(qkv[b], nq, nk, cos, sin, cache_k[b, L_:], cache_v[b, L_:])
+    want = attention(q, cache_k, cache_v, nq, nk, cos=cos, sin=sin, causal_from=L_, q_offset=L_)
+    assert torch.equal(got, want)
+
+
 def test_attention_batched_and_strided():
     """A batch of independent problems with k and v as views into the fused qkv rows."""
     from so101_smolvla_edge_b200.ops import attention
