@@ -411,8 +411,15 @@ __device__ __forceinline__ float acc_value(uint32_t r) {
 }
 
 // ================================================================ one tile per CTA
+// 256 threads: warp 0 issues TMA, warp 1 the MMAs; in the epilogue every TMEM lane (row of the
+// 128-row tile) has two threads, one per half of the columns (warps 4-7 read the same lane
+// quadrants as warps 0-3), and the cluster reduction covers twice the items per DSMEM round trip.
+// Two CTAs fit per SM (at most 128 registers) except with the SiLU gate on swap tiles, whose two
+// accumulators' split partials need more registers and whose grids are small (M <= 64).
+constexpr int kTileThreads = 256;
+
 template <int BN, bool SWAP, bool DUAL, bool I8>
-__global__ void __launch_bounds__(128, 1)
+__global__ void __launch_bounds__(kTileThreads, (SWAP && DUAL) ? 1 : 2)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
                    const GemmArgs a, const int stages) {
   constexpr int NA = (SWAP && DUAL) ? 2 : 1;   // tiles on the MMA M side per stage
@@ -530,17 +537,19 @@ __global__ void __launch_bounds__(128, 1)
       // the tokens' RMSNorm scales, while the MMAs run (the producer's statistics are complete
       // once the previous grid is)
       const int count = SWAP ? BN : 128;
-      for (int i = threadIdx.x - 64; i < count; i += 64) rtab_s[i] = rbase + i < a.M ? rms_scale(a, rbase + i) : 1.f;
+      for (int i = threadIdx.x - 64; i < count; i += kTileThreads - 64)
+        rtab_s[i] = rbase + i < a.M ? rms_scale(a, rbase + i) : 1.f;
     }
   }
   __syncwarp();
 
-  // ---------------- epilogue: all 128 threads, thread t owns TMEM lane t (P index p0 + t)
+  // ---------------- epilogue: thread t owns TMEM lane tl = t % 128 (P index p0 + tl) and the
+  // 16-column chunks of parity hh = t / 128
   mbar_wait(accum, 0, a.status);
   tc_fence_after();
-  const int t = threadIdx.x;
-  const uint32_t lane_addr = tmem + (static_cast<uint32_t>(warp * 32) << 16);
-  const int p = p0 + t;
+  const int t = threadIdx.x, tl = t & 127, hh = t >> 7;
+  const uint32_t lane_addr = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
+  const int p = p0 + tl;
   const float* rtab = nullptr;
   if (a.rms_ss) {
     __syncthreads();  // rtab_s, written by warps 2-3 during the main loop
@@ -549,7 +558,7 @@ __global__ void __launch_bounds__(128, 1)
   float v[16], u[16];
   if (a.splits == 1) {
 #pragma unroll 1
-    for (int c = 0; c < BN; c += 16) {
+    for (int c = hh * 16; c < BN; c += 32) {
       uint32_t r0[16], r1[16];
       tmem_ld16(lane_addr + c, r0);
       if (DUAL) tmem_ld16(lane_addr + BN + c, r1);
@@ -565,12 +574,12 @@ __global__ void __launch_bounds__(128, 1)
     // stage this split's partial (column-major, lane contiguous) in the now idle stage ring
     float* part = reinterpret_cast<float*>(smem);
 #pragma unroll 1
-    for (int c = 0; c < NACC; c += 16) {
+    for (int c = hh * 16; c < NACC; c += 32) {
       uint32_t r[16];
       tmem_ld16(lane_addr + c, r);
       tmem_ld_wait();
 #pragma unroll
-      for (int j = 0; j < 16; ++j) part[(c + j) * 128 + t] = acc_value<I8>(r[j]);
+      for (int j = 0; j < 16; ++j) part[(c + j) * 128 + tl] = acc_value<I8>(r[j]);
     }
     cluster_sync();
     // CTA `rank` reduces row quads [rank*32/S, (rank+1)*32/S): per (quad, column) one 16-byte DSMEM
@@ -587,15 +596,15 @@ __global__ void __launch_bounds__(128, 1)
       // output may alias the residual, so the compiler could not reorder them itself
       const int total = nq * BN;
       if (a.stat_ss) {
-        for (int i = t; i < BN * 32; i += 128) stat_red[i] = 0.f;
+        for (int i = t; i < BN * 32; i += kTileThreads) stat_red[i] = 0.f;
         __syncthreads();
       }
-      for (int base = 0; base < total; base += 2 * 128) {
+      for (int base = 0; base < total; base += 2 * kTileThreads) {
         float4 pv[2][kMaxSplitCluster], pu[2][DUAL ? kMaxSplitCluster : 1], bia[2], res[2];
         int ok[2], col[2], quad[2];
 #pragma unroll
         for (int it = 0; it < 2; ++it) {
-          const int idx = base + it * 128 + t;
+          const int idx = base + it * kTileThreads + t;
           ok[it] = idx < total;
           quad[it] = qlo + (ok[it] ? idx % nq : 0);
           col[it] = ok[it] ? idx / nq : 0;
@@ -683,7 +692,7 @@ __global__ void __launch_bounds__(128, 1)
         }
       }
     } else {
-      for (int idx = t; idx < nq * BN; idx += 128) {
+      for (int idx = t; idx < nq * BN; idx += kTileThreads) {
         const int quad = qlo + idx % nq, col = idx / nq;
         const uint32_t off = static_cast<uint32_t>((col * 128 + quad * 4) * 4);
         const uint32_t off_u = static_cast<uint32_t>(((BN + col) * 128 + quad * 4) * 4);
@@ -719,12 +728,12 @@ __global__ void __launch_bounds__(128, 1)
     uint32_t* ws = static_cast<uint32_t*>(a.ws);
     uint32_t* part = ws + (static_cast<size_t>(tile) * a.splits + split) * NACC * 128;
 #pragma unroll 1
-    for (int c = 0; c < NACC; c += 16) {
+    for (int c = hh * 16; c < NACC; c += 32) {
       uint32_t r[16];
       tmem_ld16(lane_addr + c, r);
       tmem_ld_wait();
 #pragma unroll
-      for (int j = 0; j < 16; ++j) __stcg(part + (c + j) * 128 + t, r[j]);
+      for (int j = 0; j < 16; ++j) __stcg(part + (c + j) * 128 + tl, r[j]);
     }
     __threadfence();
     __syncthreads();
@@ -737,7 +746,7 @@ __global__ void __launch_bounds__(128, 1)
       __threadfence();
       const uint32_t* base = ws + static_cast<size_t>(tile) * a.splits * NACC * 128;
 #pragma unroll 1
-      for (int c = 0; c < BN; c += 16) {
+      for (int c = hh * 16; c < BN; c += 32) {
         if (I8) {
           int iv[16], iu[16];
 #pragma unroll
@@ -746,8 +755,8 @@ __global__ void __launch_bounds__(128, 1)
             const uint32_t* ps = base + static_cast<size_t>(s) * NACC * 128;
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
-              iv[j] += static_cast<int>(__ldcg(ps + (c + j) * 128 + t));
-              if (DUAL) iu[j] += static_cast<int>(__ldcg(ps + (BN + c + j) * 128 + t));
+              iv[j] += static_cast<int>(__ldcg(ps + (c + j) * 128 + tl));
+              if (DUAL) iu[j] += static_cast<int>(__ldcg(ps + (BN + c + j) * 128 + tl));
             }
           }
 #pragma unroll
@@ -764,8 +773,8 @@ __global__ void __launch_bounds__(128, 1)
             const uint32_t* ps = base + static_cast<size_t>(s) * NACC * 128;
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
-              pv[j] = __uint_as_float(__ldcg(ps + (c + j) * 128 + t));
-              pu[j] = DUAL ? __uint_as_float(__ldcg(ps + (BN + c + j) * 128 + t)) : 0.f;
+              pv[j] = __uint_as_float(__ldcg(ps + (c + j) * 128 + tl));
+              pu[j] = DUAL ? __uint_as_float(__ldcg(ps + (BN + c + j) * 128 + tl)) : 0.f;
             }
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
@@ -1406,7 +1415,7 @@ int launch_tile(const CUtensorMap& tx, const CUtensorMap& tw, const GemmArgs& a,
                 bool pdl) {
   static int configured = 0;
   const int smem = pl.cfg.stages * stage_bytes(BN, SWAP, DUAL) + 1024 + 256 + kTileScratch;
-  return launch(gemm_tc_kernel<BN, SWAP, DUAL, I8>, tx, tw, a, dim3(pl.tiles_q, pl.tiles_p, pl.splits), 128, smem,
+  return launch(gemm_tc_kernel<BN, SWAP, DUAL, I8>, tx, tw, a, dim3(pl.tiles_q, pl.tiles_p, pl.splits), kTileThreads, smem,
                 pl.cluster, pl.cfg.stages, stream, pdl, &configured);
 }
 
