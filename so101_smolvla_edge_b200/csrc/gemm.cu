@@ -614,7 +614,7 @@ __global__ void __launch_bounds__(kTileThreads, (SWAP && DUAL) ? 1 : 2)
           const uint32_t off_u = static_cast<uint32_t>(((BN + col[it]) * 128 + quad[it] * 4) * 4);
 #pragma unroll
           for (int sp = 0; sp < kMaxSplitCluster; ++sp) {
-            if (sp < S) {
+            if (sp < S && ok[it]) {  // padding tokens and features: nothing to load
               pv[it][sp] = ld_cluster_f32x4(peer[sp] + off);
               if constexpr (DUAL) pu[it][sp] = ld_cluster_f32x4(peer[sp] + off_u);
             }
