@@ -1511,10 +1511,13 @@ extern "C" int so101_gemm_pick(int a_type, int64_t M, int64_t N, int64_t K, int 
   const int sms = sm_count();
   so101_gemm_config c = {0, 0, 1, 0, 0};
   if (M <= 64 && a_type == SO101_BF16) {
-    // weight streaming: one 128-row weight slab per CTA, K split across a cluster to fill the GPU
+    // weight streaming: one 128-row weight slab per CTA, K split across a cluster to fill the GPU.
+    // More than 32 rows go in two 32-token tiles: each CTA then reduces half the split-K partials
+    // (the reduction through distributed shared memory bounds these GEMMs), and the second token
+    // tile re-reads its weight slab from L2.
     c.swap = 1;
-    c.bn = M <= 16 ? 16 : M <= 32 ? 32 : M <= 48 ? 48 : 64;
-    const int tiles = static_cast<int>((N + 127) / 128);
+    c.bn = M <= 16 ? 16 : 32;
+    const int tiles = static_cast<int>((N + 127) / 128) * static_cast<int>((M + c.bn - 1) / c.bn);
     int s = sms / tiles;
     if (s > kMaxCluster) s = kMaxCluster;
     const int max_s = kb / 3 > 0 ? kb / 3 : 1;  // at least three K blocks per split

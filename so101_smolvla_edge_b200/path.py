@@ -41,7 +41,11 @@ STAT_SLOTS = 64  # statistics slots per row for the RMSNorm finished in a GEMM (
 TUNE_CANDIDATES = (None, (0, 256, 1, 0, L.GEMM_PERSISTENT), (0, 192, 1, 0, L.GEMM_PERSISTENT),
                    (0, 128, 1, 0, L.GEMM_PERSISTENT), (0, 256, 1, 0, L.GEMM_PAIR),
                    (0, 128, 1, 0, L.GEMM_PAIR))  # fmt: skip
-TUNE_MIN_ROWS = 1024  # fewer rows: weight-streaming tiles, whose pick is kept
+TUNE_MIN_ROWS = 1024  # token-tile candidates from this many rows on
+# Weight-streaming plans for at most 64 token rows (the expert at batch 1): 32- and 64-token
+# tiles with 2-8 K splits over a cluster.
+TUNE_SMALL = (None,) + tuple((1, bn, s, 0, 0) for bn in (32, 64) for s in (2, 3, 4, 6, 8))
+TUNE_SMALL_ROWS = 64
 TUNE_MARGIN = 0.97  # a candidate replaces the pick only when at least 3% faster
 
 
@@ -160,9 +164,9 @@ class B200Path:
         self._build_denoise(self.progs["denoise"])
 
     def autotune(self, reps: int = 5) -> dict[str, dict]:
-        """Time every candidate plan (TUNE_CANDIDATES) of each distinct GEMM with many token rows
-        on this GPU, on its first launch site's own buffers, and rebuild the programs with the
-        fastest. The B200 counterpart of the reference's autotuned GEMMs (`compile="autotune"`,
+        """Time every candidate plan (TUNE_CANDIDATES; TUNE_SMALL for at most 64 rows) of each
+        distinct GEMM with many or few token rows on this GPU, on its first launch site's own
+        buffers, and rebuild the programs with the fastest. The B200 counterpart of the reference's autotuned GEMMs (`compile="autotune"`,
         pkg/model/engine.py:219-233, and `scripts/tune_gemm.py`). Rebuilding matters: a residual
         GEMM's plan sets how many statistics slots the next norm's GEMM reads. Overwrites the
         work buffers (the next chunk recomputes them). Returns {site: {"plan", "ms"}}."""
@@ -170,7 +174,7 @@ class B200Path:
         report: dict[str, dict] = {}
         for key, (what, args) in self._sites.items():
             times: dict[tuple | None, float] = {}
-            for cand in TUNE_CANDIDATES:
+            for cand in (TUNE_SMALL if key[1] <= TUNE_SMALL_ROWS else TUNE_CANDIDATES):
                 cfg = None if cand is None else L.GemmConfig(*cand)
                 a = list(args)
                 a[12] = None if cfg is None else C.byref(cfg)
@@ -375,7 +379,7 @@ class B200Path:
                 DTYPE[y.dtype], m, n, k, C.byref(epi), cfg_ref, self.ws.partials.data_ptr(), self.ws.nbytes,
                 self.ws.tickets.data_ptr(), self.ws.tickets.numel())  # fmt: skip
         prog.add(what, self.lib.so101_gemm, *args, keep=(epi, cfg))
-        if m >= TUNE_MIN_ROWS and key not in self._sites:
+        if (m >= TUNE_MIN_ROWS or (m <= TUNE_SMALL_ROWS and a_type == L.BF16)) and key not in self._sites:
             self._sites[key] = (what, args)
         if stat is not None and slots_out == 0:
             slots_out = self._stats(prog, f"{what}.stats", y, stat[2], stat[1], stat[0])

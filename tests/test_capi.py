@@ -78,11 +78,11 @@ def test_split_k_plans_report_their_workspace(lib):
 
 
 def test_gemm_pick_heuristic(lib):
-    """Few token rows stream weights (swap tiling, split over a cluster of at most 8); many rows
-    put tokens on the MMA M side with one split."""
+    """Few token rows stream weights (swap tiling in 32-token tiles, split over a cluster of at
+    most 8); many rows put tokens on the MMA M side with one split."""
     cfg = L.GemmConfig()
     assert lib.so101_gemm_pick(L.BF16, 50, 4096, 720, L.EPI_SILU_GATE, C.byref(cfg)) == L.OK
-    assert cfg.swap == 1 and cfg.bn == 64 and 1 <= cfg.splits <= 8
+    assert cfg.swap == 1 and cfg.bn == 32 and 1 <= cfg.splits <= 8
     assert lib.so101_gemm_pick(L.I8, 196608, 3072, 768, L.EPI_GELU, C.byref(cfg)) == L.OK
     assert cfg.swap == 0 and cfg.bn == 256 and cfg.splits == 1
 
