@@ -42,10 +42,10 @@ TUNE_CANDIDATES = (None, (0, 256, 1, 0, L.GEMM_PERSISTENT), (0, 192, 1, 0, L.GEM
                    (0, 128, 1, 0, L.GEMM_PERSISTENT), (0, 256, 1, 0, L.GEMM_PAIR),
                    (0, 128, 1, 0, L.GEMM_PAIR))  # fmt: skip
 TUNE_MIN_ROWS = 1024  # token-tile candidates from this many rows on
-# Weight-streaming plans for at most 64 token rows (the expert at batch 1): 32- and 64-token
-# tiles with 2-8 K splits over a cluster.
-TUNE_SMALL = (None,) + tuple((1, bn, s, 0, 0) for bn in (32, 64) for s in (2, 3, 4, 6, 8))
-TUNE_SMALL_ROWS = 64
+# Weight-streaming plans for at most 256 token rows (the expert and the prefix at batch 1): 32- and
+# 64-token tiles with 1-8 K splits over a cluster.
+TUNE_SMALL = (None,) + tuple((1, bn, s, 0, 0) for bn in (32, 64) for s in (1, 2, 3, 4, 6, 8))
+TUNE_SMALL_ROWS = 256
 TUNE_MARGIN = 0.97  # a candidate replaces the pick only when at least 3% faster
 
 
@@ -164,7 +164,7 @@ class B200Path:
         self._build_denoise(self.progs["denoise"])
 
     def autotune(self, reps: int = 5) -> dict[str, dict]:
-        """Time every candidate plan (TUNE_CANDIDATES; TUNE_SMALL for at most 64 rows) of each
+        """Time every candidate plan (TUNE_CANDIDATES; TUNE_SMALL for at most 256 rows) of each
         distinct GEMM with many or few token rows on this GPU, on its first launch site's own
         buffers, and rebuild the programs with the fastest. The B200 counterpart of the reference's autotuned GEMMs (`compile="autotune"`,
         pkg/model/engine.py:219-233, and `scripts/tune_gemm.py`). Rebuilding matters: a residual
