@@ -318,7 +318,6 @@ __device__ __forceinline__ void attention_body(const AttnArgs& a, int split, int
     constexpr int LDO = HD + 4;
     float* sO = reinterpret_cast<float*>(sK);
     float* sML = reinterpret_cast<float*>(sQ);   // [64][2]: running max, row sum
-    float* sW = sML + 2 * BM;                    // [64][8]: merge weights
     const int lr0 = warp * 16 + (lane >> 2), lr1 = lr0 + 8;
     __syncthreads();  // every warp is done with the Q and K/V areas (a split may have had no tile)
 #pragma unroll
@@ -334,63 +333,75 @@ __device__ __forceinline__ void attention_body(const AttnArgs& a, int split, int
       sML[2 * lr1 + 1] = l1;
     }
     cluster_sync();
-    // CTA `split` merges rows [split*64/S, (split+1)*64/S) over all splits, in split order
+    // CTA `split` merges rows [split*64/S, (split+1)*64/S) over all splits, in split order. Per
+    // item (row, 4 columns) every split's running max, row sum and O partial come in one round of
+    // DSMEM loads (two items per thread and pass); each thread derives the merge weights of its
+    // rows itself.
     const int rlo = split * BM / S, rhi = (split + 1) * BM / S, nr = rhi - rlo;
     const uint32_t o_addr = smem_u32(sO), ml_addr = smem_u32(sML);
-    if (tid < nr) {
-      const int r = rlo + tid;
-      float ms[8], ls[8], mx = -INFINITY;
+    constexpr int IT = 2;
+    for (int base = 0; base < nr * (HD / 4); base += IT * 128) {
+      float ms[IT][8], ls[IT][8];
+      float4 part[IT][8];
+      int rr[IT], c4[IT];
+      bool on[IT];
 #pragma unroll
-      for (int sp = 0; sp < 8; ++sp) {
-        if (sp < S) {
-          const uint32_t pa = mapa_shared(ml_addr, static_cast<uint32_t>(sp)) + static_cast<uint32_t>(8 * r);
-          ms[sp] = ld_cluster_f32(pa);
-          ls[sp] = ld_cluster_f32(pa + 4);
-          mx = fmaxf(mx, ms[sp]);
+      for (int it = 0; it < IT; ++it) {
+        const int idx = base + it * 128 + tid;
+        on[it] = idx < nr * (HD / 4);
+        rr[it] = on[it] ? idx / (HD / 4) : 0;
+        c4[it] = on[it] ? (idx % (HD / 4)) * 4 : 0;
+        const int r = rlo + rr[it];
+#pragma unroll
+        for (int sp = 0; sp < 8; ++sp) {
+          if (sp < S && on[it]) {
+            const uint32_t pa = mapa_shared(ml_addr, static_cast<uint32_t>(sp)) + static_cast<uint32_t>(8 * r);
+            ms[it][sp] = ld_cluster_f32(pa);
+            ls[it][sp] = ld_cluster_f32(pa + 4);
+            part[it][sp] = ld_cluster_f32x4(mapa_shared(o_addr, static_cast<uint32_t>(sp)) +
+                                            static_cast<uint32_t>((r * LDO + c4[it]) * 4));
+          }
         }
       }
-      if (mx == -INFINITY) mx = 0.f;
-      float l = 0.f;
 #pragma unroll
-      for (int sp = 0; sp < 8; ++sp) {
-        if (sp < S) {
-          ms[sp] = exp2f(ms[sp] - mx);
-          l += ls[sp] * ms[sp];
+      for (int it = 0; it < IT; ++it) {
+        if (!on[it]) continue;
+        float mx = -INFINITY;
+#pragma unroll
+        for (int sp = 0; sp < 8; ++sp)
+          if (sp < S) mx = fmaxf(mx, ms[it][sp]);
+        if (mx == -INFINITY) mx = 0.f;
+        float l = 0.f;
+#pragma unroll
+        for (int sp = 0; sp < 8; ++sp) {
+          if (sp < S) {
+            ms[it][sp] = exp2f(ms[it][sp] - mx);
+            l += ls[it][sp] * ms[it][sp];
+          }
         }
-      }
-      const float inv = 1.f / l;
+        const float inv = 1.f / l;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-      for (int sp = 0; sp < 8; ++sp) sW[8 * tid + sp] = sp < S ? ms[sp] * inv : 0.f;
-    }
-    __syncthreads();
-    for (int idx = tid; idx < nr * (HD / 4); idx += 128) {
-      const int rr = idx / (HD / 4), c4 = (idx % (HD / 4)) * 4;
-      const int row = q0 + rlo + rr;
-      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-      float4 part[8];
-#pragma unroll
-      for (int sp = 0; sp < 8; ++sp)
-        if (sp < S)
-          part[sp] = ld_cluster_f32x4(mapa_shared(o_addr, static_cast<uint32_t>(sp)) +
-                                      static_cast<uint32_t>(((rlo + rr) * LDO + c4) * 4));
-#pragma unroll
-      for (int sp = 0; sp < 8; ++sp) {
-        if (sp < S) {
-          const float wgt = sW[8 * rr + sp];
-          acc.x += part[sp].x * wgt, acc.y += part[sp].y * wgt, acc.z += part[sp].z * wgt, acc.w += part[sp].w * wgt;
+        for (int sp = 0; sp < 8; ++sp) {
+          if (sp < S) {
+            const float wgt = ms[it][sp] * inv;
+            acc.x += part[it][sp].x * wgt, acc.y += part[it][sp].y * wgt, acc.z += part[it][sp].z * wgt,
+                acc.w += part[it][sp].w * wgt;
+          }
         }
-      }
-      if (row < a.Lq) {
-        const long long off = obase + static_cast<long long>(row) * a.ldo + c4;
-        if (a.o_type == SO101_BF16) {
-          __nv_bfloat162 hv[2] = {__floats2bfloat162_rn(acc.x, acc.y), __floats2bfloat162_rn(acc.z, acc.w)};
-          *reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(a.o) + off) = *reinterpret_cast<uint2*>(hv);
-        } else {
-          int8_t* pq = static_cast<int8_t*>(a.o) + off;
-          pq[0] = quant_i8(acc.x, a.o_qscale);
-          pq[1] = quant_i8(acc.y, a.o_qscale);
-          pq[2] = quant_i8(acc.z, a.o_qscale);
-          pq[3] = quant_i8(acc.w, a.o_qscale);
+        const int row = q0 + rlo + rr[it];
+        if (row < a.Lq) {
+          const long long off = obase + static_cast<long long>(row) * a.ldo + c4[it];
+          if (a.o_type == SO101_BF16) {
+            __nv_bfloat162 hv[2] = {__floats2bfloat162_rn(acc.x, acc.y), __floats2bfloat162_rn(acc.z, acc.w)};
+            *reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(a.o) + off) = *reinterpret_cast<uint2*>(hv);
+          } else {
+            int8_t* pq = static_cast<int8_t*>(a.o) + off;
+            pq[0] = quant_i8(acc.x, a.o_qscale);
+            pq[1] = quant_i8(acc.y, a.o_qscale);
+            pq[2] = quant_i8(acc.z, a.o_qscale);
+            pq[3] = quant_i8(acc.w, a.o_qscale);
+          }
         }
       }
     }
