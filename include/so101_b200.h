@@ -167,6 +167,44 @@ SO101_API int so101_attention_rows(const void* q, int64_t ldq, const void* k, in
                                    int64_t b_own, int64_t own_from, const float* k_cos, const float* k_sin,
                                    cudaStream_t stream);
 
+/* Attention fused with its output projection and residual (the few query rows of one
+ * observation): y = residual + attention(q, k, v) @ w_o^T, attention arguments and mask as
+ * so101_attention_rows (k_own NULL: every key from k / v), bf16 attention output rows, hd 64,
+ * nq <= 16 query heads (one cluster of nq CTAs per 128-feature output tile). y and residual fp32
+ * (rows b * Lq + i; residual may be y), w_o (n_out x nq * 64) bf16 with row stride ldw. Optional
+ * y16 = bf16(y * y16_scale[col]) and stat_ss[row * stat_ld + tile] = the row's sum of squares over
+ * output tile `tile` (ceil(n_out / 128) statistics slots, the rms_ss/rms_slots of the next GEMM's
+ * so101_epilogue). The projection sums heads in head order: deterministic; not bit-identical to
+ * so101_attention followed by so101_gemm (which sums K in another order). Replaces the expert's
+ * attention launch and o-projection launch, model/smolvla_triton.py:118-125 (attention, then
+ * lin(a, exp.{i}.o, residual=e); the torch path's model/smolvla.py:298-304).
+ * SO101_ERR_ARG when the GPU cannot hold a cluster of nq CTAs. */
+SO101_API int so101_attention_o(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v,
+                                int64_t ldv, int64_t Lq, int64_t Lk, int nq, int nkv, int hd,
+                                int64_t causal_from, int64_t q_offset, const float* cos, const float* sin,
+                                int batch, int64_t bq, int64_t bk, int64_t bv, const void* k_own,
+                                const void* v_own, int64_t ld_own, int64_t b_own, int64_t own_from,
+                                const float* k_cos, const float* k_sin, const void* w_o, int64_t ldw,
+                                int64_t n_out, float* y, int64_t ldy, const float* residual, int64_t ldr,
+                                void* y16, int64_t ld16, const float* y16_scale, float* stat_ss,
+                                int64_t stat_ld, cudaStream_t stream);
+
+/* The SwiGLU MLP block of the few token rows of one observation in one launch:
+ * y = residual + (silu(rs * x @ w_gate^T) * (rs * x @ w_up^T)) @ w_down^T, x (batch * rows x k)
+ * bf16 with rows <= 64 per observation, rs = rsqrt(sum of the row's rms_slots statistics / k +
+ * rms_eps) (rms_ss NULL: rs = 1), w_gate_up (2 * mlp x k: gate rows, then up rows) and w_down
+ * (n_out x mlp) bf16, mlp a multiple of 128 and at most 2048 (one cluster of mlp / 128 CTAs per
+ * 128-feature output tile, each owning 128 hidden features; hidden activations rounded to bf16
+ * as the unfused chain stores them). y, residual, y16, y16_scale and stat_ss as
+ * so101_attention_o. Replaces model/smolvla_triton.py:126-128 (rms_norm ln_post, lin gate_up with
+ * the SiLU gate, lin down with the residual; the torch path's model/smolvla.py:305-307).
+ * SO101_ERR_ARG when the GPU cannot hold a cluster of mlp / 128 CTAs. */
+SO101_API int so101_mlp(const void* x, int64_t ldx, int64_t rows, int batch, int64_t k, const float* rms_ss,
+                        int rms_slots, int64_t rms_ld, float rms_eps, const void* w_gate_up, int64_t ldw1,
+                        int64_t mlp, const void* w_down, int64_t ldw2, int64_t n_out, float* y, int64_t ldy,
+                        const float* residual, int64_t ldr, void* y16, int64_t ld16, const float* y16_scale,
+                        float* stat_ss, int64_t stat_ld, cudaStream_t stream);
+
 /* y (rows x n) = x * rsqrt(mean(x^2) + eps) * w, statistics in fp32, one rounding to y_type.
  * x_type SO101_F32 or SO101_BF16. Replaces kernels/norm.py:14-42 and model/smolvla.py:72-74. */
 SO101_API int so101_rms_norm(const void* x, int64_t ldx, int x_type, const float* w, void* y,

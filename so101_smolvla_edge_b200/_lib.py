@@ -96,6 +96,10 @@ SIGNATURES = {
                         I64, I64, I64, I64, S],
     "so101_attention_rows": [P, I64, P, I64, P, I64, P, I64, I, F, I64, I64, I, I, I, I64, I64, P, P, I,
                              I64, I64, I64, I64, P, P, I64, I64, I64, P, P, S],
+    "so101_attention_o": [P, I64, P, I64, P, I64, I64, I64, I, I, I, I64, I64, P, P, I, I64, I64, I64,
+                          P, P, I64, I64, I64, P, P, P, I64, I64, P, I64, P, I64, P, I64, P, P, I64, S],
+    "so101_mlp": [P, I64, I64, I, I64, P, I, I64, F, P, I64, I64, P, I64, I64, P, I64, P, I64, P, I64, P, P,
+                  I64, S],
     "so101_rms_norm": [P, I64, I, P, P, I64, I, I64, I64, F, S],
     "so101_layer_norm": [P, I64, P, P, P, I64, I, F, I64, I64, F, I, I64, S],
     "so101_rope_kv": [P, I64, I, I, I, P, P, P, I64, P, I64, I64, I, I64, I64, I64, S],

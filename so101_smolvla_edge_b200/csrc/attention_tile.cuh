@@ -76,22 +76,29 @@ __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
-// Shared-memory bytes attention_body<HD, ...> uses.
-template <int HD>
+// Shared-memory bytes attention_body<HD, ..., NBUF> uses: the Q tile and NBUF K and V tiles.
+template <int HD, int NBUF = 2>
 constexpr int attention_smem_bytes() {
-  return (64 * (HD + 8) + 4 * 64 * (HD + 8)) * 2;
+  return (1 + 2 * NBUF) * 64 * (HD + 8) * 2;
 }
 
 // One CTA's work (128 threads, all of which must call it): query rows [q0, q0 + 64) of head h of
-// problem bi, key tiles of split `split` of a.kv_splits (SPLIT) or all of them.
-template <int HD, bool SPLIT>
+// problem bi, key tiles of split `split` of a.kv_splits (SPLIT) or all of them. TILE_OUT (HD 64,
+// no split): the normalised rows go to o_tile in shared memory instead of a.o, as bf16 in the
+// K-major TMA SWIZZLE_128B layout (64 rows of 128 bytes; 16-byte chunk c of row r stored at chunk
+// c ^ (r % 8); 1024-byte aligned), the B operand of a tcgen05 MMA; rows at or past Lq are zero.
+// NBUF: depth of the K/V ring; NBUF - 1 tiles are loaded ahead of the one being used, so a CTA
+// with at most NBUF - 1 tiles (the expert's 291 keys at NBUF 6) pays one load latency in all.
+template <int HD, bool SPLIT, bool TILE_OUT = false, int NBUF = 2>
 __device__ __forceinline__ void attention_body(const AttnArgs& a, int split, int q0, int h, int bi,
-                                               uint8_t* smem_raw) {
+                                               uint8_t* smem_raw, uint8_t* o_tile = nullptr) {
+  static_assert(!TILE_OUT || (HD == 64 && !SPLIT), "the shared-memory output tile holds one 64-dim head");
   constexpr int BM = 64, BN = 64, LDS = HD + 8, HALF = HD / 2;
   constexpr int CHUNKS = HD / 8;  // 16-byte chunks per row
   __nv_bfloat16* sQ = reinterpret_cast<__nv_bfloat16*>(smem_raw);
-  __nv_bfloat16* sK = sQ + BM * LDS;          // [2][BN * LDS]
-  __nv_bfloat16* sV = sK + 2 * BN * LDS;      // [2][BN * LDS]
+  static_assert(NBUF >= 2, "the K/V ring needs two buffers");
+  __nv_bfloat16* sK = sQ + BM * LDS;          // [NBUF][BN * LDS]
+  __nv_bfloat16* sV = sK + NBUF * BN * LDS;   // [NBUF][BN * LDS]
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int S = SPLIT ? a.kv_splits : 1;
@@ -130,7 +137,7 @@ __device__ __forceinline__ void attention_body(const AttnArgs& a, int split, int
     cp_async_commit();
   };
 
-  if (n_tiles > 0) load_kv(t_begin, 0);
+  for (int i = 0; i < NBUF - 1 && i < n_tiles; ++i) load_kv(t_begin + i, i);
 
   // stage Q (rotated) into shared memory: 8 dims of each rotary half per step, 16-byte loads
   constexpr int VH = HALF / 8;
@@ -188,10 +195,11 @@ __device__ __forceinline__ void attention_body(const AttnArgs& a, int split, int
   const int r1 = r0 + 8;
 
   for (int tile = 0; tile < n_tiles; ++tile) {
-    const int buf = tile & 1;
-    if (tile + 1 < n_tiles) {
-      load_kv(t_begin + tile + 1, buf ^ 1);
-      cp_async_wait<1>();
+    const int buf = tile % NBUF;
+    if (tile + NBUF - 1 < n_tiles) {
+      // refill the buffer the previous tile used (every warp is past it: the loop's last barrier)
+      load_kv(t_begin + tile + NBUF - 1, (tile + NBUF - 1) % NBUF);
+      cp_async_wait<NBUF - 1>();
     } else {
       cp_async_wait<0>();
     }
@@ -305,7 +313,7 @@ __device__ __forceinline__ void attention_body(const AttnArgs& a, int split, int
         mma_bf16_16816(o[2 * t2 + 1], pf[j], b2, b3);
       }
     }
-    __syncthreads();  // this buffer is refilled two tiles from now
+    __syncthreads();  // this buffer is refilled at the top of the next tile
   }
 
   l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
@@ -409,22 +417,36 @@ __device__ __forceinline__ void attention_body(const AttnArgs& a, int split, int
     return;
   }
   const float inv0 = 1.f / l0, inv1 = 1.f / l1;
+  if constexpr (TILE_OUT) {
+    // this thread's columns t*8 + (lane&3)*2 + {0, 1} of a row are bytes (lane&3)*4 of chunk t
 #pragma unroll
-  for (int t = 0; t < HD / 8; ++t) {
-    const int col = t * 8 + (lane & 3) * 2;
+    for (int t = 0; t < HD / 8; ++t) {
 #pragma unroll
-    for (int half = 0; half < 2; ++half) {
-      const int row = half ? r1 : r0;
-      if (row >= a.Lq) continue;
-      const float x0 = o[t][half * 2] * (half ? inv1 : inv0);
-      const float x1 = o[t][half * 2 + 1] * (half ? inv1 : inv0);
-      const long long off = obase + static_cast<long long>(row) * a.ldo + col;
-      if (a.o_type == SO101_BF16) {
-        *reinterpret_cast<__nv_bfloat162*>(static_cast<__nv_bfloat16*>(a.o) + off) = __floats2bfloat162_rn(x0, x1);
-      } else {
-        int8_t* p = static_cast<int8_t*>(a.o) + off;
-        p[0] = quant_i8(x0, a.o_qscale);
-        p[1] = quant_i8(x1, a.o_qscale);
+      for (int half = 0; half < 2; ++half) {
+        const int row = half ? r1 : r0, lr = row - q0;
+        const float inv = half ? inv1 : inv0;
+        const uint32_t val = row < a.Lq ? pack_bf16(o[t][half * 2] * inv, o[t][half * 2 + 1] * inv) : 0u;
+        *reinterpret_cast<uint32_t*>(o_tile + lr * 128 + ((t ^ (lr & 7)) << 4) + (lane & 3) * 4) = val;
+      }
+    }
+  } else {
+#pragma unroll
+    for (int t = 0; t < HD / 8; ++t) {
+      const int col = t * 8 + (lane & 3) * 2;
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        const int row = half ? r1 : r0;
+        if (row >= a.Lq) continue;
+        const float x0 = o[t][half * 2] * (half ? inv1 : inv0);
+        const float x1 = o[t][half * 2 + 1] * (half ? inv1 : inv0);
+        const long long off = obase + static_cast<long long>(row) * a.ldo + col;
+        if (a.o_type == SO101_BF16) {
+          *reinterpret_cast<__nv_bfloat162*>(static_cast<__nv_bfloat16*>(a.o) + off) = __floats2bfloat162_rn(x0, x1);
+        } else {
+          int8_t* p = static_cast<int8_t*>(a.o) + off;
+          p[0] = quant_i8(x0, a.o_qscale);
+          p[1] = quant_i8(x1, a.o_qscale);
+        }
       }
     }
   }

@@ -471,36 +471,46 @@ __global__ void __launch_bounds__(kTileThreads, (SWAP && DUAL) ? 1 : 2)
   grid_dep_launch();  // the next kernel may start its own prologue and weight prefetch
 
   if (warp == 0 && lane == 0) {
-    // TMA producer: the first stages' weight tiles go out before waiting for the previous grid
+    // TMA producer: the weight tiles of the ring's first round go out before waiting for the
+    // previous grid
     tma_prefetch_desc(&tm_x);
     tma_prefetch_desc(&tm_w);
     const uint64_t pol_w = SWAP ? policy_evict_first() : policy_evict_last();
     const uint64_t pol_x = SWAP ? policy_evict_last() : policy_evict_first();
-    bool waited = false;
-    for (int i = 0; i < nkb; ++i) {
-      const int s = i % stages;
-      const uint32_t round = static_cast<uint32_t>(i / stages);
-      if (i >= stages && !mbar_wait(&empty[s], (round - 1) & 1u, a.status)) break;
-      uint8_t* st = smem + s * STAGE_BYTES;
-      mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
+    auto load_w = [&](int i, uint8_t* st, uint64_t* bar) {
       const int kx = (kb0 + i) * KB_ELEMS;
       if (SWAP) {
 #pragma unroll
-        for (int t = 0; t < NA; ++t) tma_load_2d(st + t * A_BYTES, &tm_w, &full[s], kx, p0 + t * a.N, pol_w);
+        for (int t = 0; t < NA; ++t) tma_load_2d(st + t * A_BYTES, &tm_w, bar, kx, p0 + t * a.N, pol_w);
       } else {
 #pragma unroll
-        for (int t = 0; t < NB; ++t) tma_load_2d(st + NA * A_BYTES + t * B_BYTES, &tm_w, &full[s], kx, q0 + t * a.N, pol_w);
+        for (int t = 0; t < NB; ++t) tma_load_2d(st + NA * A_BYTES + t * B_BYTES, &tm_w, bar, kx, q0 + t * a.N, pol_w);
       }
-      if (!waited) {
-        grid_dep_wait();
-        waited = true;
-      }
+    };
+    auto load_x = [&](int i, uint8_t* st, uint64_t* bar) {
+      const int kx = (kb0 + i) * KB_ELEMS;
       if (SWAP)
-        tma_load_2d(st + NA * A_BYTES, &tm_x, &full[s], kx, q0, pol_x);
+        tma_load_2d(st + NA * A_BYTES, &tm_x, bar, kx, q0, pol_x);
       else
-        tma_load_2d(st, &tm_x, &full[s], kx, p0, pol_x);
+        tma_load_2d(st, &tm_x, bar, kx, p0, pol_x);
+    };
+    // the ring's whole first round of weights, then (once the previous grid is done) its tokens
+    const int pre = min(stages, nkb);
+    for (int i = 0; i < pre; ++i) {
+      mbar_arrive_expect_tx(&full[i], STAGE_BYTES);
+      load_w(i, smem + i * STAGE_BYTES, &full[i]);
     }
-    if (!waited) grid_dep_wait();
+    grid_dep_wait();
+    for (int i = 0; i < pre; ++i) load_x(i, smem + i * STAGE_BYTES, &full[i]);
+    for (int i = pre; i < nkb; ++i) {
+      const int s = i % stages;
+      const uint32_t round = static_cast<uint32_t>(i / stages);
+      if (!mbar_wait(&empty[s], (round - 1) & 1u, a.status)) break;
+      uint8_t* st = smem + s * STAGE_BYTES;
+      mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
+      load_w(i, st, &full[s]);
+      load_x(i, st, &full[s]);
+    }
   } else if (warp == 1 && lane == 0) {
     // MMA issuer
     for (int i = 0; i < nkb; ++i) {

@@ -253,6 +253,124 @@ def attention(
     return out
 
 
+def attention_o(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    n_heads: int,
+    n_kv: int,
+    w_o: torch.Tensor,
+    y: torch.Tensor,
+    *,
+    residual: torch.Tensor | None = None,
+    cos: torch.Tensor | None = None,
+    sin: torch.Tensor | None = None,
+    causal_from: int | None = None,
+    q_offset: int = 0,
+    own: tuple | None = None,
+    y16: torch.Tensor | None = None,
+    y16_scale: torch.Tensor | None = None,
+    stat_ss: torch.Tensor | None = None,
+) -> int:
+    """y = residual + attention(q, k, v) @ w_o^T in one launch (so101_attention_o).
+
+    q, k, v, cos, sin, causal_from, q_offset and own as `attention` (head_dim 64, at most 16 query
+    heads); y and residual fp32 (rows b * Lq + i, residual may be y); w_o (N, n_heads * 64) bf16.
+    y16 (bf16) receives y * y16_scale per column and stat_ss[row, t] the row's sum of squares over
+    output features [128 t, 128 t + 128). Returns the number of statistics slots, ceil(N / 128).
+    """
+    _cuda(q, k, v, w_o, y, residual, y16, y16_scale, stat_ss)
+    batched = q.dim() == 3
+    qb, kb, vb = (q, k, v) if batched else (q[None], k[None], v[None])
+    bsz, lq, lk = qb.shape[0], qb.shape[1], kb.shape[1]
+    hd = kb.shape[2] // n_kv
+    for name, t in (("q", qb), ("k", kb), ("v", vb), ("w_o", w_o)):
+        if t.stride(-1) != 1:
+            raise ValueError(f"{name} needs unit column stride, has {t.stride()}")
+        if t.dtype != torch.bfloat16:
+            raise ValueError(f"{name} must be bf16")
+    n_out = w_o.shape[0]
+    y2 = y.reshape(-1, n_out) if y.dim() == 3 else y
+    r2 = None if residual is None else (residual.reshape(-1, n_out) if residual.dim() == 3 else residual)
+    for name, t in (("y", y2), ("residual", r2), ("stat_ss", stat_ss)):
+        if t is not None and t.dtype != torch.float32:
+            raise ValueError(f"{name} must be float32")
+    if y16 is not None and y16.dtype != torch.bfloat16:
+        raise ValueError("y16 must be bf16")
+    if cos is not None:
+        cos = cos.reshape(lq, hd // 2).float().contiguous()
+        sin = sin.reshape(lq, hd // 2).float().contiguous()
+    if y16_scale is not None:
+        y16_scale = y16_scale.float().contiguous()
+    ck = lk if causal_from is None else causal_from
+    own_args: tuple = (None, None, 0, 0, 0, None, None)
+    if own is not None:
+        k_own, v_own, own_from, k_cos, k_sin = own
+        ko = k_own if k_own.dim() == 3 else k_own[None]
+        vo = v_own if v_own.dim() == 3 else v_own[None]
+        if ko.stride(1) != vo.stride(1) or ko.stride(0) != vo.stride(0):
+            raise ValueError("k_own and v_own need the same strides (views of one fused buffer)")
+        own_args = (ko.data_ptr(), vo.data_ptr(), ko.stride(1), ko.stride(0), own_from, k_cos.data_ptr(),
+                    k_sin.data_ptr())  # fmt: skip
+    y16_2 = None if y16 is None else y16.reshape(-1, n_out) if y16.dim() == 3 else y16
+    rc = L.lib().so101_attention_o(
+        qb.data_ptr(), qb.stride(1), kb.data_ptr(), kb.stride(1), vb.data_ptr(), vb.stride(1), lq, lk, n_heads,
+        n_kv, hd, ck, q_offset, _ptr(cos), _ptr(sin), bsz, qb.stride(0), kb.stride(0), vb.stride(0), *own_args,
+        w_o.data_ptr(), w_o.stride(0), n_out, y2.data_ptr(), y2.stride(0), _ptr(r2), 0 if r2 is None else r2.stride(0),
+        _ptr(y16_2), 0 if y16_2 is None else y16_2.stride(0), _ptr(y16_scale), _ptr(stat_ss),
+        0 if stat_ss is None else stat_ss.stride(0), _stream(q.device),
+    )  # fmt: skip
+    L.check(rc, "so101_attention_o")
+    return (n_out + 127) // 128
+
+
+def mlp(
+    x: torch.Tensor,
+    w_gate_up: torch.Tensor,
+    w_down: torch.Tensor,
+    y: torch.Tensor,
+    *,
+    residual: torch.Tensor | None = None,
+    rms: tuple[torch.Tensor, int, float] | None = None,
+    rows: int | None = None,
+    y16: torch.Tensor | None = None,
+    y16_scale: torch.Tensor | None = None,
+    stat_ss: torch.Tensor | None = None,
+) -> int:
+    """y = residual + (silu(x @ gate^T) * (x @ up^T)) @ w_down^T in one launch (so101_mlp).
+
+    x (B * rows, K) bf16 with at most 64 rows per observation (rows defaults to all of x: one
+    observation); w_gate_up (2 * mlp, K) is [gate; up]; w_down (N, mlp). rms=(ss, slots, eps)
+    finishes the RMSNorm of x as `linear` does. y, residual, y16, y16_scale and stat_ss as
+    `attention_o`. Returns the number of statistics slots, ceil(N / 128).
+    """
+    _cuda(x, w_gate_up, w_down, y, residual, y16, y16_scale, stat_ss)
+    for name, t in (("x", x), ("w_gate_up", w_gate_up), ("w_down", w_down)):
+        if t.dtype != torch.bfloat16 or t.stride(-1) != 1:
+            raise ValueError(f"{name} must be bf16 with unit column stride")
+    rows = x.shape[0] if rows is None else rows
+    if x.shape[0] % rows:
+        raise ValueError("x's rows are not a whole number of observations")
+    n_out, hidden = w_down.shape
+    if w_gate_up.shape[0] != 2 * hidden:
+        raise ValueError("w_gate_up needs 2 * mlp rows for w_down's mlp columns")
+    for name, t in (("y", y), ("residual", residual), ("stat_ss", stat_ss)):
+        if t is not None and t.dtype != torch.float32:
+            raise ValueError(f"{name} must be float32")
+    if y16_scale is not None:
+        y16_scale = y16_scale.float().contiguous()
+    ss, slots, eps = rms if rms is not None else (None, 0, 0.0)
+    rc = L.lib().so101_mlp(
+        x.data_ptr(), x.stride(0), rows, x.shape[0] // rows, x.shape[1], _ptr(ss), slots,
+        0 if ss is None else ss.stride(0), eps, w_gate_up.data_ptr(), w_gate_up.stride(0), hidden,
+        w_down.data_ptr(), w_down.stride(0), n_out, y.data_ptr(), y.stride(0), _ptr(residual),
+        0 if residual is None else residual.stride(0), _ptr(y16), 0 if y16 is None else y16.stride(0),
+        _ptr(y16_scale), _ptr(stat_ss), 0 if stat_ss is None else stat_ss.stride(0), _stream(x.device),
+    )  # fmt: skip
+    L.check(rc, "so101_mlp")
+    return (n_out + 127) // 128
+
+
 def rope_kv(
     qkv: torch.Tensor,
     n_heads: int,

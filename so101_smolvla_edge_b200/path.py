@@ -24,6 +24,7 @@ from __future__ import annotations
 
 import ctypes as C
 import math
+import os
 
 import numpy as np
 import torch
@@ -147,6 +148,20 @@ class B200Path:
         if expert_step not in ("auto", "fused", "ops"):
             raise ValueError(f"expert_step must be 'auto', 'fused' or 'ops', not {expert_step!r}")
         self.fold = bool(fold_norms)  # RMSNorm split into the GEMMs around it (else an rms_norm launch each)
+        # one observation: each expert layer's SwiGLU MLP block in one launch (so101_mlp) unless
+        # SO101_FUSED_MLP=0, and the cross-attention layers' attention, output projection and
+        # residual in one launch (so101_attention_o). SO101_ATTN_O: "cross" (default; on B200 the
+        # fused launch beats attention + GEMM over the 241 prefix keys, 13.2 against 15.0 us, but not
+        # over the self layers' 291 keys, 16.1 against 15.8), "all" or "0".
+        one = self.B == 1 and s.chunk <= 64
+        self.mlp_fused = (one and s.exp_mlp % 128 == 0 and s.exp_mlp <= 2048
+                          and os.environ.get("SO101_FUSED_MLP", "1") != "0")  # fmt: skip
+        mode = os.environ.get("SO101_ATTN_O", "cross")
+        if mode not in ("cross", "all", "0"):
+            raise ValueError(f"SO101_ATTN_O must be 'cross', 'all' or '0', not {mode!r}")
+        ok = one and s.head_dim == 64 and s.n_heads <= 16
+        self.attn_o_layers = {i for i in range(s.n_layers)
+                              if ok and (mode == "all" or (mode == "cross" and not s.is_self_attn(i)))}  # fmt: skip
         self.ws = workspace(device)  # split-K partials and tickets exist before any capture
         self._amax: tuple[torch.Tensor, dict[str, int]] | None = None  # calibration hooks
         self._upload(bundle)
@@ -406,6 +421,36 @@ class B200Path:
             prog.add(what, self.lib.so101_attention_rows, *args, k_own, v_own, ld_own, b_own, own_from,
                      k_cos.data_ptr(), k_sin.data_ptr())  # fmt: skip
 
+    def _attn_o(self, prog, what, q, ldq, bq, k, ldk, bk, v, ldv, bv, *, w_o, y, stat, Lq, Lk, nq, nkv, hd,
+                causal_from, q_offset=0, cos=None, sin=None, batch=1, own=None) -> int:  # fmt: skip
+        """Attention, output projection and residual in one launch (so101_attention_o): y += attention
+        @ w_o^T. stat=(ss, x16, norm_w) also writes the statistics slots (returned) and
+        bf16(y * norm_w) for the next norm's GEMM."""
+        own_args = (None, None, 0, 0, 0, None, None) if own is None else \
+            (*own[:5], own[5].data_ptr(), own[6].data_ptr())  # fmt: skip
+        ss, x16, nw = stat if stat is not None else (None, None, None)
+        prog.add(what, self.lib.so101_attention_o, q, ldq, k, ldk, v, ldv, Lq, Lk, nq, nkv, hd, causal_from,
+                 q_offset, None if cos is None else cos.data_ptr(), None if sin is None else sin.data_ptr(), batch,
+                 bq, bk, bv, *own_args, w_o.data_ptr(), w_o.stride(0), w_o.shape[0], y.data_ptr(), y.stride(0),
+                 y.data_ptr(), y.stride(0), None if x16 is None else x16.data_ptr(),
+                 0 if x16 is None else x16.stride(0), None if nw is None else nw.data_ptr(),
+                 None if ss is None else ss.data_ptr(), 0 if ss is None else ss.stride(0))  # fmt: skip
+        return (w_o.shape[0] + 127) // 128 if stat is not None else 0
+
+    def _mlp(self, prog, what, x, w_gu, w_down, y, *, rms, stat) -> int:
+        """The SwiGLU MLP block in one launch (so101_mlp): y += silu(x gate^T) (x up^T) w_down^T, the
+        RMSNorm of x finished from rms=(ss, slots); stat as _attn_o. One observation of <= 64 rows."""
+        ss, slots = rms if rms is not None else (None, 0)
+        s_ss, x16, nw = stat if stat is not None else (None, None, None)
+        prog.add(what, self.lib.so101_mlp, x.data_ptr(), x.stride(0), x.shape[0], 1, x.shape[1],
+                 None if ss is None else ss.data_ptr(), slots, 0 if ss is None else ss.stride(0), self.spec.rms_eps,
+                 w_gu.data_ptr(), w_gu.stride(0), w_down.shape[1], w_down.data_ptr(), w_down.stride(0),
+                 w_down.shape[0], y.data_ptr(), y.stride(0), y.data_ptr(), y.stride(0),
+                 None if x16 is None else x16.data_ptr(), 0 if x16 is None else x16.stride(0),
+                 None if nw is None else nw.data_ptr(), None if s_ss is None else s_ss.data_ptr(),
+                 0 if s_ss is None else s_ss.stride(0))  # fmt: skip
+        return (w_down.shape[0] + 127) // 128 if stat is not None else 0
+
     def _rms(self, prog, what, x, w, y, rows):
         s = self.spec
         prog.add(what, self.lib.so101_rms_norm, x.data_ptr(), x.stride(0), DTYPE[x.dtype], w.data_ptr(),
@@ -567,28 +612,38 @@ class B200Path:
                     p.add(f"s{k}.{i}.rope_kv", self.lib.so101_rope_kv, self.qkv_e.data_ptr(), qd, nq, nk, hd,
                           w["cos_s"].data_ptr(), w["sin_s"].data_ptr(), self.ck[i].data_ptr() + off, kv,
                           self.cv[i].data_ptr() + off, kv, H, B, H * qd, bk, bk)  # fmt: skip
-                self._attn(p, f"s{k}.{i}.attn", self.qkv_e.data_ptr(), qd, H * qd, self.ck[i].data_ptr(),
-                           kv, bk, self.cv[i].data_ptr(), kv, bk, self.attn_e, s.q_dim, H * s.q_dim,
-                           Lq=H, Lk=L_ + H, nq=nq, nkv=nk, hd=hd, causal_from=L_, q_offset=L_,
-                           cos=w["cos_s"], sin=w["sin_s"], batch=B, own=own)  # fmt: skip
+                operands = (self.qkv_e.data_ptr(), qd, H * qd, self.ck[i].data_ptr(), kv, bk, self.cv[i].data_ptr(),
+                            kv, bk)  # fmt: skip
+                geom = dict(Lq=H, Lk=L_ + H, nq=nq, nkv=nk, hd=hd, causal_from=L_, q_offset=L_, cos=w["cos_s"],
+                            sin=w["sin_s"], batch=B, own=own)  # fmt: skip
             else:
                 qv = self.qkv_e[:, : s.q_dim]
                 self._gemm(p, f"s{k}.{i}.q", self.h_e, w[pre + "q"], qv, rms=rms)
-                self._attn(p, f"s{k}.{i}.attn", self.qkv_e.data_ptr(), qd, H * qd, self.kx[i].data_ptr(),
-                           kv, L_ * kv, self.vx[i].data_ptr(), kv, L_ * kv, self.attn_e, s.q_dim,
-                           H * s.q_dim, Lq=H, Lk=L_, nq=nq, nkv=nk, hd=hd, causal_from=L_,
-                           cos=w["cos_c"], sin=w["sin_c"], batch=B)  # fmt: skip
-            if fold:
-                slots = self._gemm(p, f"s{k}.{i}.o", self.attn_e, w[pre + "o"], e, residual=e,
-                                   stat=(self.ss_e, self.h_e, w[pre + "ln_post"]))  # fmt: skip
+                operands = (self.qkv_e.data_ptr(), qd, H * qd, self.kx[i].data_ptr(), kv, L_ * kv,
+                            self.vx[i].data_ptr(), kv, L_ * kv)  # fmt: skip
+                geom = dict(Lq=H, Lk=L_, nq=nq, nkv=nk, hd=hd, causal_from=L_, cos=w["cos_c"], sin=w["sin_c"],
+                            batch=B)  # fmt: skip
+            post = (self.ss_e, self.h_e, w[pre + "ln_post"]) if fold else None
+            if i in self.attn_o_layers:  # attention, output projection and residual in one launch
+                slots = self._attn_o(p, f"s{k}.{i}.attn_o", *operands, w_o=w[pre + "o"], y=e, stat=post, **geom)
+                if not fold:
+                    self._rms(p, f"s{k}.{i}.ln_post", e, w[pre + "ln_post"], self.h_e, M)
             else:
-                self._gemm(p, f"s{k}.{i}.o", self.attn_e, w[pre + "o"], e, residual=e)
-                self._rms(p, f"s{k}.{i}.ln_post", e, w[pre + "ln_post"], self.h_e, M)
-            self._gemm(p, f"s{k}.{i}.gate_up", self.h_e, w[pre + "gate_up"], self.mlp_e, gate=True,
-                       rms=(self.ss_e, slots) if fold else None)  # fmt: skip
+                self._attn(p, f"s{k}.{i}.attn", *operands, self.attn_e, s.q_dim, H * s.q_dim, **geom)
+                if fold:
+                    slots = self._gemm(p, f"s{k}.{i}.o", self.attn_e, w[pre + "o"], e, residual=e, stat=post)
+                else:
+                    self._gemm(p, f"s{k}.{i}.o", self.attn_e, w[pre + "o"], e, residual=e)
+                    self._rms(p, f"s{k}.{i}.ln_post", e, w[pre + "ln_post"], self.h_e, M)
             # the last layer's output goes to the final norm of so101_expert_out (fp32, from e)
             nxt = (self.ss_e, self.h_e, w[f"exp.{i + 1}.ln_in"]) if fold and i + 1 < s.n_layers else None
-            slots = self._gemm(p, f"s{k}.{i}.down", self.mlp_e, w[pre + "down"], e, residual=e, stat=nxt)
+            if self.mlp_fused:  # gate/up, SiLU gate, down and residual in one launch
+                slots = self._mlp(p, f"s{k}.{i}.mlp", self.h_e, w[pre + "gate_up"], w[pre + "down"], e,
+                                  rms=(self.ss_e, slots) if fold else None, stat=nxt)  # fmt: skip
+            else:
+                self._gemm(p, f"s{k}.{i}.gate_up", self.h_e, w[pre + "gate_up"], self.mlp_e, gate=True,
+                           rms=(self.ss_e, slots) if fold else None)  # fmt: skip
+                slots = self._gemm(p, f"s{k}.{i}.down", self.mlp_e, w[pre + "down"], e, residual=e, stat=nxt)
         p.add(f"s{k}.out+euler", self.lib.so101_expert_out, e.data_ptr(), s.exp_dim, w["exp.norm"].data_ptr(),
               s.rms_eps, w["act.out.w"].data_ptr(), w["act.out.b"].data_ptr(), x_out.data_ptr(),
               s.max_action, M, s.max_action, s.exp_dim, dt)  # fmt: skip

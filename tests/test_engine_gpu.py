@@ -216,6 +216,30 @@ def test_fused_expert_step_matches_per_op_path(case):
     torch.cuda.empty_cache()
 
 
+@pytest.mark.parametrize("attn_o,mlp", [("all", "1"), ("cross", "1"), ("0", "0")])
+def test_fused_expert_blocks_match_reference(attn_o, mlp, monkeypatch):
+    """configs[0] with the expert layers' attention + output projection (so101_attention_o, on all
+    layers, on the cross layers or off) and SwiGLU blocks (so101_mlp, on or off) fused: every
+    combination stays within the action tolerance of the reference's float32 chunk, replays bit
+    for bit, and fusing removes launches."""
+    from so101_smolvla_edge_b200.engine import Engine
+
+    monkeypatch.setenv("SO101_ATTN_O", attn_o)
+    monkeypatch.setenv("SO101_FUSED_MLP", mlp)
+    g = golden("config0")
+    b = config0_bundle()
+    eng = Engine(b, warmup=1)
+    s = eng.path.spec
+    want_o = {"all": s.n_layers, "cross": sum(not s.is_self_attn(i) for i in range(s.n_layers)), "0": 0}[attn_o]
+    assert len(eng.path.attn_o_layers) == want_o and eng.path.mlp_fused == (mlp == "1")
+    images, state, noise = observation(b, 0)
+    a = eng.infer(images, state, noise)
+    assert np.array_equal(a, eng.infer(images, state, noise))
+    assert np.abs(a - g["actions"][0]).max() <= ACTION_TOL
+    del eng
+    torch.cuda.empty_cache()
+
+
 def test_autotuned_engine_matches_reference():
     """compile="autotune" (the reference's autotuned GEMMs) times the GEMM plans of every large
     GEMM and rebuilds the programs with the fastest: configs[0]'s vision GEMMs (3072 rows) are

@@ -342,6 +342,70 @@ def test_attention_own_rows_equal_rope_cache_then_attention(batch):
     assert torch.equal(got, want)
 
 
+@pytest.mark.parametrize(
+    "kind,batch,n_out",
+    [("self", 1, 720), ("cross", 1, 720), ("self", 2, 720), ("prefix", 1, 960), ("cross", 1, 100)],
+)
+def test_attention_o_equals_attention_then_projection(kind, batch, n_out):
+    """so101_attention_o (attention, output projection and residual in one launch, the heads of
+    each 128-feature tile summed across a cluster) against the float32 expression (fp32 softmax
+    attention, fp32 projection): no further from it than twice the two-launch chain
+    (so101_attention's bf16 rows, whose split-key merge rounds differently, projected in fp32)
+    + 1e-3 * max|projection|. y16 and the statistics slots are checked against the fused output
+    itself: bf16(y * w) exactly, per-tile sums of squares to fp32 rounding; a second call repeats
+    the bits. The expert's self (own rows rotated on chip, causal onto its own rows) and cross
+    attention at 50 rows, a batch of two, a 241-row prefix (4 query blocks) and a ragged
+    100-feature output."""
+    from so101_smolvla_edge_b200.ops import attention, attention_o, rope_kv
+
+    L_, nq, nk, hd = 241, 15, 5, 64
+    H = 241 if kind == "prefix" else 50
+    qd = (nq + 2 * nk) * hd
+    qkv = rnd(batch, H, qd, dtype=torch.bfloat16, scale=2.0)
+    q = qkv[:, :, : nq * hd]
+    if kind == "self":
+        k = rnd(batch, L_ + H, nk * hd, dtype=torch.bfloat16, seed=1)
+        v = rnd(batch, L_ + H, nk * hd, dtype=torch.bfloat16, seed=2)
+        cos, sin = rope_tables(torch.arange(L_, L_ + H, device="cuda"), hd, 100000.0)
+        kw = dict(cos=cos, sin=sin, causal_from=L_, q_offset=L_,
+                  own=(qkv[:, :, nq * hd : (nq + nk) * hd], qkv[:, :, (nq + nk) * hd :], L_, cos, sin))
+    elif kind == "cross":
+        k = rnd(batch, L_, nk * hd, dtype=torch.bfloat16, seed=1)
+        v = rnd(batch, L_, nk * hd, dtype=torch.bfloat16, seed=2)
+        cos, sin = rope_tables(torch.arange(H, device="cuda"), hd, 100000.0)
+        kw = dict(cos=cos, sin=sin, causal_from=L_)
+    else:  # the prefix's own attention: keys are the rows themselves, prefix-LM mask
+        k, v = qkv[:, :, nq * hd : (nq + nk) * hd], qkv[:, :, (nq + nk) * hd :]
+        cos, sin = rope_tables(torch.arange(H, device="cuda"), hd, 100000.0)
+        kw = dict(cos=cos, sin=sin, causal_from=H - 1)
+    w_o = rnd(n_out, nq * hd, dtype=torch.bfloat16, scale=0.02, seed=3)
+    res = rnd(batch * H, n_out, seed=4)
+    scale = 1.0 + 0.1 * rnd(n_out, seed=5)
+    tiles = (n_out + 127) // 128
+    y = res.clone()
+    y16 = torch.zeros(batch * H, n_out, dtype=torch.bfloat16, device="cuda")
+    ss = torch.full((batch * H, 64), -1.0, device="cuda")
+    assert attention_o(q, k, v, nq, nk, w_o, y, residual=y, y16=y16, y16_scale=scale, stat_ss=ss, **kw) == tiles
+    kc, vc, vis = k, v, visibility(H, k.shape[1], kw.get("causal_from", k.shape[1]), kw.get("q_offset", 0))
+    if kind == "self":  # the reference cache holds the rotated own keys and the own values
+        kc, vc = k.clone(), v.clone()
+        for b in range(batch):
+            rope_kv(qkv[b], nq, nk, cos, sin, kc[b, L_:], vc[b, L_:])
+    a_ref = torch.cat([attention_ref(q[b], kc[b], vc[b], nq, nk, vis, cos, sin) for b in range(batch)])
+    want = res + a_ref @ w_o.float().T
+    chain = res + attention(q, k, v, nq, nk, **kw).reshape(batch * H, nq * hd).float() @ w_o.float().T
+    size = (want - res).abs().max().item()
+    err, err_chain = (y - want).abs().max().item(), (chain - want).abs().max().item()
+    assert err <= 2 * err_chain + 1e-3 * size, (err, err_chain, size)
+    assert torch.equal(y16, (y * scale).to(torch.bfloat16))
+    sq = F.pad(y * y, (0, tiles * 128 - n_out)).view(batch * H, tiles, 128).sum(-1)
+    assert torch.allclose(ss[:, :tiles], sq, rtol=1e-5, atol=1e-6)
+    assert bool((ss[:, tiles:] == -1.0).all())  # no slot past the tiles is written
+    y2 = res.clone()
+    attention_o(q, k, v, nq, nk, w_o, y2, residual=y2, **kw)
+    assert torch.equal(y2, y)
+
+
 def test_attention_batched_and_strided():
     """A batch of independent problems with k and v as views into the fused qkv rows."""
     from so101_smolvla_edge_b200.ops import attention
@@ -429,6 +493,51 @@ def test_linear_f32_tiles_agree_bit_for_bit(silu):
 def _rms_ref(x, w, eps):
     x = x.float()
     return x * torch.rsqrt((x * x).mean(-1, keepdim=True) + eps) * w.float()
+
+
+@pytest.mark.parametrize("rows,batch,k,hidden,n_out,use_rms", [
+    (50, 1, 720, 2048, 720, True), (50, 2, 720, 2048, 720, True), (64, 1, 960, 1024, 960, False),
+    (7, 1, 128, 128, 100, True)])  # fmt: skip
+def test_mlp_block_matches_chain(rows, batch, k, hidden, n_out, use_rms):
+    """so101_mlp (gate/up, SiLU gate, down and residual in one launch, the hidden features split
+    over a cluster) against the float32 block computed from the same bf16 operand: no further
+    from it than twice the two-launch chain (the gate/up GEMM's bf16 activations, then the down
+    projection) + 1e-3 * max|block|. y16 and statistics against the fused output itself, and a
+    second run repeats the bits. The expert's shape (50 rows, 720 -> 2048 -> 720) at one and two
+    observations, a 64-row block without the norm, and a 7-row block with one hidden slice."""
+    from so101_smolvla_edge_b200.ops import linear, mlp, rms_stats
+
+    eps, m = 1e-5, rows * batch
+    ss = torch.zeros(m, 64, device="cuda")
+    if use_rms:
+        x16 = torch.empty(m, k, device="cuda", dtype=torch.bfloat16)
+        rms_stats(rnd(m, k, scale=2.0), x16, ss, 1.0 + 0.1 * rnd(k, seed=3))
+        rs = torch.rsqrt(ss[:, :1] / k + eps)
+    else:
+        x16, rs = rnd(m, k, dtype=torch.bfloat16), torch.ones(m, 1, device="cuda")
+    rms = (ss, 1, eps) if use_rms else None
+    w_gu = rnd(2 * hidden, k, dtype=torch.bfloat16, scale=k**-0.5, seed=1)
+    w_d = rnd(n_out, hidden, dtype=torch.bfloat16, scale=hidden**-0.5, seed=2)
+    res = rnd(m, n_out, seed=4)
+    scale = 1.0 + 0.1 * rnd(n_out, seed=5)
+    tiles = (n_out + 127) // 128
+    y = res.clone()
+    y16 = torch.zeros(m, n_out, dtype=torch.bfloat16, device="cuda")
+    st = torch.full((m, 64), -1.0, device="cuda")
+    assert mlp(x16, w_gu, w_d, y, residual=y, rms=rms, rows=rows, y16=y16, y16_scale=scale, stat_ss=st) == tiles
+    g, u = ((x16.float() * rs) @ w_gu.float().T).chunk(2, dim=-1)
+    want = res + (F.silu(g) * u).to(torch.bfloat16).float() @ w_d.float().T
+    chain = res + linear(x16, w_gu, silu_gate=True, rms=rms).float() @ w_d.float().T
+    size = (want - res).abs().max().item()
+    err, err_chain = (y - want).abs().max().item(), (chain - want).abs().max().item()
+    assert err <= 2 * err_chain + 1e-3 * size, (err, err_chain, size)
+    assert torch.equal(y16, (y * scale).to(torch.bfloat16))
+    sq = F.pad(y * y, (0, tiles * 128 - n_out)).view(m, tiles, 128).sum(-1)
+    assert torch.allclose(st[:, :tiles], sq, rtol=1e-5, atol=1e-6)
+    assert bool((st[:, tiles:] == -1.0).all())
+    y2 = res.clone()
+    mlp(x16, w_gu, w_d, y2, residual=y2, rms=rms, rows=rows)
+    assert torch.equal(y2, y)
 
 
 def test_rms_stats_matches_torch():
