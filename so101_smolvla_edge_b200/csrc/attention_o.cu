@@ -9,7 +9,8 @@
 //   1  issues the TMA load of its W_o block (128 features x 64, SWIZZLE_128B) before waiting for
 //      the previous grid: the weights do not depend on it;
 //   2  runs the flash attention of its head over all key tiles (attention_tile.cuh; a six-tile K/V
-//      ring, so the expert's 291 keys arrive in one round of loads), writing the
+//      ring, so the expert's 291 keys arrive in one round of loads; two warp groups taking the
+//      tiles in turn, merged at the end), writing the
 //      normalised rows as bf16 straight into the MMA's B operand tile in shared memory (the same
 //      bf16 rounding the unfused path applies before storing them);
 //   3  issues one M=128, N=64, K=64 tcgen05.mma: its head's fp32 partial (features x tokens) in
@@ -34,7 +35,8 @@ struct AttnOArgs {
   int* status;
 };
 
-constexpr int kAoThreads = 128;
+constexpr int kAoGroups = 2;                            // warp groups taking the key tiles in turn
+constexpr int kAoThreads = 128 * kAoGroups;
 constexpr int kAoBuf = 6;                               // K/V ring: the expert's 5 key tiles at once
 constexpr int kAoMaxHeads = 16;                         // largest (non-portable) cluster
 constexpr int kAoOffW = 0;                              // W_o block: 128 x 64 bf16, 16 KB
@@ -46,7 +48,7 @@ static_assert(attention_smem_bytes<64, kAoBuf>() >= 64 * 128 * 4, "the fp32 part
 
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
-__global__ void __launch_bounds__(kAoThreads) attention_o_kernel(const __grid_constant__ CUtensorMap tm_w,
+__global__ void __launch_bounds__(kAoThreads, 1) attention_o_kernel(const __grid_constant__ CUtensorMap tm_w,
                                                                  const AttnOArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -83,7 +85,7 @@ __global__ void __launch_bounds__(kAoThreads) attention_o_kernel(const __grid_co
   const long long row0 = static_cast<long long>(bi) * a.at.Lq + q0;
   const TokenPrefetch pf = token_prefetch<kAoThreads>(a.ep, a.at.nq, nv, row0, tile);
 
-  attention_body<64, false, true, kAoBuf>(a.at, 0, q0, h, bi, smem + kAoOffAttn, smem + kAoOffO);
+  attention_body<64, false, true, kAoBuf, kAoGroups>(a.at, 0, q0, h, bi, smem + kAoOffAttn, smem + kAoOffO);
   fence_async_smem();  // the O tile's generic-proxy stores, before the tensor core reads them
   __syncthreads();
   if (t == 0) {
@@ -104,14 +106,16 @@ __global__ void __launch_bounds__(kAoThreads) attention_o_kernel(const __grid_co
   // this head's partial, column-major (a token's 128 features contiguous), over the attention area
   float* part = reinterpret_cast<float*>(smem + kAoOffAttn);
   if (mma_ok) {
-    const uint32_t lane_addr = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+    // thread t: TMEM lane t % 128 (warp w reads lanes 32 (w % 4) ..), 16-token chunks of parity t / 128
+    const int tl = t & 127;
+    const uint32_t lane_addr = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
 #pragma unroll 1
-    for (int c = 0; c < nv; c += 16) {
+    for (int c = (t >> 7) * 16; c < nv; c += 32) {
       uint32_t r[16];
       tmem_ld16(lane_addr + c, r);
       tmem_ld_wait(r);
 #pragma unroll
-      for (int j = 0; j < 16; ++j) part[(c + j) * 128 + t] = __uint_as_float(r[j]);
+      for (int j = 0; j < 16; ++j) part[(c + j) * 128 + tl] = __uint_as_float(r[j]);
     }
   }
   tc_fence_before();

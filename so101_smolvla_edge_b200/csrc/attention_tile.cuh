@@ -87,12 +87,17 @@ constexpr int attention_smem_bytes() {
 // no split): the normalised rows go to o_tile in shared memory instead of a.o, as bf16 in the
 // K-major TMA SWIZZLE_128B layout (64 rows of 128 bytes; 16-byte chunk c of row r stored at chunk
 // c ^ (r % 8); 1024-byte aligned), the B operand of a tcgen05 MMA; rows at or past Lq are zero.
-// NBUF: depth of the K/V ring; NBUF - 1 tiles are loaded ahead of the one being used, so a CTA
-// with at most NBUF - 1 tiles (the expert's 291 keys at NBUF 6) pays one load latency in all.
-template <int HD, bool SPLIT, bool TILE_OUT = false, int NBUF = 2>
+// NBUF: depth of the K/V ring; NBUF - WG tiles are loaded ahead of the ones being used, so a CTA
+// with at most NBUF - WG tiles (the expert's 291 keys at NBUF 6) pays one load latency in all.
+// WG (TILE_OUT only): warp groups of 128 threads (the CTA has 128 * WG), which take the key tiles
+// in turn, tile g + WG * i to group g, each with its own running max, sums and output rows; group 0
+// merges the others' in group order at the end and writes the tile.
+template <int HD, bool SPLIT, bool TILE_OUT = false, int NBUF = 2, int WG = 1>
 __device__ __forceinline__ void attention_body(const AttnArgs& a, int split, int q0, int h, int bi,
                                                uint8_t* smem_raw, uint8_t* o_tile = nullptr) {
   static_assert(!TILE_OUT || (HD == 64 && !SPLIT), "the shared-memory output tile holds one 64-dim head");
+  static_assert(WG == 1 || (TILE_OUT && NBUF >= 2 * WG), "warp groups: tile output, a ring of two rounds");
+  constexpr int NT = 128 * WG;  // threads
   constexpr int BM = 64, BN = 64, LDS = HD + 8, HALF = HD / 2;
   constexpr int CHUNKS = HD / 8;  // 16-byte chunks per row
   __nv_bfloat16* sQ = reinterpret_cast<__nv_bfloat16*>(smem_raw);
@@ -100,7 +105,8 @@ __device__ __forceinline__ void attention_body(const AttnArgs& a, int split, int
   __nv_bfloat16* sK = sQ + BM * LDS;          // [NBUF][BN * LDS]
   __nv_bfloat16* sV = sK + NBUF * BN * LDS;   // [NBUF][BN * LDS]
 
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  // warp: this thread's warp within its group (its 16 query rows); grp: its group
+  const int tid = threadIdx.x, warp = (tid >> 5) & 3, lane = tid & 31, grp = tid >> 7;
   const int S = SPLIT ? a.kv_splits : 1;
   const int kvh = h / (a.nq / a.nkv);
   const __nv_bfloat16* Q = a.q + bi * a.bq + static_cast<long long>(h) * HD;
@@ -123,7 +129,7 @@ __device__ __forceinline__ void attention_body(const AttnArgs& a, int split, int
 
   auto load_kv = [&](int tile, int buf) {
     const int j0 = tile * BN;
-    for (int c = tid; c < BN * CHUNKS; c += 128) {
+    for (int c = tid; c < BN * CHUNKS; c += NT) {
       const int r = c / CHUNKS, cc = c % CHUNKS;
       const int j = j0 + r;
       const bool ok = j < a.Lk;
@@ -137,11 +143,11 @@ __device__ __forceinline__ void attention_body(const AttnArgs& a, int split, int
     cp_async_commit();
   };
 
-  for (int i = 0; i < NBUF - 1 && i < n_tiles; ++i) load_kv(t_begin + i, i);
+  for (int i = 0; i < NBUF - WG && i < n_tiles; ++i) load_kv(t_begin + i, i);
 
   // stage Q (rotated) into shared memory: 8 dims of each rotary half per step, 16-byte loads
   constexpr int VH = HALF / 8;
-  for (int idx = tid; idx < BM * VH; idx += 128) {
+  for (int idx = tid; idx < BM * VH; idx += NT) {
     const int r = idx / VH, d0 = (idx % VH) * 8;
     const int i = q0 + r;
     uint4 o1 = make_uint4(0, 0, 0, 0), o2 = o1;
@@ -194,25 +200,33 @@ __device__ __forceinline__ void attention_body(const AttnArgs& a, int split, int
   const int r0 = q0 + warp * 16 + (lane >> 2);  // this thread's two query rows
   const int r1 = r0 + 8;
 
-  for (int tile = 0; tile < n_tiles; ++tile) {
-    const int buf = tile % NBUF;
-    if (tile + NBUF - 1 < n_tiles) {
-      // refill the buffer the previous tile used (every warp is past it: the loop's last barrier)
-      load_kv(t_begin + tile + NBUF - 1, (tile + NBUF - 1) % NBUF);
-      cp_async_wait<NBUF - 1>();
+  // rounds of WG tiles (one tile per round without warp groups)
+  for (int first = 0; first < n_tiles; first += WG) {
+    if (first + NBUF - 1 < n_tiles) {
+      // refill the buffers of the previous round's tiles (every warp is past them: the round's
+      // last barrier)
+#pragma unroll
+      for (int j = 0; j < WG; ++j) load_kv(t_begin + first + NBUF - WG + j, (first + NBUF - WG + j) % NBUF);
+      cp_async_wait<NBUF - WG>();
     } else {
+#pragma unroll
+      for (int j = 0; j < WG; ++j)
+        if (first + NBUF - WG + j < n_tiles) load_kv(t_begin + first + NBUF - WG + j, (first + NBUF - WG + j) % NBUF);
       cp_async_wait<0>();
     }
     __syncthreads();
-    {
-      // the step's own keys in this tile, rotated in place as the RoPE K/V cache kernel would
-      // have written them (per-operation rounding, one rounding to bf16)
-      const long long j0 = static_cast<long long>(t_begin + tile) * BN;
-      if (own && j0 + BN > a.own_from) {
+    // the step's own keys in this round's tiles, rotated in place as the RoPE K/V cache kernel
+    // would have written them (per-operation rounding, one rounding to bf16)
+    bool rotated = false;
+#pragma unroll
+    for (int jt = 0; jt < WG; ++jt) {
+      const long long j0 = static_cast<long long>(t_begin + first + jt) * BN;
+      if (own && first + jt < n_tiles && j0 + BN > a.own_from) {
+        rotated = true;
         const int r_lo = static_cast<int>(a.own_from > j0 ? a.own_from - j0 : 0);
         const int r_hi = static_cast<int>(a.Lk - j0 < BN ? a.Lk - j0 : BN);
-        __nv_bfloat16* kt = sK + buf * BN * LDS;
-        for (int idx = tid; idx < (r_hi - r_lo) * HALF; idx += 128) {
+        __nv_bfloat16* kt = sK + ((first + jt) % NBUF) * BN * LDS;
+        for (int idx = tid; idx < (r_hi - r_lo) * HALF; idx += NT) {
           const int r = r_lo + idx / HALF, d = idx % HALF;
           const long long jr = j0 + r - a.own_from;
           const float k1 = __bfloat162float(kt[r * LDS + d]), k2 = __bfloat162float(kt[r * LDS + d + HALF]);
@@ -220,9 +234,12 @@ __device__ __forceinline__ void attention_body(const AttnArgs& a, int split, int
           kt[r * LDS + d] = __float2bfloat16_rn(__fsub_rn(__fmul_rn(k1, c), __fmul_rn(k2, sn)));
           kt[r * LDS + d + HALF] = __float2bfloat16_rn(__fadd_rn(__fmul_rn(k2, c), __fmul_rn(k1, sn)));
         }
-        __syncthreads();
       }
     }
+    if (rotated) __syncthreads();
+    const int tile = first + grp;  // this group's tile of the round
+    const int buf = tile % NBUF;
+    if (WG == 1 || tile < n_tiles) {
     const __nv_bfloat16* k_s = sK + buf * BN * LDS;
     const __nv_bfloat16* v_s = sV + buf * BN * LDS;
 
@@ -313,7 +330,42 @@ __device__ __forceinline__ void attention_body(const AttnArgs& a, int split, int
         mma_bf16_16816(o[2 * t2 + 1], pf[j], b2, b3);
       }
     }
-    __syncthreads();  // this buffer is refilled at the top of the next tile
+    }
+    __syncthreads();  // these buffers are refilled at the top of the round after next
+  }
+  if constexpr (WG > 1) {
+    // groups 1.. hand their running max, row sums (this thread's share) and output rows to group
+    // 0 through the idle K/V ring; group 0 rescales and adds them in group order
+    constexpr int XS = 4 + HD / 2;
+    float* xch = reinterpret_cast<float*>(sK);
+    if (grp > 0) {
+      float* d = xch + ((grp - 1) * 128 + (tid & 127)) * XS;
+      d[0] = m0, d[1] = m1, d[2] = l0, d[3] = l1;
+#pragma unroll
+      for (int t = 0; t < HD / 8; ++t)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) d[4 + t * 4 + e] = o[t][e];
+    }
+    __syncthreads();
+    if (grp > 0) return;
+#pragma unroll 1
+    for (int g = 1; g < WG; ++g) {
+      const float* d = xch + ((g - 1) * 128 + tid) * XS;
+      const float n0 = fmaxf(m0, d[0]), n1 = fmaxf(m1, d[1]);
+      const float b0 = n0 == -INFINITY ? 0.f : n0, b1 = n1 == -INFINITY ? 0.f : n1;
+      const float sa0 = ex2(m0 - b0), sb0 = ex2(d[0] - b0), sa1 = ex2(m1 - b1), sb1 = ex2(d[1] - b1);
+      l0 = l0 * sa0 + d[2] * sb0;
+      l1 = l1 * sa1 + d[3] * sb1;
+#pragma unroll
+      for (int t = 0; t < HD / 8; ++t) {
+        o[t][0] = o[t][0] * sa0 + d[4 + t * 4 + 0] * sb0;
+        o[t][1] = o[t][1] * sa0 + d[4 + t * 4 + 1] * sb0;
+        o[t][2] = o[t][2] * sa1 + d[4 + t * 4 + 2] * sb1;
+        o[t][3] = o[t][3] * sa1 + d[4 + t * 4 + 3] * sb1;
+      }
+      m0 = n0;
+      m1 = n1;
+    }
   }
 
   l0 += __shfl_xor_sync(0xffffffffu, l0, 1);

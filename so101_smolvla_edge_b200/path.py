@@ -149,14 +149,14 @@ class B200Path:
             raise ValueError(f"expert_step must be 'auto', 'fused' or 'ops', not {expert_step!r}")
         self.fold = bool(fold_norms)  # RMSNorm split into the GEMMs around it (else an rms_norm launch each)
         # one observation: each expert layer's SwiGLU MLP block in one launch (so101_mlp) unless
-        # SO101_FUSED_MLP=0, and the cross-attention layers' attention, output projection and
-        # residual in one launch (so101_attention_o). SO101_ATTN_O: "cross" (default; on B200 the
-        # fused launch beats attention + GEMM over the 241 prefix keys, 13.2 against 15.0 us, but not
-        # over the self layers' 291 keys, 16.1 against 15.8), "all" or "0".
+        # SO101_FUSED_MLP=0, and its attention, output projection and residual in one launch
+        # (so101_attention_o). SO101_ATTN_O: "all" (default; on B200 14.7 against 15.2 us for the
+        # attention + GEMM launches over the self layers' 291 keys, 12.1 against 14.2 over the cross
+        # layers' 241), "cross" or "0".
         one = self.B == 1 and s.chunk <= 64
         self.mlp_fused = (one and s.exp_mlp % 128 == 0 and s.exp_mlp <= 2048
                           and os.environ.get("SO101_FUSED_MLP", "1") != "0")  # fmt: skip
-        mode = os.environ.get("SO101_ATTN_O", "cross")
+        mode = os.environ.get("SO101_ATTN_O", "all")
         if mode not in ("cross", "all", "0"):
             raise ValueError(f"SO101_ATTN_O must be 'cross', 'all' or '0', not {mode!r}")
         ok = one and s.head_dim == 64 and s.n_heads <= 16
