@@ -122,6 +122,32 @@ def test_batched_matches_reference_and_single():
             assert np.abs(got[i] - ref).max() <= ACTION_TOL * max(1.0, np.abs(ref).max()), i
 
 
+def test_infer_stream_equals_infer_batch():
+    """infer_stream (the next batch staged on a copy stream while the current graph runs) yields,
+    batch by batch, the same bits as infer_batch on the same inputs: four batches that cycle
+    both pinned buffer sets, given noise and device-drawn noise (the same generator draws in the
+    same order), and the engine is still right for infer_batch afterwards."""
+    from so101_smolvla_edge_b200.engine import Engine
+
+    b = case_bundle("small_absolute")
+    eng = Engine(b, warmup=1, batch=3)
+    batches = []
+    for k in range(4):
+        obs = [observation(b, 3 * k + s) for s in range(3)]
+        noises = [o[2] for o in obs] if k != 2 else None
+        batches.append(([o[0] for o in obs], [o[1] for o in obs], noises))
+    torch.manual_seed(0)
+    want = [eng.infer_batch(*bt) if bt[2] is not None else eng.infer_batch(bt[0], bt[1]) for bt in batches]
+    torch.manual_seed(0)
+    got = list(eng.infer_stream([bt if bt[2] is not None else bt[:2] for bt in batches]))
+    assert len(got) == len(want)
+    for k, (g_, w_) in enumerate(zip(got, want, strict=True)):
+        assert np.array_equal(g_, w_), k
+    assert np.array_equal(eng.infer_batch(*batches[0]), want[0])
+    del eng
+    torch.cuda.empty_cache()
+
+
 def _int8_check(g, a, scale):
     """W8A8 parity: the int8 chunk matches the reference's own int8 chunk (its fake-quant
     arithmetic, `tests/test_ov_engine.py:227-236`) within the action tolerance, and drifts from
