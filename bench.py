@@ -412,6 +412,7 @@ def run_ours(args) -> None:
             errs = max(float(np.abs(e1b.infer(*o0[i]) - g["actions"][i]).max()) for i in range(4))
         prof = e1b.profile(*o0[0][:2])
         H, E, F, QD, KV, Lp = s.chunk, s.exp_dim, s.exp_mlp, s.q_dim, s.kv_dim, s.prefix_len
+        traffic = None  # DRAM bytes per launch from a committed ncu summary, where there is one
         if e1b.path.xs is not None:
             # the fused expert step: every expert weight once per step, plus the K/V rows attention reads
             fn, cargs = find_call(e1b.path.progs["denoise"], "s0.expert_layers")
@@ -429,6 +430,7 @@ def run_ours(args) -> None:
             gms = time_call(fn, cargs)
             byts = 2 * F * E * 2 + E * F * 2 + H * E * 2 + 2 * H * E * 4
             kname = "mlp_kernel s0.0.mlp (M=50, gate/up + down fused)"
+            traffic = profile_traffic("exp.mlp/mlp_kernel")
         else:
             fn, cargs = find_call(e1b.path.progs["denoise"], "s0.0.gate_up")
             gms = time_call(fn, cargs)
@@ -438,7 +440,7 @@ def run_ours(args) -> None:
                "stages_ms": prof, "launches_per_chunk": e1b.launches(), "max_err_rad": errs,
                "config": "configs[3]: batch 1, bf16, one CUDA graph, host frames in -> actions out",
                "roofline_expert": {"kernel": kname, "bound": "hbm", "achieved": byts / (gms * 1e-3) / 1e9,
-                                   "bytes": byts, "peak": pk["hbm_gbs"], "unit": "GB/s", "ms": gms,
+                                   "bytes": byts, "peak": pk["hbm_gbs"], "unit": "GB/s", "ms": gms, "traffic": traffic,
                                    "frac": byts / (gms * 1e-3) / 1e9 / pk["hbm_gbs"]}}  # fmt: skip
         del e1b
     if world > 1:
