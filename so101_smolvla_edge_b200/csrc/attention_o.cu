@@ -9,8 +9,8 @@
 //   1  issues the TMA load of its W_o block (128 features x 64, SWIZZLE_128B) before waiting for
 //      the previous grid: the weights do not depend on it;
 //   2  runs the flash attention of its head over all key tiles (attention_tile.cuh; a six-tile K/V
-//      ring, so the expert's 291 keys arrive in one round of loads; two warp groups taking the
-//      tiles in turn, merged at the end), writing the
+//      ring, so the expert's 291 keys arrive in one round of loads; two or three warp groups
+//      taking the tiles in turn, whichever needs fewer rounds, merged at the end), writing the
 //      normalised rows as bf16 straight into the MMA's B operand tile in shared memory (the same
 //      bf16 rounding the unfused path applies before storing them);
 //   3  issues one M=128, N=64, K=64 tcgen05.mma: its head's fp32 partial (features x tokens) in
@@ -35,8 +35,6 @@ struct AttnOArgs {
   int* status;
 };
 
-constexpr int kAoGroups = 2;                            // warp groups taking the key tiles in turn
-constexpr int kAoThreads = 128 * kAoGroups;
 constexpr int kAoBuf = 6;                               // K/V ring: the expert's 5 key tiles at once
 constexpr int kAoMaxHeads = 16;                         // largest (non-portable) cluster
 constexpr int kAoOffW = 0;                              // W_o block: 128 x 64 bf16, 16 KB
@@ -48,8 +46,11 @@ static_assert(attention_smem_bytes<64, kAoBuf>() >= 64 * 128 * 4, "the fp32 part
 
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
-__global__ void __launch_bounds__(kAoThreads, 1) attention_o_kernel(const __grid_constant__ CUtensorMap tm_w,
+// G warp groups of 128 threads take the key tiles in turn (attention_body's WG).
+template <int G>
+__global__ void __launch_bounds__(128 * G, 1) attention_o_kernel(const __grid_constant__ CUtensorMap tm_w,
                                                                  const AttnOArgs a) {
+  constexpr int kAoThreads = 128 * G;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* w_full = reinterpret_cast<uint64_t*>(smem + kAoOffBar);
@@ -85,7 +86,7 @@ __global__ void __launch_bounds__(kAoThreads, 1) attention_o_kernel(const __grid
   const long long row0 = static_cast<long long>(bi) * a.at.Lq + q0;
   const TokenPrefetch pf = token_prefetch<kAoThreads>(a.ep, a.at.nq, nv, row0, tile);
 
-  attention_body<64, false, true, kAoBuf, kAoGroups>(a.at, 0, q0, h, bi, smem + kAoOffAttn, smem + kAoOffO);
+  attention_body<64, false, true, kAoBuf, G>(a.at, 0, q0, h, bi, smem + kAoOffAttn, smem + kAoOffO);
   fence_async_smem();  // the O tile's generic-proxy stores, before the tensor core reads them
   __syncthreads();
   if (t == 0) {
@@ -106,11 +107,12 @@ __global__ void __launch_bounds__(kAoThreads, 1) attention_o_kernel(const __grid
   // this head's partial, column-major (a token's 128 features contiguous), over the attention area
   float* part = reinterpret_cast<float*>(smem + kAoOffAttn);
   if (mma_ok) {
-    // thread t: TMEM lane t % 128 (warp w reads lanes 32 (w % 4) ..), 16-token chunks of parity t / 128
+    // thread t: TMEM lane t % 128 (warp w reads lanes 32 (w % 4) ..), 16-token chunks c with
+    // c / 16 = t / 128 modulo the group count
     const int tl = t & 127;
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
 #pragma unroll 1
-    for (int c = (t >> 7) * 16; c < nv; c += 32) {
+    for (int c = (t >> 7) * 16; c < nv; c += 16 * G) {
       uint32_t r[16];
       tmem_ld16(lane_addr + c, r);
       tmem_ld_wait(r);
@@ -152,23 +154,25 @@ EncodeFn encode_fn() {
 
 bool aligned16(const void* p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; }
 
-// Whether a cluster of `heads` CTAs of the kernel can be resident at all (non-portable sizes above
-// 8 depend on the GPU); cached per cluster size.
+// Whether a cluster of `heads` CTAs of attention_o_kernel<G> can be resident at all (non-portable
+// sizes above 8 depend on the GPU); cached per group count and cluster size.
+template <int G>
 int cluster_fits(int heads, cudaStream_t stream) {
   static int known[kAoMaxHeads + 1] = {};  // 0 unknown, 1 fits, -1 does not
   static std::mutex mu;
   std::lock_guard<std::mutex> lock(mu);
   static bool configured = false;
   if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(attention_o_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kAoSmem);
-    if (e == cudaSuccess) e = cudaFuncSetAttribute(attention_o_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    cudaError_t e = cudaFuncSetAttribute(attention_o_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize, kAoSmem);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(attention_o_kernel<G>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
     if (e != cudaSuccess) return launch_error(e);
     configured = true;
   }
   if (known[heads] == 0) {
     cudaLaunchConfig_t lc = {};
     lc.gridDim = dim3(heads, 1, 1);
-    lc.blockDim = dim3(kAoThreads);
+    lc.blockDim = dim3(128 * G);
     lc.dynamicSmemBytes = kAoSmem;
     lc.stream = stream;
     cudaLaunchAttribute attr[1];
@@ -179,7 +183,7 @@ int cluster_fits(int heads, cudaStream_t stream) {
     lc.attrs = attr;
     lc.numAttrs = 1;
     int clusters = 0;
-    const cudaError_t e = cudaOccupancyMaxActiveClusters(&clusters, attention_o_kernel, &lc);
+    const cudaError_t e = cudaOccupancyMaxActiveClusters(&clusters, attention_o_kernel<G>, &lc);
     if (e != cudaSuccess) return launch_error(e);
     known[heads] = clusters > 0 ? 1 : -1;
   }
@@ -235,7 +239,14 @@ extern "C" int so101_attention_o(const void* q, int64_t ldq, const void* k, int6
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
       return SO101_ERR_ARG;
   }
-  const int fit = cluster_fits(nq, stream);
+  // key tiles of the last query block (attention_body's count): three warp groups when that takes
+  // fewer rounds than two (the expert's 291 self-attention keys: 5 tiles, 2 rounds against 3)
+  long long last = causal_from - 1;
+  if ((q_blocks - 1) * 64 + 63 + q_offset > last) last = (q_blocks - 1) * 64 + 63 + q_offset;
+  if (last > Lk - 1) last = Lk - 1;
+  const long long key_tiles = (last + 64) / 64;
+  const int groups = (key_tiles + 2) / 3 < (key_tiles + 1) / 2 ? 3 : 2;
+  const int fit = groups == 3 ? cluster_fits<3>(nq, stream) : cluster_fits<2>(nq, stream);
   if (fit != SO101_OK) return fit;
 
   AttnOArgs a;
@@ -278,7 +289,7 @@ extern "C" int so101_attention_o(const void* q, int64_t ldq, const void* k, int6
 
   cudaLaunchConfig_t lc = {};
   lc.gridDim = dim3(nq, tiles, static_cast<unsigned>(q_blocks * batch));
-  lc.blockDim = dim3(kAoThreads);
+  lc.blockDim = dim3(128 * groups);
   lc.dynamicSmemBytes = kAoSmem;
   lc.stream = stream;
   cudaLaunchAttribute attr[2];
@@ -290,6 +301,7 @@ extern "C" int so101_attention_o(const void* q, int64_t ldq, const void* k, int6
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   lc.attrs = attr;
   lc.numAttrs = pdl_enabled() ? 2 : 1;
-  const cudaError_t e = cudaLaunchKernelEx(&lc, attention_o_kernel, tm, a);
+  const cudaError_t e = groups == 3 ? cudaLaunchKernelEx(&lc, attention_o_kernel<3>, tm, a)
+                                    : cudaLaunchKernelEx(&lc, attention_o_kernel<2>, tm, a);
   return e == cudaSuccess ? SO101_OK : launch_error(e);
 }
