@@ -504,8 +504,10 @@ __device__ __forceinline__ void attention_body(const AttnArgs& a, int split, int
   }
 }
 
+// Four CTAs per SM where the registers allow it (head_dim <= 64: the unsplit kernel of the batched
+// prefix and expert fits 128 registers).
 template <int HD, bool SPLIT>
-__global__ void __launch_bounds__(128) attention_kernel(const AttnArgs a) {
+__global__ void __launch_bounds__(128, HD <= 64 ? 4 : 1) attention_kernel(const AttnArgs a) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   grid_dep_launch();
   grid_dep_wait();
