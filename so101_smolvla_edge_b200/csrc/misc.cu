@@ -74,6 +74,70 @@ __global__ void preprocess_kernel(const uint8_t* __restrict__ img, int n_img, in
   }
 }
 
+// The same for frames already at the model's size (no resize, no padding) and 16 x 16 patches:
+// one warp per patch. Its 16 rows of 48 bytes come in as 16-byte loads (each input byte once)
+// through shared memory, and its 768 channel-major values leave as 16-byte stores; the per-value
+// arithmetic is preprocess_kernel's.
+constexpr int kPpWarps = 8;
+
+__global__ void __launch_bounds__(32 * kPpWarps) preprocess_patch_kernel(const uint8_t* __restrict__ img,
+                                                                       int n_img, int S, void* __restrict__ out,
+                                                                       int y_type, float qs) {
+  grid_dep_launch();
+  grid_dep_wait();
+  __shared__ __align__(16) uint8_t tiles[kPpWarps][16 * 48];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int G = S / 16;
+  const long long patch = static_cast<long long>(blockIdx.x) * kPpWarps + warp;
+  if (patch >= static_cast<long long>(n_img) * G * G) return;  // whole warps
+  const int im = static_cast<int>(patch / (G * G)), pr = static_cast<int>(patch % (G * G));
+  const int gy = pr / G, gx = pr % G;
+  const uint8_t* src = img + (static_cast<long long>(im) * S * S + static_cast<long long>(gy) * 16 * S + gx * 16) * 3;
+  uint8_t* t = tiles[warp];
+  for (int c = lane; c < 48; c += 32) {  // row c / 3, 16-byte piece c % 3
+    const int r = c / 3, k = c % 3;
+    *reinterpret_cast<uint4*>(t + r * 48 + k * 16) =
+        __ldg(reinterpret_cast<const uint4*>(src + static_cast<long long>(r) * S * 3 + k * 16));
+  }
+  __syncwarp();
+  auto value = [&](int ch, int py, int px) {
+    const float val = static_cast<float>(t[py * 48 + px * 3 + ch]) / 255.0f;
+    return val * 2.0f - 1.0f;
+  };
+  if (y_type == SO101_I8) {
+    int8_t* o = static_cast<int8_t*>(out) + patch * 768;
+    for (int c = lane; c < 48; c += 32) {  // 16 values: channel c / 16, patch row c % 16
+      const int ch = c / 16, py = c % 16;
+      uint32_t wv[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        uint32_t packed = 0;
+#pragma unroll
+        for (int b = 0; b < 4; ++b)
+          packed |= static_cast<uint32_t>(static_cast<uint8_t>(quant_i8(value(ch, py, 4 * q + b), qs))) << (8 * b);
+        wv[q] = packed;
+      }
+      *reinterpret_cast<uint4*>(o + c * 16) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+    }
+  } else if (y_type == SO101_BF16) {
+    __nv_bfloat16* o = static_cast<__nv_bfloat16*>(out) + patch * 768;
+    for (int c = lane; c < 96; c += 32) {  // 8 values: channel c / 32, patch row (c / 2) % 16, half c % 2
+      const int ch = c / 32, py = (c / 2) % 16, px0 = (c % 2) * 8;
+      __nv_bfloat162 hv[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) hv[q] = __floats2bfloat162_rn(value(ch, py, px0 + 2 * q), value(ch, py, px0 + 2 * q + 1));
+      *reinterpret_cast<uint4*>(o + c * 8) = *reinterpret_cast<const uint4*>(hv);
+    }
+  } else {
+    float* o = static_cast<float*>(out) + patch * 768;
+    for (int c = lane; c < 192; c += 32) {  // 4 values: channel c / 64, patch row (c / 4) % 16, quarter c % 4
+      const int ch = c / 64, py = (c / 4) % 16, px0 = (c % 4) * 4;
+      *reinterpret_cast<float4*>(o + c * 4) =
+          make_float4(value(ch, py, px0), value(ch, py, px0 + 1), value(ch, py, px0 + 2), value(ch, py, px0 + 3));
+    }
+  }
+}
+
 // ------------------------------------------------------------------ fp32 linear (CUDA cores)
 // 64 x 8 output tile per 128-thread block (each thread 1 row x 4 columns), K in chunks of 32
 // streamed through a 3-stage cp.async ring so global latency overlaps the FMAs. Rows of x and w
@@ -349,6 +413,13 @@ extern "C" int so101_preprocess(const uint8_t* img, int n_img, int h, int w, int
   if (rh <= 0 || rw <= 0 || rh > S || rw > S || (3 * P * P) % 2) return SO101_ERR_ARG;
   if (y_type == SO101_I8 && !(y_qscale > 0.f)) return SO101_ERR_ARG;
   const long long G = S / P;
+  if (h == S && w == S && rh == S && rw == S && P == 16 && (S * 3) % 16 == 0 &&
+      reinterpret_cast<uintptr_t>(img) % 16 == 0 && reinterpret_cast<uintptr_t>(patches) % 16 == 0) {
+    const long long blocks = (n_img * G * G + kPpWarps - 1) / kPpWarps;
+    if (blocks > 0x7fffffffLL) return SO101_ERR_ARG;
+    return launch_kernel(preprocess_patch_kernel, dim3(static_cast<unsigned>(blocks)), dim3(32 * kPpWarps), 0, stream,
+                         img, n_img, S, patches, y_type, y_qscale);
+  }
   const long long pairs = n_img * G * G * (3 * P * P / 2);
   const long long blocks = (pairs + 255) / 256;
   if (blocks > 0x7fffffffLL) return SO101_ERR_ARG;

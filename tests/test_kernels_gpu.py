@@ -540,6 +540,43 @@ def test_mlp_block_matches_chain(rows, batch, k, hidden, n_out, use_rms):
     assert torch.equal(y2, y)
 
 
+@pytest.mark.parametrize("y", ["bf16", "i8", "f32", "resize"])
+def test_preprocess_patches_match_torch(y):
+    """so101_preprocess: uint8 HWC frames -> /255 -> *2-1 -> 16 x 16 patch rows, channel-major
+    within a patch (`engine.py:236-245` and the patch unfold of `smolvla.py:166-170`). 512^2 frames
+    take the per-patch kernel: bf16 and fp32 bit for bit against torch's float32 arithmetic, int8
+    within one step of torch's round(v / scale) (exact but at rounding ties). A 480 x 640 frame
+    takes the bilinear resize (align_corners False) to 384 x 512, zero-padded at the top before the
+    shift: against torch's interpolate within fp32 rounding."""
+    from so101_smolvla_edge_b200 import _lib as L
+
+    g = torch.Generator(device="cuda").manual_seed(0)
+    n, S, P = 3, 512, 16
+    h, w = (480, 640) if y == "resize" else (S, S)
+    img = torch.randint(0, 256, (n, h, w, 3), generator=g, device="cuda", dtype=torch.uint8)
+    dt = {"bf16": torch.bfloat16, "i8": torch.int8}.get(y, torch.float32)
+    code = {"bf16": L.BF16, "i8": L.I8}.get(y, L.F32)
+    qs = 0.0123 if y == "i8" else 0.0  # 2 / 255 would put every value on a rounding tie
+    rh, rw = (384, 512) if y == "resize" else (S, S)
+    out = torch.empty(n * (S // P) ** 2, 3 * P * P, dtype=dt, device="cuda")
+    L.check(L.lib().so101_preprocess(img.data_ptr(), n, h, w, rh, rw, S, P, out.data_ptr(), code, qs,
+                                     torch.cuda.current_stream().cuda_stream), "so101_preprocess")  # fmt: skip
+    # a true division (torch divides by a scalar as a multiply by its reciprocal)
+    x = img.float() / torch.full(img.shape, 255.0, device="cuda")
+    if y == "resize":
+        x = F.interpolate(x.permute(0, 3, 1, 2), size=(rh, rw), mode="bilinear", align_corners=False)
+        x = F.pad(x, (S - rw, 0, S - rh, 0)).permute(0, 2, 3, 1)  # zero in [0, 1]: -1 after the shift
+    x = x * 2.0 - 1.0
+    ref = x.reshape(n, S // P, P, S // P, P, 3).permute(0, 1, 3, 5, 2, 4).reshape(n * (S // P) ** 2, 3 * P * P)
+    if y == "i8":
+        d = (out.float() - torch.round(ref / qs).clamp(-128, 127)).abs()
+        assert d.max().item() <= 1 and (d == 0).float().mean().item() > 0.999
+    elif y == "resize":
+        assert (out - ref).abs().max().item() <= 1e-5
+    else:
+        assert torch.equal(out, ref.to(dt))
+
+
 def test_rms_stats_matches_torch():
     from so101_smolvla_edge_b200.ops import rms_stats
 
