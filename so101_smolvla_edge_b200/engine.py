@@ -313,6 +313,13 @@ class Engine:
         if cur is None:
             return
         consumed.record(comp)  # the staging buffers are free
+        try:
+            yield from self._stream_loop(it, cur, stage, bufs, comp, staged, consumed, done)
+        finally:  # a caller that stops early leaves no upload in flight into the pinned buffers
+            copy.synchronize()
+
+    def _stream_loop(self, it, cur, stage, bufs, comp, staged, consumed, done):
+        """infer_stream's loop: replay batch i while batch i+1 is staged."""
         draw = stage(cur, 0)
         k = 0
         while cur is not None:
