@@ -100,6 +100,37 @@ def test_other_entry_points_validate_arguments(lib):
     assert lib.so101_finish(fake, 8, fake, 6, fake, fake, fake, fake, fake, fake, fake, 6, 10, 3, 1, None) == L.ERR_ARG
 
 
+def test_fused_expert_entry_points_validate_arguments(lib):
+    """so101_attention_o and so101_mlp refuse, before touching the GPU, what their kernels cannot
+    run: head_dim other than 64, more heads than a cluster holds, an output width that is not a
+    multiple of 4, more than 64 rows per observation, a hidden width that is not a multiple of 128
+    or needs more than 16 CTAs, unaligned operands."""
+    fake, S = 1 << 20, None
+
+    def attn_o(**kw):
+        a = dict(q=fake, ldq=1600, k=fake, ldk=320, v=fake, ldv=320, Lq=50, Lk=291, nq=15, nkv=5, hd=64,
+                 causal_from=241, q_offset=241, cos=None, sin=None, batch=1, bq=0, bk=0, bv=0, k_own=None,
+                 v_own=None, ld_own=0, b_own=0, own_from=0, k_cos=None, k_sin=None, w_o=fake, ldw=960,
+                 n_out=720, y=fake, ldy=720, res=None, ldr=0, y16=None, ld16=0, y16_scale=None, stat=None,
+                 stat_ld=0)  # fmt: skip
+        a.update(kw)
+        return lib.so101_attention_o(*a.values(), S)
+
+    def mlp(**kw):
+        a = dict(x=fake, ldx=720, rows=50, batch=1, k=720, rms=None, slots=0, rms_ld=0, eps=1e-5, w_gu=fake,
+                 ldw1=720, hidden=2048, w_d=fake, ldw2=2048, n_out=720, y=fake, ldy=720, res=None, ldr=0,
+                 y16=None, ld16=0, y16_scale=None, stat=None, stat_ld=0)  # fmt: skip
+        a.update(kw)
+        return lib.so101_mlp(*a.values(), S)
+
+    for bad in (dict(hd=32, ldk=160, ldv=160), dict(nq=20, nkv=5), dict(n_out=718), dict(nq=15, nkv=4),
+                dict(w_o=fake + 8), dict(y=fake + 4), dict(ldw=480), dict(k_own=fake, own_from=10)):  # fmt: skip
+        assert attn_o(**bad) == L.ERR_ARG, bad
+    for bad in (dict(rows=65), dict(hidden=2000, ldw2=2000), dict(hidden=2176, ldw2=2176), dict(n_out=722),
+                dict(x=fake + 8), dict(ldx=700), dict(rms=fake, slots=65, rms_ld=65)):  # fmt: skip
+        assert mlp(**bad) == L.ERR_ARG, bad
+
+
 def test_tune_gemm_candidates():
     """The plan sweep (the counterpart of the reference's scripts/tune_gemm.py) offers the pick,
     weight-streaming swap tiles for few rows (not for int8, which has no swap tiles) and the
