@@ -310,10 +310,10 @@ class B200Path:
 
         "fused" requires it (one observation, shapes the library accepts); "auto" and "ops" use the
         per-op launch chain, which is the faster of the two on B200 (0.78 ms against 1.36 ms per
-        denoising step at configs[0] when compared, 0.57 ms now with the fused expert kernels: the
-        persistent kernel's phases are chains of dependent
-        global-memory round trips plus a grid barrier, while consecutive per-op kernels overlap
-        their prologues through programmatic dependent launch)."""
+        denoising step at configs[0] when compared, 0.57 ms now with the fused expert kernels): the
+        persistent kernel's phases are chains of dependent global-memory round trips plus a grid
+        barrier, while consecutive per-op kernels overlap their prologues through programmatic
+        dependent launch."""
         s, w = self.spec, self.w
         if mode in ("ops", "auto"):
             return None
