@@ -26,7 +26,7 @@
 
 namespace so101 {
 
-constexpr int kMlpThreads = 256;  // two threads per TMEM lane in the epilogues
+constexpr int kMlpThreads = 512;  // four threads per TMEM lane in the epilogues
 constexpr int kMlpMaxCluster = 16;
 constexpr int kMlpStages = 3;  // 4 stages and L2 prefetches of the later blocks measured no faster
 constexpr int kMlpWBlk = 128 * 128;                      // 128 rows x 64 bf16
@@ -179,7 +179,7 @@ __global__ void __launch_bounds__(kMlpThreads, 1) mlp_kernel(const __grid_consta
     uint8_t* act = smem + kMlpOffAct + (tl >> 6) * kMlpXBlk;
     const int e = tl & 63;
 #pragma unroll 1
-    for (int c = hh * 16; c < nv; c += 32) {
+    for (int c = hh * 16; c < nv; c += 16 * (kMlpThreads / 128)) {
       uint32_t g[16], u[16];
       tmem_ld16(lane_addr + c, g);
       tmem_ld16(lane_addr + 64 + c, u);
@@ -220,7 +220,7 @@ __global__ void __launch_bounds__(kMlpThreads, 1) mlp_kernel(const __grid_consta
   float* part = reinterpret_cast<float*>(smem);
   if (down_ok) {
 #pragma unroll 1
-    for (int c = hh * 16; c < nv; c += 32) {
+    for (int c = hh * 16; c < nv; c += 16 * (kMlpThreads / 128)) {
       uint32_t d[16];
       tmem_ld16(lane_addr + 128 + c, d);
       tmem_ld_wait(d);
