@@ -19,8 +19,12 @@ configs[3] batch-1 bf16 chunk, p50/p99 over 200 `Engine.infer` calls (rank 0); r
 dominant kernel timed alone with CUDA events against MEASURED_PEAKS.json; cpu_baseline = the
 float32 CPU oracle (the reference's own algorithm restated) on this host's cores.
 
-`--impl reference` times the reference's CPU path (the float32 oracle port, batch 1) on the
-host's cores with the same metric and unit; under torchrun only rank 0 runs it.
+reference_gpu = the reference's own Triton and torch engines (baseline/_ref) on the same GPU at
+configs[3], each in a child process.
+
+`--impl reference` times the reference's own float32 CPU path (its `Engine(device="cpu")` from
+baseline/_ref, else the oracle port) on the host's cores with the same metric and unit; under
+torchrun only rank 0 runs it.
 """
 
 from __future__ import annotations
@@ -114,29 +118,127 @@ def peaks() -> tuple[dict, str]:
     return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
 
 
-# ------------------------------------------------------------------------------ CPU baseline
+# ------------------------------------------------------------------------------ the reference
+REF_DIR = ROOT / "baseline" / "_ref"  # the reference package (installed there, git-ignored)
+
+
+def reference_engine_class():
+    """The reference's own `Engine` from baseline/_ref, or None when it is not there."""
+    if not (REF_DIR / "so101_smolvla_edge").exists():
+        return None
+    if str(REF_DIR) not in sys.path:
+        sys.path.insert(0, str(REF_DIR))
+    try:
+        from so101_smolvla_edge.model.engine import Engine as RefEngine
+    except Exception:  # noqa: BLE001  (a reference that does not import is reported as absent)
+        return None
+    return RefEngine
+
+
+def cpu_chunker():
+    """(chunk(obs) -> actions, kind, description) for the float32 CPU path: the reference's own
+    `Engine(device="cpu", dtype="fp32")` from baseline/_ref when present, else the oracle port."""
+    from so101_smolvla_edge_b200.bundle import seeded_bundle, write_bundle
+
+    b = seeded_bundle()
+    RefEngine = reference_engine_class()
+    if RefEngine is not None:
+        d = write_bundle(b, Path(tempfile.mkdtemp(prefix="so101_ref_")) / "config0")
+        eng = RefEngine(str(d), device="cpu", dtype="fp32", cuda_graph=False, warmup=0)
+        return (lambda o: eng.infer(o[0], o[1], noise=o[2])), "reference", (
+            "the reference's own Engine(device='cpu', dtype='fp32', cuda_graph=False) from baseline/_ref")
+    from oracle.smolvla_fp32 import Oracle
+
+    o_ = Oracle(b)
+    return (lambda o: o_.actions(*o)), "port", "float32 torch CPU oracle (oracle/smolvla_fp32.py)"
+
+
 def cpu_chunks_per_s(seconds: float = 15.0, min_chunks: int = 2, max_chunks: int | None = None) -> dict:
-    """The float32 CPU oracle on configs[0] at batch 1, on every host thread."""
+    """The float32 CPU path on configs[0] at batch 1, on every host thread."""
     import torch
 
-    from oracle.smolvla_fp32 import Oracle
     from so101_smolvla_edge_b200.bundle import observation, seeded_bundle
 
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
     b = seeded_bundle()
-    o = Oracle(b)
-    o.actions(*observation(b, 0))  # warm
+    chunk, kind, what = cpu_chunker()
+    chunk(observation(b, 0))  # warm
     n, t0 = 0, time.perf_counter()
     while True:
-        o.actions(*observation(b, n + 1))
+        chunk(observation(b, n + 1))
         n += 1
         el = time.perf_counter() - t0
         if (n >= min_chunks and el >= seconds) or (max_chunks and n >= max_chunks):
             break
-    return {"value": n / el, "unit": UNIT, "cores": threads, "kind": "port",
-            "sample": f"{n} chunks of configs[0] at batch 1 in {el:.1f} s, float32 torch CPU "
-                      f"(oracle/smolvla_fp32.py)"}  # fmt: skip
+    return {"value": n / el, "unit": UNIT, "cores": threads, "kind": kind,
+            "sample": f"{n} chunks of configs[0] at batch 1 in {el:.1f} s: {what}"}  # fmt: skip
+
+
+def reference_gpu_probe(kernels: str, chunks: int) -> None:
+    """Child process: the reference's own engine on this GPU (configs[3]: batch 1, bf16, one CUDA
+    graph per chunk, `vision="torch"`) with `kernels` "triton" or "torch". Prints one JSON line."""
+    import torch
+
+    from so101_smolvla_edge_b200.bundle import observation, seeded_bundle, write_bundle
+
+    RefEngine = reference_engine_class()
+    if RefEngine is None:
+        print(json.dumps({"unavailable": "the reference package is not in baseline/_ref"}))
+        return
+    b = seeded_bundle()
+    d = write_bundle(b, Path(tempfile.mkdtemp(prefix="so101_refgpu_")) / "config0")
+    t0 = time.perf_counter()
+    eng = RefEngine(str(d), device="cuda", dtype="bf16", kernels=kernels, vision="torch", warmup=3)
+    build_s = time.perf_counter() - t0
+    obs = [observation(b, s) for s in range(4)]
+    for i in range(5):
+        eng.infer(obs[i % 4][0], obs[i % 4][1])
+    eng.timing.history.clear()
+    for i in range(chunks):
+        eng.infer(obs[i % 4][0], obs[i % 4][1])
+    sm = eng.timing.summary()
+    err = None
+    gpath = ROOT / "tests" / "golden" / "golden_config0.npz"
+    if gpath.exists():
+        g = np.load(gpath)
+        err = max(float(np.abs(eng.infer(*obs[i][:2], noise=obs[i][2]) - g["actions"][i]).max()) for i in range(4))
+    stages = eng.profile(obs[0][0], obs[0][1], reps=10)
+    names: dict[str, int] = {}
+    from torch.profiler import ProfilerActivity, profile
+
+    with profile(activities=[ProfilerActivity.CUDA]) as prof, torch.no_grad():
+        eng._fwd()
+        torch.cuda.synchronize()
+    for ev in prof.events():
+        if ev.device_type == torch.autograd.DeviceType.CUDA:
+            names[ev.name] = names.get(ev.name, 0) + 1
+    top = sorted(names.items(), key=lambda kv: -kv[1])
+    print(json.dumps({"kernels": eng.kernels, "p50_ms": sm["p50_ms"], "p99_ms": sm["p99_ms"], "n": sm["n"],
+                      "stages_ms": stages, "max_err_rad": err, "build_s": build_s,
+                      "launches_per_chunk": sum(names.values()),
+                      "kernel_names": [f"{k} x{v}" for k, v in top[:24]],
+                      "triton_kernels": sum(v for k, v in names.items() if k.startswith("_") or "triton" in k.lower())}),
+          flush=True)  # fmt: skip
+
+
+def reference_gpu(chunks: int) -> dict:
+    """The reference's own Triton and torch engines timed on this GPU, each in a child process
+    (its Triton JIT, allocator and graphs stay out of this process)."""
+    out = {}
+    for kernels in ("triton", "torch"):
+        try:
+            r = subprocess.run([sys.executable, str(ROOT / "bench.py"), "--reference-gpu", kernels,
+                                "--latency-chunks", str(chunks)], capture_output=True, text=True,
+                               timeout=900)  # fmt: skip
+            line = [x for x in r.stdout.splitlines() if x.startswith("{")]
+            out[kernels] = json.loads(line[-1]) if line else {
+                "unavailable": f"exit {r.returncode}: {(r.stderr or r.stdout).strip().splitlines()[-1:]}"}
+        except subprocess.TimeoutExpired:
+            out[kernels] = {"unavailable": "timed out after 900 s"}
+    out["config"] = ("configs[3] through the reference's own Engine from baseline/_ref: batch 1, bf16, "
+                     "one CUDA graph per chunk, vision='torch' (TensorRT is not installed)")
+    return out
 
 
 def arm_config(world: int, batch: int) -> dict:
@@ -147,33 +249,35 @@ def arm_config(world: int, batch: int) -> dict:
             "parallelism": f"replicas x{world} (no collective)",
             "l2": "inputs larger than L2 (0.7 GB weights, >4 GB activations per replay)",
             "gemm_plans": "autotuned at engine build (compile='autotune')",
+            "act_clip": "the reference's calibration over 32 seeded observations (max |x| per vision linear)",
             "weights": "seeded configs[0] stand-in"}  # fmt: skip
 
 
 def run_reference(args) -> None:
+    """The reference arm: the reference's own float32 CPU path on this host's cores (the reference
+    package from baseline/_ref, else the oracle port), one observation per chunk."""
     rank, _, world = env_rank()
     if rank != 0:
         return
     import torch
 
-    from oracle.smolvla_fp32 import Oracle
     from so101_smolvla_edge_b200.bundle import observation, seeded_bundle
 
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
     b = seeded_bundle()
-    o = Oracle(b)
+    chunk, kind, what = cpu_chunker()
     for w in range(args.warmup):
-        o.actions(*observation(b, 10_000 + w))
+        chunk(observation(b, 10_000 + w))
     t0 = time.perf_counter()
     for k in range(args.steps):
-        o.actions(*observation(b, k))
+        chunk(observation(b, k))
     el = time.perf_counter() - t0
     v = args.steps / el
-    cpu = {"value": v, "unit": UNIT, "cores": threads, "kind": "port",
+    cpu = {"value": v, "unit": UNIT, "cores": threads, "kind": kind,
            "sample": f"{args.steps} chunks of the workload's observations one at a time (configs[0] "
-                     "weights, float32 torch CPU oracle, all host threads); chunks/s is per chunk, so "
-                     "the sample measures the same metric"}  # fmt: skip
+                     f"weights, all host threads): {what}; chunks/s is per chunk, so the sample "
+                     "measures the same metric"}  # fmt: skip
     print(json.dumps({
         "impl": "reference", "metric": metric_name(args.batch), "value": v, "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * el / args.steps,
@@ -238,7 +342,8 @@ def observations(b, seeds):
 
 
 def calibrate(b, dev) -> dict[str, float]:
-    """per-tensor activation clips from 32 seeded observations (bf16 vision)."""
+    """Per-tensor activation clips from the 32 calibration observations, through this engine's
+    own bf16 vision (Engine.calibrate)."""
     import torch
 
     from so101_smolvla_edge_b200.engine import Engine
@@ -248,6 +353,38 @@ def calibrate(b, dev) -> dict[str, float]:
     del eng
     torch.cuda.empty_cache()
     return clip
+
+
+INT8_GOLDEN = ROOT / "tests" / "golden" / "golden_int8_config0.npz"
+
+
+def reference_clips() -> dict[str, float] | None:
+    """configs[4]'s calibration: the clips the reference's own calibration hook produced over the
+    32 seeded calibration observations (max |x| per vision linear, `tests/test_ov_engine.py:
+    222-225`), as the reference reads them from a bundle's trt/act_clip.json. Stored with the int8
+    golden chunks that tests/golden/make_golden.py wrote by running the reference."""
+    if not INT8_GOLDEN.exists():
+        return None
+    g = np.load(INT8_GOLDEN)
+    return dict(zip(g["clip_names"].tolist(), (float(v) for v in g["clip_values"]), strict=True))
+
+
+def int8_parity(acts: np.ndarray) -> dict | None:
+    """The timed engine's W8A8 chunks for the golden seeds against the reference's own int8
+    chunks, beside the reference's one-ulp reproducibility band (how far its own int8 chunk moves
+    when its quantizers' float32 inputs move by one ulp) and against float32."""
+    if not INT8_GOLDEN.exists():
+        return None
+    g = np.load(INT8_GOLDEN)
+    ref, fp, ulp = g["actions_int8"], g["actions_fp32"], g["actions_int8_ulp"]
+    n = ref.shape[0]
+    return {"seeds": n,
+            "max_err_rad_vs_reference_int8": np.abs(acts[:n] - ref).max(axis=(1, 2)).round(5).tolist(),
+            "mean_err_rad_vs_reference_int8": float(np.abs(acts[:n] - ref).mean()),
+            "reference_ulp_band_max_rad": float(np.abs(ulp - ref[None]).max()),
+            "reference_ulp_band_mean_rad": float(np.abs(ulp - ref[None]).mean()),
+            "max_err_rad_vs_fp32": np.abs(acts[:n] - fp).max(axis=(1, 2)).round(5).tolist(),
+            "reference_int8_drift_vs_fp32": np.abs(ref - fp).max(axis=(1, 2)).round(5).tolist()}  # fmt: skip
 
 
 def time_call(fn, args, reps: int = 20) -> float:
@@ -306,7 +443,9 @@ def run_ours(args) -> None:
     from so101_smolvla_edge_b200.engine import Engine
 
     b = seeded_bundle()
-    clip = calibrate(b, dev)
+    own_clip = calibrate(b, dev)
+    clip = reference_clips() or own_clip
+    clip_src = "reference" if clip is not own_clip else "engine"
     batch = args.batch
     eng = Engine(b, device=dev, batch=batch, trt_precision="int8", act_clip=clip, warmup=2,
                  pdl=args.pdl, compile="autotune")
@@ -352,8 +491,9 @@ def run_ours(args) -> None:
     h2d = eng.img.numel() + eng.state.numel() * 4 + eng.noise.numel() * 4
     d2h = eng.out.numel() * 4
 
-    # ---- accuracy of the timed configuration against the float32 reference goldens
-    err = None
+    # ---- accuracy of the timed configuration against the reference's goldens: float32, and its
+    # own W8A8 chunk (with the reference's clips, and with this engine's own calibration)
+    err, parity = None, None
     gpath = ROOT / "tests" / "golden" / "golden_config0.npz"
     if gpath.exists() and rank == 0:
         g = np.load(gpath)
@@ -361,6 +501,18 @@ def run_ours(args) -> None:
         gobs = observations(b, range(n)) + obs[n:]
         res = eng.infer_batch([o[0] for o in gobs], [o[1] for o in gobs], [o[2] for o in gobs])
         err = float(np.abs(res[:n] - g["actions"]).max())
+        parity = int8_parity(res)
+        if parity is not None:
+            parity["clips"] = clip_src
+            if clip_src == "reference":  # the same chunks with the engine's own calibration
+                eo = Engine(b, device=dev, batch=n, trt_precision="int8", act_clip=own_clip, warmup=1)
+                own = eo.infer_batch([o[0] for o in gobs[:n]], [o[1] for o in gobs[:n]], [o[2] for o in gobs[:n]])
+                po = int8_parity(own)
+                parity["engine_calibration"] = {k: po[k] for k in ("max_err_rad_vs_reference_int8",
+                                                                  "mean_err_rad_vs_reference_int8",
+                                                                  "max_err_rad_vs_fp32")}  # fmt: skip
+                del eo
+                torch.cuda.empty_cache()
 
     # ---- dominant kernel alone: vision fc1 (int8 W8A8 GEMM + GELU + int8 requant epilogue)
     p = eng.path
@@ -448,6 +600,7 @@ def run_ours(args) -> None:
 
     if rank == 0:
         cpu = cpu_chunks_per_s() if world == 1 and not args.no_cpu else None
+        ref_gpu = reference_gpu(args.reference_gpu_chunks) if world == 1 and args.reference_gpu_chunks > 0 else None
         line = {
             "metric": metric_name(batch), "value": value, "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
@@ -459,11 +612,13 @@ def run_ours(args) -> None:
             "gpu_launches": launches * args.steps,
             "pdl": bool(args.pdl),
             "max_err_rad": err,
+            "int8_parity": parity,
             "roofline": roof,
             "roofline_attention": roof_attn,
             "latency": lat,
             "clocks": clk,
             "cpu_baseline": cpu,
+            "reference_gpu": ref_gpu,
         }  # fmt: skip
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -482,7 +637,13 @@ def main() -> None:
     ap.add_argument("--batch", type=int, default=BATCH,
                     help=f"observations per GPU per step (the metric is quoted at {BATCH}; smaller "
                          "batches are for profiling captures that must stay small)")  # fmt: skip
+    ap.add_argument("--reference-gpu-chunks", type=int, default=100,
+                    help="chunks per reference GPU engine (0: skip the reference's own GPU paths)")
+    ap.add_argument("--reference-gpu", choices=["triton", "torch"], default=None, help=argparse.SUPPRESS)
     a = ap.parse_args()
+    if a.reference_gpu:
+        reference_gpu_probe(a.reference_gpu, a.latency_chunks)
+        return
     if a.warmup < 3:
         a.warmup = 3
     if a.impl == "reference":

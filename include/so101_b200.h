@@ -31,7 +31,7 @@ extern "C" {
 #define SO101_ERR_LAUNCH 2      /* the CUDA launch failed (cudaGetLastError after the launch) */
 #define SO101_ERR_WORKSPACE 3   /* split-K workspace or ticket array too small */
 #define SO101_ERR_TIMEOUT 4     /* a device wait hit its bound (read with so101_device_status) */
-#define SO101_ERR_DRIVER 5      /* the driver entry point for TMA descriptors is unavailable */
+#define SO101_ERR_DRIVER 5      /* a driver entry point (TMA descriptors, current context) is unavailable */
 
 /* ---- element types --------------------------------------------------------------------- */
 #define SO101_BF16 0
@@ -242,6 +242,13 @@ SO101_API int so101_rope_kv(const void* qkv, int64_t ldqkv, int nq, int nkv, int
 SO101_API int so101_preprocess(const uint8_t* img, int n_img, int h, int w, int rh, int rw, int S, int P,
                      void* patches, int y_type, float y_qscale, cudaStream_t stream);
 
+/* Preprocessed frames to SigLIP patch rows: px (n_img, 3, S, S) float32 in [-1, 1] -> patches
+ * (n_img * (S/P)^2, 3*P*P) in bf16, int8 (with y_qscale) or fp32. The patch unfold of
+ * model/smolvla.py:166-168 for callers that hand over px, as the reference's TrtVision input
+ * (model/trt_vision.py:212-252) is. */
+SO101_API int so101_patchify(const float* px, int n_img, int S, int P, void* patches, int y_type, float y_qscale,
+                             cudaStream_t stream);
+
 /* Dense fp32 linear on CUDA cores (the reference keeps these small MLPs fp32):
  * y[m, n] = act(x[m, :] @ w[n, :] + bias[n] (+ bias2[n])), act 0 none, 2 SiLU (act 1 is
  * accepted and means none: SiLU belongs on the producer's output). K, ldx, ldw multiples of 4,
@@ -300,7 +307,9 @@ SO101_API int so101_clear_device_status(void);
  * more return SO101_ERR_WORKSPACE. It allocates nothing and frees nothing; the tickets are
  * cleared on the stream before each launch. The first call on a device looks the array's device
  * address up (cudaGetSymbolAddress, with that device current): make that first call before any
- * stream capture. All calls share the one array, so calls that overlap on the GPU (other streams,
+ * stream capture. The address is kept beside the device's current context and looked up again
+ * when that context changes (after cudaDeviceReset), so make the first call after a reset outside
+ * capture too. All calls share the one array, so calls that overlap on the GPU (other streams,
  * other host threads) race; keep them ordered on one stream. */
 SO101_API int so101_gemm_static(int a_type, const void* x, int64_t ldx, const void* w, int64_t ldw,
                                 void* y, int64_t ldy, int y_type, int64_t M, int64_t N, int64_t K,
@@ -350,6 +359,15 @@ typedef struct so101_expert_step {
 
 SO101_API int so101_expert_step_workspace(const so101_expert_step* s, int64_t* bytes);
 SO101_API int so101_expert_step_run(const so101_expert_step* s, cudaStream_t stream);
+
+/* Test hook for the bounded waits of so101_expert_step_run (no counterpart in the reference, whose
+ * kernels never wait on one another). wait_limit_ns bounds each grid-barrier and split-count wait
+ * (0: the default 2 s; at most 2 s); withhold_cta >= 0 makes that CTA leave at its first grid
+ * barrier without arriving, so every other CTA gives up after the bound, records
+ * SO101_ERR_TIMEOUT in the device status word and returns (its weight copies landed, its TMEM
+ * freed); -1 turns it off. Read at each launch: eager launches only, a captured graph keeps the
+ * values of its capture. */
+SO101_API int so101_expert_step_test_hooks(int64_t wait_limit_ns, int withhold_cta);
 
 /* The CUDA error string behind this thread's most recent SO101_ERR_LAUNCH ("" if none). No
  * counterpart in the reference, whose TensorRT enqueue reports a bare failure. */

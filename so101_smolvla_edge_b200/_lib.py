@@ -104,6 +104,7 @@ SIGNATURES = {
     "so101_layer_norm": [P, I64, P, P, P, I64, I, F, I64, I64, F, I, I64, S],
     "so101_rope_kv": [P, I64, I, I, I, P, P, P, I64, P, I64, I64, I, I64, I64, I64, S],
     "so101_preprocess": [P, I, I, I, I, I, I, I, P, I, F, S],
+    "so101_patchify": [P, I, I, I, P, I, F, S],
     "so101_linear_f32": [P, I64, P, I64, P, P, P, I64, I64, I64, I64, I, S],
     "so101_expert_out": [P, I64, P, F, P, P, P, I64, I64, I64, I64, F, S],
     "so101_prefix_tail": [P, I, P, P, P, I, P, P, I, I, P, I64, I64, I64, I, S],
@@ -117,6 +118,7 @@ SIGNATURES = {
     "so101_rms_stats": [P, I64, I64, I64, P, P, I64, P, I64, S],
     "so101_expert_step_workspace": [C.POINTER(ExpertStep), C.POINTER(C.c_int64)],
     "so101_expert_step_run": [C.POINTER(ExpertStep), S],
+    "so101_expert_step_test_hooks": [I64, I],
 }  # fmt: skip
 
 

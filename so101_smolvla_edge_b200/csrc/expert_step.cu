@@ -74,6 +74,8 @@ struct XsParams {
   int kbs[4];      // K blocks per work item, per GEMM kind
   float eps, scale_log2;
   int* status;
+  unsigned long long wait_ns;  // bound of the grid-barrier and split-count waits
+  int withhold;                // test hook: this CTA never arrives at a grid barrier (-1: none)
 };
 
 // ------------------------------------------------------------------------------ small helpers
@@ -103,7 +105,7 @@ __device__ bool xs_wait_count(const XsParams& p, const unsigned* word, unsigned 
   while (ld_acquire_u32(word) < target) {
     __nanosleep(64);
     if (ld_relaxed_u32(abort)) return false;
-    if (globaltimer() - t0 > kWaitLimitNs) {
+    if (globaltimer() - t0 > p.wait_ns) {
       record_error(p.status, SO101_ERR_TIMEOUT);
       atomicExch(const_cast<unsigned*>(abort), 1u);
       return false;
@@ -121,7 +123,11 @@ __device__ bool xs_wait_count(const XsParams& p, const unsigned* word, unsigned 
 __device__ bool xs_grid_sync(const XsParams& p, bool ok, int* s_flag) {
   tc_fence_before();
   __syncthreads();
-  if (threadIdx.x == 0) {
+  if (threadIdx.x == 0 && static_cast<int>(blockIdx.x) == p.withhold) {
+    // test hook: leave without arriving (and without raising the abort flag), so that every
+    // other CTA's wait runs into its bound
+    *s_flag = 0;
+  } else if (threadIdx.x == 0) {
     unsigned* gen = p.bar;
     unsigned* abort = p.bar + 1;
     unsigned* top = p.bar + 2;
@@ -151,7 +157,7 @@ __device__ bool xs_grid_sync(const XsParams& p, bool ok, int* s_flag) {
           good = 0;
           break;
         }
-        if (globaltimer() - t0 > kWaitLimitNs) {
+        if (globaltimer() - t0 > p.wait_ns) {
           record_error(p.status, SO101_ERR_TIMEOUT);
           atomicExch(abort, 1u);
           good = 0;
@@ -698,6 +704,11 @@ int xs_kbs(int n, int k, int sms) {
   return kbs;
 }
 
+// Test hooks (so101_expert_step_test_hooks): read at each launch, so they reach eager launches
+// only; a CUDA graph keeps the values its capture saw.
+long long g_xs_wait_ns = 0;  // 0: kWaitLimitNs
+int g_xs_withhold = -1;
+
 struct XsLayout {
   long long partials, tickets, bar, ss, total;
 };
@@ -838,6 +849,8 @@ extern "C" int so101_expert_step_run(const so101_expert_step* s, cudaStream_t st
   p.eps = s->eps;
   p.scale_log2 = static_cast<float>(1.4426950408889634 / 8.0);
   p.status = status_ptr();
+  p.wait_ns = g_xs_wait_ns > 0 ? static_cast<unsigned long long>(g_xs_wait_ns) : kWaitLimitNs;
+  p.withhold = g_xs_withhold < sms ? g_xs_withhold : -1;
   // tickets and barrier state start at zero (a launch that aborted may have left them set)
   e = cudaMemsetAsync(ws + lay.tickets, 0, static_cast<size_t>(lay.ss - lay.tickets), stream);
   if (e != cudaSuccess) return launch_error(e);
@@ -854,4 +867,12 @@ extern "C" int so101_expert_step_run(const so101_expert_step* s, cudaStream_t st
   lc.numAttrs = 1;
   e = cudaLaunchKernelEx(&lc, expert_step_kernel, p);
   return e == cudaSuccess ? SO101_OK : launch_error(e);
+}
+
+extern "C" int so101_expert_step_test_hooks(int64_t wait_limit_ns, int withhold_cta) {
+  if (wait_limit_ns < 0 || wait_limit_ns > static_cast<int64_t>(kWaitLimitNs) || withhold_cta < -1)
+    return SO101_ERR_ARG;
+  g_xs_wait_ns = wait_limit_ns;
+  g_xs_withhold = withhold_cta;
+  return SO101_OK;
 }

@@ -1720,26 +1720,48 @@ constexpr long long kStaticTickets = 4096;            // one per output tile
 
 static __device__ __align__(256) unsigned char g_static_scratch[kStaticPartialBytes + kStaticTickets * 4];
 
-// Host-side device address of g_static_scratch, looked up once per device with that device
-// current (the symbol's host name is only a stand-in, never a device address).
+// Host-side device address of g_static_scratch, looked up per device with that device current
+// (the symbol's host name is only a stand-in, never a device address). The address belongs to the
+// device's current context: it is kept beside that context's handle and looked up again when the
+// context changes (after cudaDeviceReset a new primary context loads the module afresh).
 struct StaticScratch {
+  void* ctx = nullptr;
   void* base = nullptr;
 };
 StaticScratch g_static_scratch_addr[64];
 std::mutex g_static_scratch_mu;
 
+using CtxGetCurrentFn = int (*)(void**);  // CUresult cuCtxGetCurrent(CUcontext*)
+
+CtxGetCurrentFn ctx_get_current() {
+  static CtxGetCurrentFn fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      return reinterpret_cast<CtxGetCurrentFn>(p);
+    return static_cast<CtxGetCurrentFn>(nullptr);
+  }();
+  return fn;
+}
+
 int static_scratch(void** partials, int** tickets) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return SO101_ERR_LAUNCH;
+  CtxGetCurrentFn get = ctx_get_current();
+  void* ctx = nullptr;  // null before the runtime's first call on this thread made a context current
+  if (!get || get(&ctx) != 0) return SO101_ERR_DRIVER;
   std::lock_guard<std::mutex> lock(g_static_scratch_mu);
-  if (!g_static_scratch_addr[dev].base) {
+  StaticScratch& slot = g_static_scratch_addr[dev];
+  if (!ctx || !slot.base || slot.ctx != ctx) {
     void* p = nullptr;
     if (cudaGetSymbolAddress(&p, g_static_scratch) != cudaSuccess || !p) return SO101_ERR_LAUNCH;
-    g_static_scratch_addr[dev].base = p;
+    if (get(&ctx) != 0 || !ctx) return SO101_ERR_LAUNCH;
+    slot.base = p;
+    slot.ctx = ctx;
   }
-  *partials = g_static_scratch_addr[dev].base;
-  *tickets = reinterpret_cast<int*>(static_cast<unsigned char*>(g_static_scratch_addr[dev].base) +
-                                    kStaticPartialBytes);
+  *partials = slot.base;
+  *tickets = reinterpret_cast<int*>(static_cast<unsigned char*>(slot.base) + kStaticPartialBytes);
   return SO101_OK;
 }
 

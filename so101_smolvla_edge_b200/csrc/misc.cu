@@ -402,10 +402,50 @@ __global__ void finish_kernel(const float* __restrict__ x_t, int max_action, con
   }
 }
 
+// Preprocessed frames px (n, 3, S, S) float -> patch rows (n * G^2, 3 P^2): one thread per patch
+// row segment (image, patch, channel, row py): P consecutive floats of px in, P values out.
+__global__ void patchify_kernel(const float* __restrict__ px, int n_img, int S, int P, void* __restrict__ out,
+                                int y_type, float qs) {
+  grid_dep_launch();
+  grid_dep_wait();
+  const int G = S / P;
+  const long long segs = static_cast<long long>(n_img) * G * G * 3 * P;
+  const long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
+  if (i >= segs) return;
+  const int py = static_cast<int>(i % P);
+  const int c = static_cast<int>((i / P) % 3);
+  const long long row = i / (3 * P);  // patch row: image * G^2 + gy * G + gx
+  const int im = static_cast<int>(row / (G * G)), pr = static_cast<int>(row % (G * G));
+  const int gy = pr / G, gx = pr % G;
+  const float* src = px + ((static_cast<long long>(im) * 3 + c) * S + gy * P + py) * S + gx * P;
+  const long long o = row * 3 * P * P + (c * P + py) * P;
+  for (int x = 0; x < P; ++x) {
+    const float v = src[x];
+    if (y_type == SO101_BF16)
+      static_cast<__nv_bfloat16*>(out)[o + x] = __float2bfloat16_rn(v);
+    else if (y_type == SO101_I8)
+      static_cast<int8_t*>(out)[o + x] = quant_i8(v, qs);
+    else
+      static_cast<float*>(out)[o + x] = v;
+  }
+}
+
 }  // namespace so101
 
 using namespace so101;
 
+extern "C" int so101_patchify(const float* px, int n_img, int S, int P, void* patches, int y_type, float y_qscale,
+                              cudaStream_t stream) {
+  if (!px || !patches || n_img <= 0 || P <= 0 || S <= 0 || S % P) return SO101_ERR_ARG;
+  if (y_type != SO101_BF16 && y_type != SO101_I8 && y_type != SO101_F32) return SO101_ERR_ARG;
+  if (y_type == SO101_I8 && !(y_qscale > 0.f)) return SO101_ERR_ARG;
+  const long long G = S / P;
+  const long long segs = static_cast<long long>(n_img) * G * G * 3 * P;
+  const long long blocks = (segs + 255) / 256;
+  if (blocks > 0x7fffffffLL) return SO101_ERR_ARG;
+  return launch_kernel(patchify_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, stream, px, n_img,
+                       static_cast<int>(S), static_cast<int>(P), patches, y_type, y_qscale);
+}
 
 extern "C" int so101_preprocess(const uint8_t* img, int n_img, int h, int w, int rh, int rw, int S, int P,
                                 void* patches, int y_type, float y_qscale, cudaStream_t stream) {

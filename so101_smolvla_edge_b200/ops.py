@@ -54,7 +54,7 @@ _WS: dict[torch.device, Workspace] = {}
 
 def workspace(device: torch.device | str) -> Workspace:
     device = torch.device(device)
-    if device.index is None:
+    if device.type == "cuda" and device.index is None:
         device = torch.device("cuda", torch.cuda.current_device())
     ws = _WS.get(device)
     if ws is None:

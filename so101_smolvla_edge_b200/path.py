@@ -14,7 +14,7 @@ all B's rows at once, attention per observation).
 
 Layout (B observations, C cameras, Np patches per camera, L prefix rows, H action rows):
     img      (B*C, h, w, 3) u8       patches (B*C*Np, 3 P^2)     xv  (B*C*Np, vis_dim) fp32
-    prefix   (B*L, text_dim) fp32 residual stream of the prefix pass
+    x_pre    (B*L, text_dim) fp32 residual stream of the prefix pass
     ck/cv[i] (B, L+H, kv) bf16 self layers: rows [:L] VLM keys/values, rows [L:] this step's own
     kx/vx[i] (B, L, kv) bf16 cross layers: the expert's projections of the VLM keys/values
     x_t      (B*H, max_action) fp32, e (B*H, exp_dim) fp32 expert residual stream
@@ -122,7 +122,7 @@ class B200Path:
 
     def __init__(self, bundle: Bundle, device: torch.device, batch: int = 1,
                  vision_precision: str = "bf16", act_clip: dict[str, float] | None = None,
-                 expert_step: str = "auto", fold_norms: bool = True):  # fmt: skip
+                 expert_step: str = "auto", fold_norms: bool = True, lib=None):  # fmt: skip
         s = self.spec = bundle.spec
         why = unsupported(s)
         if why:
@@ -134,7 +134,7 @@ class B200Path:
         self.bundle, self.meta = bundle, bundle.meta
         self.dev = device
         self.B = B = int(batch)
-        self.lib = L.lib()
+        self.lib = L.lib() if lib is None else lib  # lib: a stand-in, for host-logic tests only
         self.int8 = vision_precision == "int8"
         self.clip = dict(act_clip or {})
         if self.int8:
@@ -177,6 +177,20 @@ class B200Path:
         self._build_vision(self.progs["vision"])
         self._build_prefix(self.progs["prefix"])
         self._build_denoise(self.progs["denoise"])
+        # the reference's backend seams (prefix / velocity / vision from px): the same launches
+        # over caller-given rows, time projection and frames
+        pl = Program("prefix_layers")
+        pl.calls = [c for c in self.progs["prefix"].calls if c[0] != "prefix_tail"]
+        pl._keep = [self.progs["prefix"]]
+        vx = Program("velocity")
+        self._build_step(vx, 0, self.x_seam, self.v_buf, 1.0, tp=self.tp_seam)
+        vp = Program("vision_px")
+        s = self.spec
+        vp.add("patchify", self.lib.so101_patchify, self.px_seam.data_ptr(), self.B * self.C, s.image_size,
+               s.patch, self.patches.data_ptr(), DTYPE[self.patches.dtype], self._qs("patch"))  # fmt: skip
+        vp.calls += [c for c in self.progs["vision"].calls if c[0] != "preprocess"]
+        vp._keep = [self.progs["vision"]]
+        self.seams = {"prefix": pl, "velocity": vx, "vision": vp}
 
     def autotune(self, reps: int = 5) -> dict[str, dict]:
         """Time every candidate plan (TUNE_CANDIDATES; TUNE_SMALL for at most 256 rows) of each
@@ -282,7 +296,7 @@ class B200Path:
         self.mlp_v_i8 = z(rows_v, s.vis_mlp, dtype=i8) if self.int8 else None
         self.shuf = z(rows_v // sh**2, vd * sh**2, dtype=qdt("conn"))
         # prefix
-        self.prefix = z(B * L_, s.text_dim)
+        self.x_pre = z(B * L_, s.text_dim)  # the prefix residual stream
         self.h_t = z(B * L_, s.text_dim, dtype=bf)
         self.qkv_t = z(B * L_, s.qkv_dim, dtype=bf)
         self.attn_t = z(B * L_, s.q_dim, dtype=bf)
@@ -303,6 +317,10 @@ class B200Path:
         self.attn_e = z(B * H, s.q_dim, dtype=bf)
         self.mlp_e = z(B * H, s.exp_mlp, dtype=bf)
         self.v_buf = z(B * H, s.max_action)
+        # inputs of the reference's backend seams (velocity's x_t and time projection, vision's px)
+        self.x_seam = z(B * H, s.max_action)
+        self.tp_seam = z(s.exp_dim)
+        self.px_seam = z(B * C_, 3, s.image_size, s.image_size)
         self.ss_e = z(B * H, STAT_SLOTS)  # per-row sums of squares of the expert residual stream
 
     def _expert_step(self, mode: str) -> L.ExpertStep | None:
@@ -503,7 +521,7 @@ class B200Path:
               w["vis.post_ln.w"].data_ptr(), w["vis.post_ln.b"].data_ptr(), self.shuf.data_ptr(),
               self.shuf.stride(0), DTYPE[self.shuf.dtype], self._qs("conn"), rows_v, vd, s.vis_eps,
               s.shuffle, Np)  # fmt: skip
-        self._lin(p, "conn", self.shuf, "conn.w", self.prefix, out_scale=math.sqrt(s.text_dim),
+        self._lin(p, "conn", self.shuf, "conn.w", self.x_pre, out_scale=math.sqrt(s.text_dim),
                   row_map=(C_ * s.img_tokens, self.L))  # fmt: skip
 
     def _vis_in(self, name: str, bf: torch.Tensor, i8: torch.Tensor | None) -> torch.Tensor:
@@ -530,8 +548,8 @@ class B200Path:
         p.add("prefix_tail", self.lib.so101_prefix_tail, self.state.data_ptr(), self.state_dim,
               w["norm.state.mean"].data_ptr(), w["norm.state.std"].data_ptr(), w["state.w"].data_ptr(),
               s.max_state, w["state.b"].data_ptr(), w["lang.emb"].data_ptr(), s.lang_len, s.text_dim,
-              self.prefix.data_ptr(), s.text_dim, L_, tail, B)  # fmt: skip
-        x = self.prefix
+              self.x_pre.data_ptr(), s.text_dim, L_, tail, B)  # fmt: skip
+        x = self.x_pre
         esz = 2  # bf16 bytes
         # RMSNorm in two halves: the residual GEMM before it writes bf16(x * w) and per-row sums of
         # squares, the GEMM after it scales its rows by rstd (fold); else an rms_norm launch
@@ -578,13 +596,15 @@ class B200Path:
             slots = self._gemm(p, f"{i}.down", self.mlp_t, w[t + "down"], x, residual=x, stat=nxt)
 
     # ------------------------------------------------------------------ denoising
-    def _build_step(self, p: Program, k: int, x_in: torch.Tensor, x_out: torch.Tensor, dt: float) -> None:
-        """One velocity evaluation at step k, folded into x_out += dt * v."""
+    def _build_step(self, p: Program, k: int, x_in: torch.Tensor, x_out: torch.Tensor, dt: float,
+                    tp: torch.Tensor | None = None) -> None:
+        """One velocity evaluation at step k, folded into x_out += dt * v; tp (exp_dim) replaces
+        step k's row of the time projection table."""
         s, w = self.spec, self.w
         B, L_, H = self.B, self.L, self.H
         nq, nk, hd, kv, qd = s.n_heads, s.n_kv, s.head_dim, s.kv_dim, s.qkv_dim
         M = B * H
-        tp = w["time_proj"][k]
+        tp = w["time_proj"][k] if tp is None else tp
         p.add(f"s{k}.act_time_in", self.lib.so101_linear_f32, x_in.data_ptr(), s.max_action,
               w["act.ain.w"].data_ptr(), s.max_action, w["act.ain.b"].data_ptr(), tp.data_ptr(),
               self.h0.data_ptr(), s.exp_dim, M, s.exp_dim, s.max_action, 2)  # fmt: skip
@@ -690,9 +710,54 @@ class B200Path:
         vals = amax.cpu().tolist()
         return {n: v for n, v in zip(names, vals, strict=True) if include_patch or n != "patch"}
 
+    # ------------------------------------------------------------------ the reference's seams
+    def prefix(self, rows: torch.Tensor) -> None:
+        """`TritonPath.prefix` (pkg/model/smolvla_triton.py:78-103): the VLM layers over the
+        prefix rows (L, text_dim) float32 — (B, L, text_dim) for a batch — filling the self layers'
+        key/value rows [:L] (ck, cv) and the cross layers' expert keys/values (kx, vx). Enqueued on
+        the current stream."""
+        s = self.spec
+        want = (self.B, self.L, s.text_dim)
+        if rows.numel() != self.B * self.L * s.text_dim or rows.shape[-1] != s.text_dim:
+            raise ValueError(f"prefix rows must be {want[1:] if self.B == 1 else want}, got {tuple(rows.shape)}")
+        self.x_pre.copy_(rows.reshape(self.B * self.L, s.text_dim))
+        self.seams["prefix"].run(self._stream())
+
+    def velocity(self, x_t: torch.Tensor, time_proj: torch.Tensor) -> torch.Tensor:
+        """`TritonPath.velocity` (pkg/model/smolvla_triton.py:105-130): v_t (B, chunk, max_action)
+        float32 for x_t (B, chunk, max_action) float32 and the time half of the action/time MLP's
+        input, time_proj (1, 1, exp_dim) with its bias (the reference's `Engine.time_proj[k]`), over
+        the caches the last `prefix` call filled. Returns a fixed buffer that the next call
+        overwrites (the caller adds dt * v_t, as the reference's `Engine.step` does)."""
+        s = self.spec
+        if x_t.numel() != self.B * self.H * s.max_action or time_proj.numel() != s.exp_dim:
+            raise ValueError(f"x_t must hold {self.B} x {self.H} x {s.max_action} and time_proj {s.exp_dim} values")
+        self.x_seam.copy_(x_t.reshape(self.x_seam.shape))
+        self.tp_seam.copy_(time_proj.reshape(s.exp_dim))
+        self.v_buf.zero_()
+        self.seams["velocity"].run(self._stream())
+        return self.v_buf.view(self.B, self.H, s.max_action)
+
+    def encode_images(self, px: torch.Tensor) -> torch.Tensor:
+        """`TrtVision.__call__` (pkg/model/trt_vision.py:247-252): px (B * n_cams, 3, S, S) float32
+        in [-1, 1] to image rows (B * n_cams * img_tokens, text_dim) float32 (B = 1: one block of
+        rows, as the reference's), in bf16 or W8A8 as this path was built. The rows are a view of
+        this path's prefix buffer, overwritten by the next call."""
+        if tuple(px.shape) != tuple(self.px_seam.shape):
+            raise ValueError(f"px must be {tuple(self.px_seam.shape)}, got {tuple(px.shape)}")
+        self.px_seam.copy_(px)
+        self.seams["vision"].run(self._stream())
+        n = self.C * self.spec.img_tokens
+        rows = self.x_pre.view(self.B, self.L, -1)[:, :n]
+        return rows[0] if self.B == 1 else rows.reshape(self.B * n, -1)
+
     # ------------------------------------------------------------------ running
+    def _stream(self) -> int:
+        """The current CUDA stream's handle (0 for a host-only stand-in path)."""
+        return torch.cuda.current_stream(self.dev).cuda_stream if self.dev.type == "cuda" else 0
+
     def run(self, stage: str, stream: int | None = None) -> None:
-        st = torch.cuda.current_stream(self.dev).cuda_stream if stream is None else stream
+        st = self._stream() if stream is None else stream
         self.progs[stage].run(st)
 
     def run_chunk(self, stream: int | None = None) -> None:

@@ -70,3 +70,32 @@ def config0_bundle():
 
         _CONFIG0["b"] = seeded_bundle()
     return _CONFIG0["b"]
+
+
+# W8A8 against the reference's own int8 chunk. That chunk is not reproducible to 1e-2 by any other
+# arithmetic, the reference's included: nudging every quantizer input of the reference by one
+# float32 ulp moves its int8 chunk by up to B = 0.0098 rad on the configs[0] seeds (the golden's
+# `actions_int8_ulp`, three runs per seed), because per-tensor max-clip quantization re-rounds
+# thousands of activations a step up or down. The int8 bars are stated against that band:
+INT8_BAND_MAX = 1.25  # every seed's max |d action| <= 1.25 x the band's largest max |d|
+INT8_BAND_MEAN = 1.5  # mean |d action| over the seeds <= 1.5 x the band's mean |d|
+INT8_FP32_DRIFT = 1.5  # no further from float32 than 1.5x the reference's own int8 drift, per seed
+
+
+def int8_band_check(g, acts) -> dict:
+    """configs[0] W8A8 parity over the golden seeds: acts (>= seeds, 50, 12) against the reference's
+    int8 chunks, judged against the reference's own one-ulp reproducibility band."""
+    ref, fp, ulp = g["actions_int8"], g["actions_fp32"], g["actions_int8_ulp"]
+    n = ref.shape[0]
+    band_max = float(np.abs(ulp - ref[None]).max())
+    band_mean = float(np.abs(ulp - ref[None]).mean())
+    err = np.abs(acts[:n] - ref).max(axis=(1, 2))
+    mean = float(np.abs(acts[:n] - ref).mean())
+    drift = np.abs(ref - fp).max(axis=(1, 2))
+    err_fp32 = np.abs(acts[:n] - fp).max(axis=(1, 2))
+    rep = {"err_int8": err.round(4).tolist(), "band_max": band_max, "mean": mean, "band_mean": band_mean,
+           "err_fp32": err_fp32.round(4).tolist(), "ref_drift": drift.round(4).tolist()}  # fmt: skip
+    assert (err <= INT8_BAND_MAX * band_max).all(), rep
+    assert mean <= INT8_BAND_MEAN * band_mean, rep
+    assert (err_fp32 <= INT8_FP32_DRIFT * drift).all(), rep
+    return rep

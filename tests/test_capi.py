@@ -17,7 +17,7 @@ def lib():
 
 def test_library_loads_and_exports_every_header_symbol(lib):
     names = L.header_symbols()
-    assert len(names) == 27
+    assert len(names) == 29
     missing = [n for n in names if not hasattr(lib, n)]
     assert not missing, missing
     assert lib.so101_version().decode().endswith("sm_100a")
@@ -144,3 +144,12 @@ def test_tune_gemm_candidates():
     assert not any(c and c[0] == 1 for c in many)
     assert any(c and c[4] == L.GEMM_PAIR for c in many) and all(c is None or c[1] <= 128 for c in many)
     assert set(SHAPES) == {"expert", "prefix", "vision"}
+
+
+def test_expert_step_test_hooks_validate(lib):
+    """The bounded-wait test hook takes a bound of at most 2 s and a CTA index or -1."""
+    assert lib.so101_expert_step_test_hooks(-1, -1) == L.ERR_ARG
+    assert lib.so101_expert_step_test_hooks(3_000_000_000, -1) == L.ERR_ARG
+    assert lib.so101_expert_step_test_hooks(0, -2) == L.ERR_ARG
+    assert lib.so101_expert_step_test_hooks(50_000_000, 3) == L.OK
+    assert lib.so101_expert_step_test_hooks(0, -1) == L.OK

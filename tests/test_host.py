@@ -132,3 +132,62 @@ def test_timing_summary_matches_the_reference_quantiles():
     for _ in range(1000):
         t.add(1.0)
     assert len(t.history) <= 1000
+
+
+class _StubLib:
+    """Stands in for libso101_b200.so: every entry point records its call and returns 0."""
+
+    def __init__(self):
+        self.calls: list[tuple[str, tuple]] = []
+
+    def __getattr__(self, name):
+        def fn(*args):
+            self.calls.append((name, args))
+            return 0
+
+        return fn
+
+
+def test_backend_seams_on_a_stub_library():
+    """The reference's backend seams on B200Path, built against a stub library on the CPU:
+    `prefix(rows)` (TritonPath.prefix) runs the prefix layers without the prefix-row launch,
+    `velocity(x_t, time_proj)` (TritonPath.velocity) one velocity evaluation fed by the caller's
+    time projection, `encode_images(px)` (TrtVision.__call__) the vision launches from px."""
+    import torch
+    from conftest import case_bundle
+
+    from so101_smolvla_edge_b200.path import B200Path
+
+    b = case_bundle("small64_absolute")
+    s = b.spec
+    lib = _StubLib()
+    p = B200Path(b, torch.device("cpu"), lib=lib)
+    names = [c[0] for c in p.progs["prefix"].calls]
+    assert names[0] == "prefix_tail"
+
+    rows = torch.randn(s.prefix_len, s.text_dim)
+    lib.calls.clear()
+    p.prefix(rows)
+    assert torch.equal(p.x_pre, rows)
+    assert len(lib.calls) == len(names) - 1 and lib.calls[0][0] != "so101_prefix_tail"
+    with pytest.raises(ValueError):
+        p.prefix(torch.zeros(s.prefix_len - 1, s.text_dim))
+
+    x_t = torch.randn(1, s.chunk, s.max_action)
+    tp = torch.randn(1, 1, s.exp_dim)
+    lib.calls.clear()
+    v = p.velocity(x_t, tp)
+    assert v.shape == (1, s.chunk, s.max_action) and v.data_ptr() == p.v_buf.data_ptr()
+    assert torch.equal(p.x_seam.view_as(x_t), x_t) and torch.equal(p.tp_seam, tp.reshape(-1))
+    first, last = lib.calls[0], lib.calls[-1]
+    assert first[0] == "so101_linear_f32" and first[1][0] == p.x_seam.data_ptr()
+    assert first[1][5] == p.tp_seam.data_ptr()  # the caller's time projection, not the step table
+    assert last[0] == "so101_expert_out" and last[1][6] == p.v_buf.data_ptr()
+
+    px = torch.rand(s.n_cams, 3, s.image_size, s.image_size) * 2 - 1
+    lib.calls.clear()
+    out = p.encode_images(px)
+    assert lib.calls[0][0] == "so101_patchify" and lib.calls[0][1][0] == p.px_seam.data_ptr()
+    assert "so101_preprocess" not in [c[0] for c in lib.calls]
+    assert out.shape == (s.n_cams * s.img_tokens, s.text_dim)
+    assert out.data_ptr() == p.x_pre.data_ptr()

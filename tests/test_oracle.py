@@ -95,3 +95,29 @@ def test_oracle_int8_matches_reference_small():
     assert np.abs(got - g["actions_int8"]).max() < 1e-4
     # quantized at all, and still near float
     assert np.abs(got - g["actions_fp32"]).max() > 1e-6
+
+
+def test_reference_int8_chunk_band():
+    """The reference's own W8A8 chunk moves by several 1e-3 rad when its quantizers' float32
+    inputs move by one ulp (three seeded runs per golden seed, written by make_golden.py from the
+    reference itself): the band every int8 parity bar here is stated against."""
+    g = golden("int8_config0")
+    d = np.abs(g["actions_int8_ulp"] - g["actions_int8"][None]).max(axis=(2, 3))  # (runs, seeds)
+    assert d.shape[1] == g["actions_int8"].shape[0] >= 4
+    assert (d > 2e-3).all() and d.max() < 2e-2, d
+
+
+def test_oracle_int8_matches_reference_config0():
+    """The float32 restatement with the reference's clips lands inside the reference's own
+    reproducibility band on every golden seed (it cannot do better: its float32 sums are
+    ordered differently, which is more than one ulp)."""
+    from conftest import int8_band_check
+
+    from oracle.smolvla_fp32 import Oracle
+
+    g = golden("int8_config0")
+    b = config0_bundle()
+    clip = dict(zip(g["clip_names"].tolist(), g["clip_values"].tolist(), strict=True))
+    o = Oracle(b, act_clip=clip)
+    acts = np.stack([o.actions(*observation(b, s)) for s in range(g["actions_int8"].shape[0])])
+    int8_band_check(g, acts)

@@ -78,6 +78,65 @@ def test_static_scratch_gemm_matches_workspace_gemm(m, n, k, cfg, gate):
     assert lib.so101_device_status() == 0
 
 
+def _both(L, lib, static, a_type, x, w, m, n, k, epi, cfg, out_dtype, y_type):
+    """so101_gemm with a caller workspace, then so101_gemm_static twice: (want, [got, got])."""
+    from so101_smolvla_edge_b200.ops import workspace
+
+    stream = torch.cuda.current_stream().cuda_stream
+    ws = workspace(x.device)
+    cp = C.byref(cfg) if cfg is not None else None
+    want = torch.empty(m, n, dtype=out_dtype, device="cuda")
+    L.check(lib.so101_gemm(a_type, x.data_ptr(), k, w.data_ptr(), k, want.data_ptr(), n, y_type, m, n,
+                           k, C.byref(epi), cp, ws.partials.data_ptr(), ws.nbytes,
+                           ws.tickets.data_ptr(), ws.tickets.numel(), stream), "so101_gemm")  # fmt: skip
+    got = []
+    for _ in range(2):
+        y = torch.full((m, n), float("nan"), dtype=out_dtype, device="cuda")
+        rc = static(a_type, x.data_ptr(), k, w.data_ptr(), k, y.data_ptr(), n, y_type, m, n, k,
+                    C.byref(epi), cp, stream)  # fmt: skip
+        assert rc == L.OK
+        torch.cuda.synchronize()
+        got.append(y)
+    return want, got
+
+
+@pytest.mark.parametrize("m,n,k", [(50, 720, 2048), (241, 320, 960), (3072, 768, 768)])
+def test_static_scratch_gemm_picks_its_own_plan(m, n, k):
+    """cfg = NULL: both entry points pick the plan themselves (the picks reduce split-K inside a
+    thread-block cluster, so the scratch is not touched, but the call must still match)."""
+    L, lib, static = _bind()
+    g = torch.Generator(device="cuda").manual_seed(1)
+    x = torch.randn(m, k, device="cuda", generator=g).to(torch.bfloat16)
+    w = (torch.randn(n, k, device="cuda", generator=g) * k**-0.5).to(torch.bfloat16)
+    epi = L.Epilogue(epilogue=L.EPI_NONE, out_scale=1.0)
+    want, got = _both(L, lib, static, L.BF16, x, w, m, n, k, epi, None, torch.float32, L.F32)
+    for y in got:
+        assert _close(y, want)
+    assert lib.so101_device_status() == 0
+
+
+def test_static_scratch_int8_split_k():
+    """W8A8 operands with per-channel weight scales: int32 partials through the static scratch."""
+    L, lib, static = _bind()
+    m, n, k = 256, 768, 3072  # int8 operands take the tokens-on-M tiles
+    g = torch.Generator(device="cuda").manual_seed(2)
+    x = torch.randint(-128, 128, (m, k), device="cuda", generator=g, dtype=torch.int32).to(torch.int8)
+    w = torch.randint(-127, 128, (n, k), device="cuda", generator=g, dtype=torch.int32).to(torch.int8)
+    ws = torch.rand(n, device="cuda", generator=g) * 1e-3 + 1e-4
+    epi = L.Epilogue(epilogue=L.EPI_NONE, out_scale=1.0, w_scale=ws.data_ptr(), x_scale=0.02)
+    cfg = L.GemmConfig(0, 128, 6, 0, L.GEMM_GLOBAL_SPLITK)
+    need, tick = C.c_int64(), C.c_int64()
+    L.check(lib.so101_gemm_workspace(L.I8, m, n, k, L.EPI_NONE, C.byref(cfg), C.byref(need),
+                                     C.byref(tick)), "workspace")  # fmt: skip
+    assert need.value > 0 and tick.value > 0, "the plan must use split-K scratch"
+    want, got = _both(L, lib, static, L.I8, x, w, m, n, k, epi, cfg, torch.float32, L.F32)
+    exact = (x.double() @ w.double().T) * 0.02 * ws.double()
+    assert torch.allclose(want.double(), exact, rtol=1e-5, atol=1e-5)
+    for y in got:
+        assert torch.equal(y, want)  # integer partials: the sum does not depend on the order
+    assert lib.so101_device_status() == 0
+
+
 def test_static_scratch_refuses_plans_beyond_its_size():
     """A split-K plan needing more than the 8 MiB array is refused with SO101_ERR_WORKSPACE."""
     L, lib, static = _bind()
