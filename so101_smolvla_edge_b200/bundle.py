@@ -49,11 +49,14 @@ class Bundle:
         return list(self.meta["cameras"])
 
     def checksum(self) -> str:
-        """crc32 over every tensor's bytes in name order: identifies a seeded bundle."""
-        c = 0
-        for k in sorted(self.tensors):
-            c = zlib.crc32(np.ascontiguousarray(self.tensors[k], dtype=np.float32).tobytes(), c)
-        return f"{c:08x}"
+        """crc32 over every tensor's bytes in name order: identifies a seeded bundle (computed
+        once per Bundle; the tensors are not meant to change after loading)."""
+        if getattr(self, "_checksum", None) is None:
+            c = 0
+            for k in sorted(self.tensors):
+                c = zlib.crc32(np.ascontiguousarray(self.tensors[k], dtype=np.float32).tobytes(), c)
+            self._checksum = f"{c:08x}"
+        return self._checksum
 
 
 def load_bundle(path: str | Path | Bundle) -> Bundle:

@@ -1,5 +1,9 @@
-// Grouped-query attention entry point: the tcgen05 kernel for the unmasked equal-length SigLIP
-// case, the mma.sync flash attention (attention_tile.cuh) for everything else.
+// Grouped-query attention entry point: the tcgen05 kernels for the unmasked equal-length SigLIP
+// case (attention_tc.cu) and for the masked prefix / expert attention over many observations
+// (attention_gqa_tc.cu), the mma.sync flash attention (attention_tile.cuh) for everything else
+// (few CTAs, where it splits the keys over a cluster, and the step's own keys rotated on chip).
+#include <cstdlib>
+
 #include "attention_tile.cuh"
 
 namespace so101 {
@@ -42,6 +46,24 @@ bool attention_tc_eligible(const void* q, long long ldq, const void* k, long lon
 int attention_tc_launch(const void* q, long long ldq, const void* k, long long ldk, const void* v, long long ldv,
                         void* o, long long ldo, int o_type, float o_qscale, long long L, int heads, int batch,
                         cudaStream_t stream);
+bool attention_gqa_tc_eligible(const void* q, long long ldq, const void* k, long long ldk, const void* v,
+                               long long ldv, const void* o, long long ldo, int o_type, long long Lq, long long Lk,
+                               int nq, int nkv, int hd, const float* cos, long long bq, long long bk, long long bv,
+                               long long bo, int batch);
+int attention_gqa_tc_launch(const void* q, long long ldq, const void* k, long long ldk, const void* v, long long ldv,
+                            void* o, long long ldo, long long Lq, long long Lk, int nq, int nkv,
+                            long long causal_from, long long q_offset, const float* cos, const float* sin, int batch,
+                            long long bq, long long bk, long long bv, long long bo, cudaStream_t stream);
+
+// The masked tcgen05 kernel for many observations; SO101_ATTN_GQA_TC=0 keeps the mma.sync kernel
+// (for comparisons).
+bool gqa_tc_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("SO101_ATTN_GQA_TC");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
 
 }  // namespace so101
 
@@ -85,6 +107,11 @@ int attention_impl(const void* q, int64_t ldq, const void* k, int64_t ldk, const
       attention_tc_eligible(q, ldq, k, ldk, v, ldv, Lq, Lk, nq, nkv, hd, causal_from, cos, bq, bk, bv, o_type) &&
       ldo % 8 == 0 && bo == Lq * ldo && reinterpret_cast<uintptr_t>(o) % 16 == 0)
     return attention_tc_launch(q, ldq, k, ldk, v, ldv, o, ldo, o_type, o_qscale, Lq, nq, batch, stream);
+  if (!own.k && gqa_tc_enabled() &&
+      attention_gqa_tc_eligible(q, ldq, k, ldk, v, ldv, o, ldo, o_type, Lq, Lk, nq, nkv, hd, cos, bq, bk, bv, bo,
+                                batch))
+    return attention_gqa_tc_launch(q, ldq, k, ldk, v, ldv, o, ldo, Lq, Lk, nq, nkv, causal_from, q_offset, cos, sin,
+                                   batch, bq, bk, bv, bo, stream);
   AttnArgs a;
   a.q = static_cast<const __nv_bfloat16*>(q);
   a.k = static_cast<const __nv_bfloat16*>(k);

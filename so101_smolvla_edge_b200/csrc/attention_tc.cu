@@ -18,7 +18,7 @@
 // K and Q are K-major operands (head dim contiguous); V is an MN-major operand (head dim
 // contiguous along N, keys along K) straight from its TMA tile. Softmax in fp32 with exp2 on
 // log2(e)/sqrt(d)-scaled scores, P rounded to bf16 for P V, row sums from the fp32 P.
-#include "common.cuh"
+#include "tc_attn.cuh"
 
 namespace so101 {
 
@@ -65,32 +65,6 @@ static_assert(kTcSmem <= 232448, "227 KB of shared memory per CTA");
 // TMEM columns: S_A, S_B (128 fp32 each), P_A, P_B (64 each: 128 bf16 keys in pairs), O_A, O_B (64)
 constexpr uint32_t kColS = 0, kColP = 256, kColO = 384;
 
-// Instruction descriptor: bf16 A/B, fp32 D, A K-major, B K-major (b_mn = 0) or MN-major (1).
-__host__ __device__ constexpr uint32_t idesc_attn(int n, int b_mn) {
-  return (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(b_mn) << 16) |
-         (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(128 >> 4) << 24);
-}
-
-
-// Two floats rounded to bf16 (nearest even) and packed, the first in the low half.
-__device__ __forceinline__ uint32_t bf16x2(float lo, float hi) {
-  const __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
-  return *reinterpret_cast<const uint32_t*>(&h);
-}
-
-// (d0, d1) = (a0 * b + c, a1 * b + c) as one packed fp32x2 FMA.
-__device__ __forceinline__ void fma2(float& d0, float& d1, float a0, float a1, float b, float c) {
-  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
-      "mov.b64 ra, {%2, %3};\n\t"
-      "mov.b64 rb, {%4, %4};\n\t"
-      "mov.b64 rc, {%5, %5};\n\t"
-      "fma.rn.f32x2 rd, ra, rb, rc;\n\t"
-      "mov.b64 {%0, %1}, rd;\n\t}"
-      : "=f"(d0), "=f"(d1)
-      : "f"(a0), "f"(a1), "f"(b), "f"(c));
-}
-
-
 // 2^x for a pair, on the FMA and integer pipes instead of the MUFU unit (which the exp2 of the
 // other pairs keeps busy). x = j + f with j = rint(x) and |f| <= 1/2: adding 1.5 * 2^23 rounds x
 // to an integer held in the low mantissa bits of t; 2^f comes from a degree-3 polynomial (a
@@ -109,53 +83,6 @@ __device__ __forceinline__ float2 exp2_poly2(float2 x) {
   q = ffma2(q, f, make_float2(9.999280572e-01f, 9.999280572e-01f));
   return make_float2(__uint_as_float(__float_as_uint(q.x) + (__float_as_uint(t.x) << 23)),
                      __uint_as_float(__float_as_uint(q.y) + (__float_as_uint(t.y) << 23)));
-}
-
-// (s0, s1) += (a0, a1) as one packed fp32x2 add.
-__device__ __forceinline__ void add2(float& s0, float& s1, float a0, float a1) {
-  asm("{\n\t.reg .b64 rs, ra;\n\t"
-      "mov.b64 rs, {%0, %1};\n\t"
-      "mov.b64 ra, {%2, %3};\n\t"
-      "add.rn.f32x2 rs, rs, ra;\n\t"
-      "mov.b64 {%0, %1}, rs;\n\t}"
-      : "+f"(s0), "+f"(s1)
-      : "f"(a0), "f"(a1));
-}
-
-// 32 lanes x 32 consecutive 32-bit columns: this thread's lane, columns [col, col+32).
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t* r) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
-      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr));
-}
-
-// This thread's lane, columns [col, col+16) <- r.
-__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* r) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
-      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16};" ::"r"(taddr),
-      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
-      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
-      : "memory");
-}
-
-__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
-
-// D[tmem] (+)= A[tmem] * B[smem desc]: A (M 128 x K 16 bf16) in TMEM, two K elements per column.
-__device__ __forceinline__ void mma_f16_ta(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
-                                           uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
 }
 
 __global__ void __launch_bounds__(kTcThreads, 1)

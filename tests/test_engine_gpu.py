@@ -113,6 +113,23 @@ def test_backend_seams_match_reference(config0_engine):
     assert rel(v[0].cpu().numpy(), g["s0.v0"]) < 3e-2, rel(v[0].cpu().numpy(), g["s0.v0"])
 
 
+def test_second_engine_reuses_packed_weights(config0_engine):
+    """A second Engine on the same bundle and device skips the upload and packing (the packed
+    set is shared) and gives the same chunk bit for bit."""
+    from so101_smolvla_edge_b200.engine import Engine
+    from so101_smolvla_edge_b200.path import Packed
+
+    n0 = Packed.packs
+    t0 = time.perf_counter()
+    e2 = Engine(config0_bundle(), warmup=1)
+    build_s = time.perf_counter() - t0
+    assert Packed.packs == n0 and e2.path.packed is config0_engine.path.packed, build_s
+    images, state, noise = observation(e2.bundle, 0)
+    assert np.array_equal(e2.infer(images, state, noise), config0_engine.infer(images, state, noise))
+    del e2
+    torch.cuda.empty_cache()
+
+
 def test_config0_actions_within_north_star(config0_engine):
     """configs[0] (3 x 512^2 cameras, 241-token prefix, 10 steps): every golden seed within
     1e-2 rad of the reference's float32 chunk; replays are deterministic."""

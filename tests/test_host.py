@@ -191,3 +191,36 @@ def test_backend_seams_on_a_stub_library():
     assert "so101_preprocess" not in [c[0] for c in lib.calls]
     assert out.shape == (s.n_cams * s.img_tokens, s.text_dim)
     assert out.data_ptr() == p.x_pre.data_ptr()
+
+
+def test_packed_weights_are_shared_per_bundle():
+    """A second path on the same bundle and device reuses the first one's packed weights (no
+    second upload or int8 packing); another int8 selection gets its own set, and the set is
+    dropped with the last path that uses it."""
+    import gc
+
+    import torch
+    from conftest import case_bundle
+
+    from so101_smolvla_edge_b200.path import B200Path, Packed
+
+    b = case_bundle("small64_absolute")
+    lib = _StubLib()
+    n0 = Packed.packs
+    p1 = B200Path(b, torch.device("cpu"), lib=lib)
+    p2 = B200Path(b, torch.device("cpu"), lib=lib)
+    assert Packed.packs == n0 + 1 and p1.packed is p2.packed
+    assert p1.w["txt.0.qkv"].data_ptr() == p2.w["txt.0.qkv"].data_ptr()
+    assert p1.w["txt.0.qkv"].dtype == torch.bfloat16
+    clip = {"vis.0.fc1": 3.0, "conn": 5.0}
+    lib.calls.clear()
+    p3 = B200Path(b, torch.device("cpu"), vision_precision="int8", act_clip=clip, lib=lib)
+    assert Packed.packs == n0 + 2 and p3.packed is not p1.packed
+    assert sorted(p3.wq) == ["conn", "vis.0.fc1"]
+    assert [c[0] for c in lib.calls].count("so101_quantize_weight") == 2
+    p4 = B200Path(b, torch.device("cpu"), vision_precision="int8", act_clip=clip, lib=lib)
+    assert p4.packed is p3.packed and Packed.packs == n0 + 2
+    key_count = len(Packed._cache)
+    del p3, p4
+    gc.collect()
+    assert len(Packed._cache) == key_count - 1

@@ -296,19 +296,29 @@ def test_siglip_attention_batched(out):
     assert torch.equal(got, again)
 
 
-@pytest.mark.parametrize("case", ["expert_self", "expert_cross", "prefix", "five_heads_per_kv"])
+@pytest.mark.parametrize("case", ["expert_self", "expert_cross", "prefix", "five_heads_per_kv", "prefix_v_rows",
+                                  "long_queries", "one_head_per_kv"])
 def test_attention_gqa_batched(case):
     """The batched prefix and expert shapes (hundreds of CTAs, grouped query heads over shared kv
     heads, prefix-LM and causal masks, RoPE on q) against the float32 reference for a sample of the
-    batch; replays are equal."""
+    batch; replays are equal. "prefix_v_rows" reads
+    q and v as column slices of fused qkv rows (the prefix's cross layers), "long_queries" needs two
+    256-row query blocks per head. The prefix shapes (at least 128 query rows per head) run the
+    masked tcgen05 kernel; the expert's 50-row shapes and "five_heads_per_kv" run mma.sync."""
     from so101_smolvla_edge_b200.ops import attention
 
     B, hd = 48, 64
     nq, nkv, lq, lk, cf, qo = {"expert_self": (15, 5, 50, 291, 241, 241), "expert_cross": (15, 5, 50, 241, 241, 0),
-                               "prefix": (15, 5, 241, 241, 240, 0), "five_heads_per_kv": (5, 1, 50, 178, 128, 128)}[case]
-    q = rnd(B, lq, nq * hd, dtype=torch.bfloat16, scale=2.0)
+                               "prefix": (15, 5, 241, 241, 240, 0), "five_heads_per_kv": (5, 1, 50, 178, 128, 128),
+                               "prefix_v_rows": (15, 5, 241, 241, 240, 0), "long_queries": (3, 1, 300, 300, 299, 0),
+                               "one_head_per_kv": (4, 4, 77, 200, 150, 120)}[case]  # fmt: skip
+    if case == "prefix_v_rows":
+        qkv = rnd(B, lq, (nq + 2 * nkv) * hd, dtype=torch.bfloat16, scale=2.0)
+        q, v = qkv[:, :, : nq * hd], qkv[:, :, (nq + nkv) * hd :]
+    else:
+        q = rnd(B, lq, nq * hd, dtype=torch.bfloat16, scale=2.0)
+        v = rnd(B, lk, nkv * hd, dtype=torch.bfloat16, seed=2)
     k = rnd(B, lk, nkv * hd, dtype=torch.bfloat16, seed=1)
-    v = rnd(B, lk, nkv * hd, dtype=torch.bfloat16, seed=2)
     cos, sin = rope_tables(torch.arange(qo, qo + lq, device="cuda"), hd, 10000.0)
     got = attention(q, k, v, nq, nkv, cos=cos, sin=sin, causal_from=cf, q_offset=qo)
     vis = visibility(lq, lk, cf, qo)
