@@ -539,6 +539,23 @@ def run_ours(args) -> None:
                  "achieved": aflops / (ams * 1e-3) / 1e12, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
                  "traffic": profile_traffic("vis.attn"), "ms": ams, "peak_source": f"{src} bf16 dense"}  # fmt: skip
     roof_attn["frac"] = roof_attn["achieved"] / roof_attn["peak"]
+    # third family, the largest by launches: the bf16 GEMMs of the batched prefix and expert. The
+    # expert's down projection (M = batch x 50, N = 720, K = 2048, fp32 residual epilogue with the
+    # next norm's bf16 operand and statistics) timed alone, against the sustained bf16 peak (these
+    # GEMMs run inside a long step)
+    fn, cargs = find_call(p.progs["denoise"], "s0.0.down")
+    gms = time_call(fn, cargs)
+    Mg, Ng, Kg = batch * s.chunk, s.exp_dim, s.exp_mlp
+    gplan = plans.get("s0.0.down")
+    gname = ("gemm_pair_kernel<%d,0,0>" % gplan[1] if gplan and gplan[4] & 8 else
+             "gemm_persistent_kernel<%d,0,0>" % gplan[1] if gplan else "library pick")  # fmt: skip
+    gbytes = Mg * Kg * 2 + Ng * Kg * 2 + Mg * Ng * (4 + 4 + 2)  # x, W, residual in/out, bf16 copy
+    roof_gemm = {"kernel": f"{gname} s0.0.down (M={Mg}, N={Ng}, K={Kg}, bf16, residual + norm operand)",
+                 "bound": "tensor", "achieved": 2.0 * Mg * Ng * Kg / (gms * 1e-3) / 1e12,
+                 "peak": pk["bf16_tflops_sustained"], "unit": "TFLOP/s", "ms": gms, "bytes": gbytes,
+                 "traffic": profile_traffic("exp.down/" + gname.split("<")[0]),
+                 "peak_source": f"{src} bf16 dense, sustained"}  # fmt: skip
+    roof_gemm["frac"] = roof_gemm["achieved"] / roof_gemm["peak"]
     launches = eng.launches()
     del eng
     torch.cuda.empty_cache()
@@ -615,6 +632,7 @@ def run_ours(args) -> None:
             "int8_parity": parity,
             "roofline": roof,
             "roofline_attention": roof_attn,
+            "roofline_gemm_bf16": roof_gemm,
             "latency": lat,
             "clocks": clk,
             "cpu_baseline": cpu,

@@ -249,6 +249,19 @@ SO101_API int so101_preprocess(const uint8_t* img, int n_img, int h, int w, int 
 SO101_API int so101_patchify(const float* px, int n_img, int S, int P, void* patches, int y_type, float y_qscale,
                              cudaStream_t stream);
 
+/* SigLIP patch embedding straight from camera frames at the model's size (no resize): uint8
+ * (n_img, S, S, 3) -> per 16 x 16 patch, (v / 255) * 2 - 1 in bf16, unfolded as channel, row,
+ * column -> y (n_img * (S/16)^2, N) fp32 = patches @ w^T + bias + pos[row % period]. The
+ * preprocessing of model/engine.py:236-245 and the unfold of model/smolvla.py:166-168 run inside
+ * the patch GEMM's operand producer (the patch rows never reach global memory); the result equals
+ * so101_preprocess followed by so101_gemm bit for bit. w: (N, 768) bf16, N a multiple of 256;
+ * S a multiple of 16 with G = S / 16 dividing 128 and G^2 a multiple of 128 (every 128
+ * consecutive patches are whole patch rows of one frame: S = 256, 512); every pointer 16-byte
+ * aligned. */
+SO101_API int so101_patch_embed(const uint8_t* img, int n_img, int S, const void* w, int64_t ldw, int64_t N,
+                                const float* bias, const float* pos, int64_t period, float* y, int64_t ldy,
+                                cudaStream_t stream);
+
 /* Dense fp32 linear on CUDA cores (the reference keeps these small MLPs fp32):
  * y[m, n] = act(x[m, :] @ w[n, :] + bias[n] (+ bias2[n])), act 0 none, 2 SiLU (act 1 is
  * accepted and means none: SiLU belongs on the producer's output). K, ldx, ldw multiples of 4,

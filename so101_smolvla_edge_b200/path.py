@@ -255,11 +255,7 @@ class B200Path:
         vx = Program("velocity")
         self._build_step(vx, 0, self.x_seam, self.v_buf, 1.0, tp=self.tp_seam)
         vp = Program("vision_px")
-        s = self.spec
-        vp.add("patchify", self.lib.so101_patchify, self.px_seam.data_ptr(), self.B * self.C, s.image_size,
-               s.patch, self.patches.data_ptr(), DTYPE[self.patches.dtype], self._qs("patch"))  # fmt: skip
-        vp.calls += [c for c in self.progs["vision"].calls if c[0] != "preprocess"]
-        vp._keep = [self.progs["vision"]]
+        self._build_vision(vp, source="px")
         self.seams = {"prefix": pl, "velocity": vx, "vision": vp}
 
     def autotune(self, reps: int = 5) -> dict[str, dict]:
@@ -518,7 +514,23 @@ class B200Path:
         return self.clip[name] / 127.0 if (self.int8 and name in self.clip) else 0.0
 
     # ------------------------------------------------------------------ vision
-    def _build_vision(self, p: Program) -> None:
+    def fused_patch(self) -> bool:
+        """Whether the frames go straight into the patch GEMM (so101_patch_embed), which needs
+        frames at the model's size (no resize), 16-pixel patches whose 128-patch blocks are whole
+        patch rows of a frame, a bf16 patch GEMM and a feature count that is a multiple of 256.
+        Opt-in (SO101_FUSED_PATCH=1): on B200 it is slower than the separate launches (917 against
+        670 us at 64 observations, 85 against 25 us at one), because each 128-patch tile streams the
+        whole 1.2 MB weight matrix through its ring, far more than the patch rows it saves."""
+        s = self.spec
+        g = s.image_size // 16
+        can = (self.h_img == s.image_size and self.w_img == s.image_size and s.patch == 16
+               and s.vis_dim % 256 == 0 and 128 % g == 0 and (g * g) % 128 == 0
+               and self._qs("patch") == 0.0 and self._amax is None)  # fmt: skip
+        return can and os.environ.get("SO101_FUSED_PATCH", "0") == "1"
+
+    def _build_vision(self, p: Program, source: str = "frames") -> None:
+        """The vision tower's launches from the uint8 frames (img), or from preprocessed px
+        (source "px", the TrtVision seam)."""
         s, w = self.spec, self.w
         B, C_, Np = self.B, self.C, self.Np
         S = s.image_size
@@ -529,10 +541,20 @@ class B200Path:
         hd = vd // nh
         rows_v = B * C_ * Np
         qs = self._qs("patch")
-        p.add("preprocess", self.lib.so101_preprocess, self.img.data_ptr(), B * C_, h, wd, rh, rw, S,
-              s.patch, self.patches.data_ptr(), DTYPE[self.patches.dtype], qs)  # fmt: skip
-        self._lin(p, "patch", self.patches, "vis.patch.w", self.xv, bias=w["vis.patch.b"],
-                  residual=w["vis.pos"], r_period=Np)  # fmt: skip
+        if source == "frames" and self.fused_patch():
+            pw = w["vis.patch.w"]
+            p.add("patch_embed", self.lib.so101_patch_embed, self.img.data_ptr(), B * C_, S, pw.data_ptr(),
+                  pw.stride(0), vd, w["vis.patch.b"].data_ptr(), w["vis.pos"].data_ptr(), Np, self.xv.data_ptr(),
+                  self.xv.stride(0))  # fmt: skip
+        else:
+            if source == "px":
+                p.add("patchify", self.lib.so101_patchify, self.px_seam.data_ptr(), B * C_, S, s.patch,
+                      self.patches.data_ptr(), DTYPE[self.patches.dtype], qs)  # fmt: skip
+            else:
+                p.add("preprocess", self.lib.so101_preprocess, self.img.data_ptr(), B * C_, h, wd, rh, rw, S,
+                      s.patch, self.patches.data_ptr(), DTYPE[self.patches.dtype], qs)  # fmt: skip
+            self._lin(p, "patch", self.patches, "vis.patch.w", self.xv, bias=w["vis.patch.b"],
+                      residual=w["vis.pos"], r_period=Np)  # fmt: skip
         for i in range(s.vis_layers):
             pre = f"vis.{i}."
             hv = self._vis_in(pre + "qkv", self.hv_bf, self.hv_i8)

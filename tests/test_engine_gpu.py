@@ -113,6 +113,30 @@ def test_backend_seams_match_reference(config0_engine):
     assert rel(v[0].cpu().numpy(), g["s0.v0"]) < 3e-2, rel(v[0].cpu().numpy(), g["s0.v0"])
 
 
+def test_fused_patch_embedding_equals_separate_preprocessing(config0_engine, monkeypatch):
+    """With SO101_FUSED_PATCH=1 the engine's frames go straight into the patch GEMM
+    (so101_patch_embed, no patch rows in global memory); by default it launches so101_preprocess
+    and the patch GEMM. The image rows agree bit for bit when the patch GEMM does not split K."""
+    from so101_smolvla_edge_b200.engine import Engine
+
+    assert not config0_engine.path.fused_patch()  # opt-in
+    monkeypatch.setenv("SO101_FUSED_PATCH", "1")
+    e1 = Engine(config0_bundle(), warmup=1)
+    assert e1.path.fused_patch()
+    names = [c[0] for c in e1.path.progs["vision"].calls]
+    assert "patch_embed" in names and "preprocess" not in names and "patch" not in names
+    images, state, noise = observation(e1.bundle, 2)
+    rows = []
+    for eng in (e1, config0_engine):
+        eng._stage([images], [state], [noise])
+        eng._vision()
+        torch.cuda.synchronize()
+        rows.append(eng.path.xv.clone())
+    assert torch.equal(rows[0], rows[1])  # the library's pick for 3072 x 768 x 768 does not split K
+    del e1
+    torch.cuda.empty_cache()
+
+
 def test_second_engine_reuses_packed_weights(config0_engine):
     """A second Engine on the same bundle and device skips the upload and packing (the packed
     set is shared) and gives the same chunk bit for bit."""

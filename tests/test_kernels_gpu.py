@@ -16,6 +16,10 @@ pytestmark = pytest.mark.gpu
 F = torch.nn.functional
 
 
+def _p(t):
+    return None if t is None else t.data_ptr()
+
+
 def rnd(*shape, dtype=torch.float32, scale=1.0, seed=0):
     g = torch.Generator(device="cuda").manual_seed(seed)
     return (torch.randn(*shape, generator=g, device="cuda") * scale).to(dtype)
@@ -585,6 +589,50 @@ def test_preprocess_patches_match_torch(y):
         assert (out - ref).abs().max().item() <= 1e-5
     else:
         assert torch.equal(out, ref.to(dt))
+
+
+@pytest.mark.parametrize("n,S,N,extras", [(3, 512, 768, True), (5, 256, 256, True), (20, 512, 768, True),
+                                          (2, 512, 512, False)])  # fmt: skip
+def test_patch_embed_equals_preprocess_then_gemm(n, S, N, extras):
+    """so101_patch_embed (the frames converted inside the patch GEMM's operand producer) gives the
+    same bits as so101_preprocess writing the patch rows followed by so101_gemm over them with the
+    bias and the position table as a periodic residual, K unsplit. (20, 512): 160 row blocks, more
+    than one per CTA; (5, 256): 16 x 16 patches per frame; (2, 512, 512): no bias or positions."""
+    import ctypes as C
+
+    from so101_smolvla_edge_b200 import _lib as L
+
+    lib = L.lib()
+    st = torch.cuda.current_stream().cuda_stream
+    g = torch.Generator(device="cuda").manual_seed(4)
+    img = torch.randint(0, 256, (n, S, S, 3), generator=g, device="cuda", dtype=torch.uint8)
+    G = S // 16
+    M, K = n * G * G, 768
+    w = (torch.randn(N, K, generator=g, device="cuda") * 0.02).to(torch.bfloat16)
+    bias = torch.randn(N, generator=g, device="cuda") * 0.1 if extras else None
+    pos = torch.randn(G * G, N, generator=g, device="cuda") * 0.02 if extras else None
+    got = torch.full((M, N), float("nan"), device="cuda")
+    L.check(lib.so101_patch_embed(img.data_ptr(), n, S, w.data_ptr(), K, N, _p(bias), _p(pos), G * G,
+                                  got.data_ptr(), N, st), "so101_patch_embed")  # fmt: skip
+    patches = torch.empty(M, K, dtype=torch.bfloat16, device="cuda")
+    L.check(lib.so101_preprocess(img.data_ptr(), n, S, S, S, S, S, 16, patches.data_ptr(), L.BF16, 0.0, st),
+            "so101_preprocess")  # fmt: skip
+    want = torch.empty(M, N, device="cuda")
+    epi = L.Epilogue(epilogue=L.EPI_NONE, bias=_p(bias), residual=_p(pos), ldr=N if extras else 0,
+                     r_type=L.F32, r_period=G * G if extras else 0, out_scale=1.0)  # fmt: skip
+    from so101_smolvla_edge_b200.ops import workspace
+
+    cfg = L.GemmConfig(0, 256, 1, 0, 0)
+    ws = workspace(img.device)
+    L.check(lib.so101_gemm(L.BF16, patches.data_ptr(), K, w.data_ptr(), K, want.data_ptr(), N, L.F32, M, N, K,
+                           C.byref(epi), C.byref(cfg), ws.partials.data_ptr(), ws.nbytes, ws.tickets.data_ptr(),
+                           ws.tickets.numel(), st), "so101_gemm")  # fmt: skip
+    torch.cuda.synchronize()
+    assert torch.equal(got, want), float((got - want).abs().max())
+    assert L.lib().so101_device_status() == 0
+    # frames whose 128 consecutive patches are not whole patch rows of one frame are refused
+    assert lib.so101_patch_embed(img.data_ptr(), 1, 64, w.data_ptr(), K, N, None, None, 1, got.data_ptr(), N,
+                                 st) == L.ERR_ARG  # fmt: skip
 
 
 def test_rms_stats_matches_torch():
