@@ -643,6 +643,114 @@ def run_ours(args) -> None:
         dist.destroy_process_group()
 
 
+# ------------------------------------------------------------------------------ profiling cases
+# Single kernels on the model's real shapes with seeded random operands, for ncu captures
+# (`python bench.py --profile-case NAME`): each case launches its kernel --reps times after the
+# producer of its inputs, as in the engine, so `ncu -k regex:<kernel> -s 2 -c 1` captures a warm
+# launch. Nothing is checked: the kernels' parity is the tests' business.
+def _rnd(g, *shape, scale=1.0, dtype=None):
+    import torch
+
+    return (torch.randn(*shape, device="cuda", generator=g) * scale).to(dtype or torch.float32)
+
+
+def case_mlp(g, reps: int) -> None:
+    """so101_mlp: the expert's SwiGLU block at one observation (50 rows, 720 -> 2048 -> 720)."""
+    import torch
+
+    from so101_smolvla_edge_b200.ops import mlp, rms_stats
+
+    e = _rnd(g, 50, 720)
+    x16 = torch.empty(50, 720, device="cuda", dtype=torch.bfloat16)
+    ss = torch.zeros(50, 64, device="cuda")
+    w_gu = _rnd(g, 4096, 720, scale=0.03, dtype=torch.bfloat16)
+    w_d = _rnd(g, 720, 2048, scale=0.02, dtype=torch.bfloat16)
+    nw = torch.ones(720, device="cuda")
+    for _ in range(reps):
+        rms_stats(e, x16, ss, nw)
+        mlp(x16, w_gu, w_d, e, residual=e, rms=(ss, 1, 1e-5), y16=x16, y16_scale=nw, stat_ss=ss)
+
+
+def case_attention_o(g, reps: int) -> None:
+    """so101_attention_o: an expert self-attention layer at one observation (50 queries, 291 keys)."""
+    import torch
+
+    from so101_smolvla_edge_b200.ops import attention_o, rms_stats
+
+    qkv = _rnd(g, 50, 1600, dtype=torch.bfloat16)
+    k, v = _rnd(g, 291, 320, dtype=torch.bfloat16), _rnd(g, 291, 320, dtype=torch.bfloat16)
+    cs = torch.rand(50, 32, device="cuda", generator=g)
+    w_o = _rnd(g, 720, 960, scale=0.02, dtype=torch.bfloat16)
+    e = _rnd(g, 50, 720)
+    x16 = torch.empty(50, 720, device="cuda", dtype=torch.bfloat16)
+    ss = torch.zeros(50, 64, device="cuda")
+    nw = torch.ones(720, device="cuda")
+    own = (qkv[:, 960:1280], qkv[:, 1280:], 241, cs, cs)
+    for _ in range(reps):
+        rms_stats(e, x16, ss, nw)
+        attention_o(qkv[:, :960], k, v, 15, 5, w_o, e, residual=e, cos=cs, sin=cs, causal_from=241, q_offset=241,
+                    own=own, y16=x16, y16_scale=nw, stat_ss=ss)  # fmt: skip
+
+
+def case_fc2(g, reps: int) -> None:
+    """so101_gemm: vision fc2 plus residual at one observation (3072 rows, K = 3072)."""
+    import torch
+
+    from so101_smolvla_edge_b200.ops import linear
+
+    x = _rnd(g, 3072, 3072, dtype=torch.bfloat16)
+    w = _rnd(g, 768, 3072, scale=0.02, dtype=torch.bfloat16)
+    r = _rnd(g, 3072, 768)
+    for _ in range(reps):
+        linear(x, w, residual=r, out=r)
+
+
+def case_expert_down64(g, reps: int) -> None:
+    """so101_gemm: the batched expert's down projection at 64 observations (3200 rows, 2048 -> 720)
+    with the residual epilogue that writes the next norm's bf16 operand and statistics, on the
+    persistent 192-wide plan the engine's autotune picks for it."""
+    import torch
+
+    from so101_smolvla_edge_b200.ops import linear
+
+    x = _rnd(g, 3200, 2048, dtype=torch.bfloat16)
+    w = _rnd(g, 720, 2048, scale=0.02, dtype=torch.bfloat16)
+    e = _rnd(g, 3200, 720)
+    x16 = torch.empty(3200, 720, device="cuda", dtype=torch.bfloat16)
+    ss = torch.zeros(3200, 64, device="cuda")
+    nw = torch.ones(720, device="cuda")
+    for _ in range(reps):
+        linear(x, w, residual=e, out=e, stat=(ss, x16, nw), config=(0, 192, 1, 0, 2))
+
+
+def case_gqa_prefix(g, reps: int) -> None:
+    """so101_attention: the prefix's grouped-query attention at 16 observations (241 rows, 15 / 5
+    heads, prefix-LM mask, RoPE), the masked tcgen05 kernel's case."""
+    import torch
+
+    from so101_smolvla_edge_b200.ops import attention
+
+    qkv = _rnd(g, 16, 241, 1600, dtype=torch.bfloat16)
+    k = _rnd(g, 16, 241, 320, dtype=torch.bfloat16)
+    cs = torch.rand(241, 32, device="cuda", generator=g)
+    out = torch.empty(16, 241, 960, dtype=torch.bfloat16, device="cuda")
+    for _ in range(reps):
+        attention(qkv[:, :, :960], k, qkv[:, :, 1280:], 15, 5, cos=cs, sin=cs, causal_from=240, out=out)
+
+
+PROFILE_CASES = {"mlp": case_mlp, "attention_o": case_attention_o, "fc2": case_fc2,
+                 "expert_down64": case_expert_down64, "gqa_prefix": case_gqa_prefix}  # fmt: skip
+
+
+def run_profile_case(name: str, reps: int) -> None:
+    import torch
+
+    g = torch.Generator(device="cuda").manual_seed(0)
+    PROFILE_CASES[name](g, reps)
+    torch.cuda.synchronize()
+    print(f"{name}: {reps} launches done", flush=True)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -658,7 +766,13 @@ def main() -> None:
     ap.add_argument("--reference-gpu-chunks", type=int, default=100,
                     help="chunks per reference GPU engine (0: skip the reference's own GPU paths)")
     ap.add_argument("--reference-gpu", choices=["triton", "torch"], default=None, help=argparse.SUPPRESS)
+    ap.add_argument("--profile-case", choices=sorted(PROFILE_CASES), default=None,
+                    help="launch one kernel on its real shape --reps times (for ncu captures) and exit")
+    ap.add_argument("--reps", type=int, default=4)
     a = ap.parse_args()
+    if a.profile_case:
+        run_profile_case(a.profile_case, a.reps)
+        return
     if a.reference_gpu:
         reference_gpu_probe(a.reference_gpu, a.latency_chunks)
         return
