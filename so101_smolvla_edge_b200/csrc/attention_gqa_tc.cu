@@ -40,39 +40,57 @@ constexpr int kGqRows = 128;
 constexpr int kGqKeys = 128;
 constexpr int kGqHd = 64;
 constexpr int kGqTile = kGqRows * kGqHd * 2;  // 16 KB
-constexpr int kGqStages = 4;
-constexpr int kGqThreads = 32 * 10;
 constexpr float kGqStaleMax = 8.f;
-constexpr int kGqOffQ = 0;
-constexpr int kGqOffK = kGqOffQ + 2 * kGqTile;
-constexpr int kGqOffV = kGqOffK + kGqStages * kGqTile;
-constexpr int kGqOffBar = kGqOffV + kGqStages * kGqTile;
 constexpr int kGqBarBytes = 512;
-static_assert((1 + 4 * kGqStages + 8) * 8 + 4 <= kGqBarBytes, "barrier region");
-constexpr int kGqSmem = kGqOffBar + kGqBarBytes + 1024;
-static_assert(kGqSmem <= 232448, "227 KB of shared memory per CTA");
-constexpr uint32_t kGqColS = 0, kGqColP = 256, kGqColO = 384;
 
-// Query row r of this CTA: its head and position, or false for a padding row.
-__device__ __forceinline__ bool gqa_row(const GqaArgs& a, int r, int head0, int qb, int& head, int& pos) {
+// NG query groups of 128 rows per CTA. Two (the prefix's 241-row heads): all 512 TMEM columns, a
+// four-stage K/V ring, one CTA per SM. One (the expert's 50-row heads, two per CTA): 256 columns
+// and a two-stage ring, two CTAs per SM, so the short, latency-bound CTAs overlap.
+template <int NG>
+struct GqCfg {
+  static constexpr int kStages = NG == 2 ? 4 : 2;
+  static constexpr int kThreads = 32 * (2 + 4 * NG);
+  static constexpr int kOffQ = 0;
+  static constexpr int kOffK = kOffQ + NG * kGqTile;
+  static constexpr int kOffV = kOffK + kStages * kGqTile;
+  static constexpr int kOffBar = kOffV + kStages * kGqTile;
+  static constexpr int kSmem = kOffBar + kGqBarBytes + 1024;
+  static constexpr uint32_t kCols = NG == 2 ? 512 : 256;
+  // TMEM columns: S (128 per group), P (64 per group: 128 bf16 keys in pairs), O (64 per group)
+  static constexpr uint32_t kColS = 0, kColP = NG * 128, kColO = NG * 128 + NG * 64;
+};
+static_assert((1 + 4 * 4 + 8) * 8 + 4 <= kGqBarBytes, "barrier region");
+static_assert(GqCfg<2>::kSmem <= 232448 && 2 * GqCfg<1>::kSmem <= 232448, "shared memory per CTA / SM");
+
+// Query row r of this CTA: its head and position, or false for a padding row. One head per CTA:
+// positions [rows qb, rows (qb + 1)); several: heads head0 .. head0 + n_heads - 1 stacked, Lq rows
+// each.
+template <int NG>
+__device__ __forceinline__ bool gqa_row(const GqaArgs& a, int r, int head0, int n_heads, int qb, int& head,
+                                        int& pos) {
   if (a.heads_per_cta == 1) {
     head = head0;
-    pos = qb * 2 * kGqRows + r;
+    pos = qb * NG * kGqRows + r;
   } else {
     head = head0 + r / a.Lq;
     pos = r % a.Lq;
-    if (r >= a.heads_per_cta * a.Lq) return false;
+    if (r >= n_heads * a.Lq) return false;
   }
   return pos < a.Lq;
 }
 
-__global__ void __launch_bounds__(kGqThreads, 1)
+template <int NG>
+__global__ void __launch_bounds__(GqCfg<NG>::kThreads, NG == 1 ? 2 : 1)
     attention_gqa_tc_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                             const GqaArgs a) {
+  using Cfg = GqCfg<NG>;
+  constexpr int kGqStages = Cfg::kStages;
+  constexpr int kGqOffQ = Cfg::kOffQ, kGqOffK = Cfg::kOffK, kGqOffV = Cfg::kOffV;
+  constexpr uint32_t kGqColS = Cfg::kColS, kGqColP = Cfg::kColP, kGqColO = Cfg::kColO;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + kGqOffBar);
-  uint64_t* q_full = bar;                      // [1] 8 softmax warps wrote their Q rows
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + Cfg::kOffBar);
+  uint64_t* q_full = bar;                      // [1] the softmax warps wrote their Q rows
   uint64_t* k_full = bar + 1;                  // [kGqStages]
   uint64_t* k_empty = k_full + kGqStages;      // [kGqStages]
   uint64_t* v_full = k_empty + kGqStages;      // [kGqStages]
@@ -88,15 +106,16 @@ __global__ void __launch_bounds__(kGqThreads, 1)
   const int qb = blockIdx.x % a.q_blocks, hg = blockIdx.x / a.q_blocks;
   const int kvh = blockIdx.y, obs = blockIdx.z;
   const int head0 = kvh * group + hg * a.heads_per_cta;
+  const int n_heads = min(a.heads_per_cta, group - hg * a.heads_per_cta);  // the last CTA may hold fewer
   // keys this CTA can see: up to the larger of causal_from - 1 and its last query's diagonal
-  const int last_pos = a.heads_per_cta == 1 ? min(a.Lq, (qb + 1) * 2 * kGqRows) - 1 : a.Lq - 1;
+  const int last_pos = a.heads_per_cta == 1 ? min(a.Lq, (qb + 1) * NG * kGqRows) - 1 : a.Lq - 1;
   long long last_key = a.causal_from - 1;
   if (last_pos + a.q_offset > last_key) last_key = last_pos + a.q_offset;
   if (last_key > a.Lk - 1) last_key = a.Lk - 1;
   const int n_tiles = static_cast<int>(last_key / kGqKeys) + 1;
 
   if (threadIdx.x == 0) {
-    mbar_init(q_full, 8);
+    mbar_init(q_full, 4 * NG);
     for (int i = 0; i < kGqStages; ++i) {
       mbar_init(&k_full[i], 1);
       mbar_init(&k_empty[i], 1);
@@ -112,7 +131,7 @@ __global__ void __launch_bounds__(kGqThreads, 1)
     fence_mbar_init();
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, 512);
+    tmem_alloc(tmem_slot, Cfg::kCols);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -155,8 +174,7 @@ __global__ void __launch_bounds__(kGqThreads, 1)
       bool ok = mbar_wait(q_full, 0, a.status) && mbar_wait(&k_full[0], 0, a.status);
       if (ok) {
         tc_fence_after();
-        issue_s(0, 0);
-        issue_s(0, 1);
+        for (int g = 0; g < NG; ++g) issue_s(0, g);
         mma_commit(&k_empty[0]);
       }
       for (int j = 0; j < n_tiles && ok; ++j) {
@@ -164,7 +182,7 @@ __global__ void __launch_bounds__(kGqThreads, 1)
         if (j + 1 < n_tiles) {
           const int sn = (j + 1) % kGqStages;
           ok = mbar_wait(&k_full[sn], static_cast<uint32_t>((j + 1) / kGqStages) & 1u, a.status);
-          for (int g = 0; g < 2 && ok; ++g) {
+          for (int g = 0; g < NG && ok; ++g) {
             ok = mbar_wait(&s_free[g], j & 1u, a.status);
             if (ok) {
               tc_fence_after();
@@ -176,7 +194,7 @@ __global__ void __launch_bounds__(kGqThreads, 1)
         }
         if (!mbar_wait(&v_full[st], static_cast<uint32_t>(j / kGqStages) & 1u, a.status)) break;
         const uint64_t vd = sw128_desc(smem_u32(smem + kGqOffV + st * kGqTile));
-        for (int g = 0; g < 2 && ok; ++g) {
+        for (int g = 0; g < NG && ok; ++g) {
           ok = mbar_wait(&p_full[g], j & 1u, a.status);
           if (!ok) break;
           tc_fence_after();
@@ -196,7 +214,7 @@ __global__ void __launch_bounds__(kGqThreads, 1)
     const int rl = quad * 32 + lane;  // TMEM lane = row within the group
     const int r = g * kGqRows + rl;
     int head = 0, pos = 0;
-    const bool live = gqa_row(a, r, head0, qb, head, pos);
+    const bool live = gqa_row<NG>(a, r, head0, n_heads, qb, head, pos);
     grid_dep_wait();
     {
       // this row's 64 query values, rotated in fp32 and rounded to bf16, into the K-major
@@ -353,7 +371,7 @@ __global__ void __launch_bounds__(kGqThreads, 1)
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 1) tmem_dealloc(tmem, 512);
+  if (warp == 1) tmem_dealloc(tmem, Cfg::kCols);
 }
 
 namespace {
@@ -391,6 +409,24 @@ int gq_map(CUtensorMap* m, const void* base, long long rows, long long cols, lon
 
 }  // namespace
 
+// How a problem maps onto CTAs: groups of 128 rows per CTA (NG), query heads stacked per CTA,
+// CTAs per kv head (head_groups) and 128 NG-row query blocks per head.
+struct GqPlan {
+  int ng, heads_per_cta, head_groups, q_blocks;
+};
+
+GqPlan gqa_plan(long long Lq, int nq, int nkv) {
+  GqPlan p;
+  const int group = nq / nkv;
+  p.ng = Lq <= 64 ? 1 : 2;
+  const long long rows = static_cast<long long>(p.ng) * kGqRows;
+  p.heads_per_cta = Lq <= rows ? static_cast<int>(rows / Lq) : 1;
+  if (p.heads_per_cta > group) p.heads_per_cta = group;
+  p.head_groups = (group + p.heads_per_cta - 1) / p.heads_per_cta;
+  p.q_blocks = p.heads_per_cta > 1 ? 1 : static_cast<int>((Lq + rows - 1) / rows);
+  return p;
+}
+
 // Whether the masked tcgen05 kernel serves this problem: head_dim 64, bf16 output, K/V rows of
 // every observation at a whole number of rows apart, 16-byte aligned rows and bases, enough
 // CTAs to fill the GPU (the mma.sync kernel splits keys over clusters when there are few).
@@ -406,36 +442,29 @@ bool attention_gqa_tc_eligible(const void* q, long long ldq, const void* k, long
       (ldo * 2) % 16 || (bq * 2) % 16 || (bo * 2) % 16)
     return false;
   if (cos && reinterpret_cast<uintptr_t>(cos) % 16) return false;
-  const int group = nq / nkv;
-  const int hpc = Lq <= 2 * kGqRows ? static_cast<int>(2 * kGqRows / Lq) : 1;
-  const int per = hpc >= group ? group : (group % hpc == 0 ? hpc : 1);
-  const long long q_blocks = per > 1 ? 1 : (Lq + 2 * kGqRows - 1) / (2 * kGqRows);
-  const long long ctas = q_blocks * (group / per) * nkv * static_cast<long long>(batch);
-  // the expert's 50-row problems stay on mma.sync: one 512-column TMEM CTA per SM leaves these
-  // latency-bound CTAs in waves (40 against 33 us at 64 observations), while the prefix's
-  // 241-row heads give each CTA enough work (87 against 92 us)
-  return Lq >= 128 && ctas >= 128 && batch <= 65535 && Lk * batch < (1LL << 31) / 2;
+  const GqPlan pl = gqa_plan(Lq, nq, nkv);
+  const long long ctas = static_cast<long long>(pl.q_blocks) * pl.head_groups * nkv * batch;
+  return ctas >= 128 && batch <= 65535 && Lk * batch < (1LL << 31) / 2;
 }
 
 int attention_gqa_tc_launch(const void* q, long long ldq, const void* k, long long ldk, const void* v, long long ldv,
                             void* o, long long ldo, long long Lq, long long Lk, int nq, int nkv,
                             long long causal_from, long long q_offset, const float* cos, const float* sin, int batch,
                             long long bq, long long bk, long long bv, long long bo, cudaStream_t stream) {
-  const int group = nq / nkv;
-  const int hpc = Lq <= 2 * kGqRows ? static_cast<int>(2 * kGqRows / Lq) : 1;
-  const int per = hpc >= group ? group : (group % hpc == 0 ? hpc : 1);
-  const int q_blocks = per > 1 ? 1 : static_cast<int>((Lq + 2 * kGqRows - 1) / (2 * kGqRows));
+  const GqPlan pl = gqa_plan(Lq, nq, nkv);
   CUtensorMap tk, tv;
   const long long k_rows = bk / ldk, v_rows = bv / ldv;
   int rc = gq_map(&tk, k, k_rows * batch, static_cast<long long>(nkv) * 64, ldk);
   if (!rc) rc = gq_map(&tv, v, v_rows * batch, static_cast<long long>(nkv) * 64, ldv);
   if (rc) return rc;
-  static bool configured = false;
-  if (!configured) {
-    const cudaError_t e =
-        cudaFuncSetAttribute(attention_gqa_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kGqSmem);
+  static bool configured[2] = {false, false};
+  if (!configured[pl.ng - 1]) {
+    const cudaError_t e = pl.ng == 1 ? cudaFuncSetAttribute(attention_gqa_tc_kernel<1>,
+                                                            cudaFuncAttributeMaxDynamicSharedMemorySize, GqCfg<1>::kSmem)
+                                     : cudaFuncSetAttribute(attention_gqa_tc_kernel<2>,
+                                                            cudaFuncAttributeMaxDynamicSharedMemorySize, GqCfg<2>::kSmem);
     if (e != cudaSuccess) return launch_error(e);
-    configured = true;
+    configured[pl.ng - 1] = true;
   }
   GqaArgs a;
   a.q = static_cast<const __nv_bfloat16*>(q);
@@ -448,8 +477,8 @@ int attention_gqa_tc_launch(const void* q, long long ldq, const void* k, long lo
   a.Lk = static_cast<int>(Lk);
   a.nq = nq;
   a.nkv = nkv;
-  a.heads_per_cta = per;
-  a.q_blocks = q_blocks;
+  a.heads_per_cta = pl.heads_per_cta;
+  a.q_blocks = pl.q_blocks;
   a.k_rows = k_rows;
   a.v_rows = v_rows;
   a.causal_from = causal_from;
@@ -458,9 +487,11 @@ int attention_gqa_tc_launch(const void* q, long long ldq, const void* k, long lo
   a.sin = sin;
   a.scale_log2 = static_cast<float>(1.4426950408889634 / 8.0);
   a.status = status_ptr();
-  const dim3 grid(static_cast<unsigned>(q_blocks * (group / per)), static_cast<unsigned>(nkv),
+  const dim3 grid(static_cast<unsigned>(pl.q_blocks * pl.head_groups), static_cast<unsigned>(nkv),
                   static_cast<unsigned>(batch));
-  return launch_kernel(attention_gqa_tc_kernel, grid, dim3(kGqThreads), kGqSmem, stream, tk, tv, a);
+  if (pl.ng == 1)
+    return launch_kernel(attention_gqa_tc_kernel<1>, grid, dim3(GqCfg<1>::kThreads), GqCfg<1>::kSmem, stream, tk, tv, a);
+  return launch_kernel(attention_gqa_tc_kernel<2>, grid, dim3(GqCfg<2>::kThreads), GqCfg<2>::kSmem, stream, tk, tv, a);
 }
 
 }  // namespace so101
