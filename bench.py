@@ -215,6 +215,7 @@ def reference_gpu_probe(kernels: str, chunks: int) -> None:
             names[ev.name] = names.get(ev.name, 0) + 1
     top = sorted(names.items(), key=lambda kv: -kv[1])
     print(json.dumps({"kernels": eng.kernels, "p50_ms": sm["p50_ms"], "p99_ms": sm["p99_ms"], "n": sm["n"],
+                      "chunks_per_s": 1e3 / sm["p50_ms"],
                       "stages_ms": stages, "max_err_rad": err, "build_s": build_s,
                       "launches_per_chunk": sum(names.values()),
                       "kernel_names": [f"{k} x{v}" for k, v in top[:24]],
@@ -237,7 +238,8 @@ def reference_gpu(chunks: int) -> dict:
         except subprocess.TimeoutExpired:
             out[kernels] = {"unavailable": "timed out after 900 s"}
     out["config"] = ("configs[3] through the reference's own Engine from baseline/_ref: batch 1, bf16, "
-                     "one CUDA graph per chunk, vision='torch' (TensorRT is not installed)")
+                     "one CUDA graph per chunk, vision='torch' (TensorRT is not installed); chunks_per_s = "
+                     "1000 / p50, the rate of its API, which serves one observation per call")
     return out
 
 
