@@ -97,7 +97,7 @@ typedef struct so101_epilogue {
 typedef struct so101_gemm_config {
   int swap;    /* 1: weights on the MMA M side (few token rows), 0: tokens on the M side */
   int bn;      /* MMA N: 16, 32, 48, 64 (swap) or 64, 128, 256, 192 (tokens on M; 192:   */
-               /* persistent kernel only, no SiLU gate)                                  */
+               /* persistent kernel or CTA pair only, no SiLU gate)                      */
   int splits;  /* K splits, reduced in split order (deterministic)                        */
   int stages;  /* shared-memory pipeline depth (0: chosen from the problem)               */
   int flags;   /* SO101_GEMM_* bits                                                       */
@@ -109,7 +109,8 @@ typedef struct so101_gemm_config {
 #define SO101_GEMM_GLOBAL_SPLITK 1     /* reduce split-K partials through the workspace       */
 #define SO101_GEMM_PERSISTENT 2        /* tokens on M, no split: always the persistent kernel */
 #define SO101_GEMM_ONE_TILE_PER_CTA 4  /* tokens on M: never the persistent kernel            */
-#define SO101_GEMM_PAIR 8              /* tokens on M, no split, bn 128/256: CTA-pair tiles    */
+#define SO101_GEMM_PAIR 8              /* tokens on M, no split, bn 128/192/256 (192 without  */
+                                       /* the SiLU gate): CTA-pair tiles                      */
                                        /* (256 x bn per two SMs, cta_group::2 MMAs)           */
 
 /* y (M x N) = epilogue(x (M x K) @ w (N x K)^T) on tcgen05 tensor cores, TMA-fed.

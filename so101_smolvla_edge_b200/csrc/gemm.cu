@@ -1351,7 +1351,7 @@ int plan_gemm(int a_type, long long M, long long N, long long K, int epi, const 
   pl->splits = ceil_div(pl->kb_total, pl->kb_per_split);  // no empty split
   c.splits = pl->splits;
   const bool pair = (c.flags & SO101_GEMM_PAIR) && !c.swap && pl->splits == 1 &&
-                    (c.bn == 256 || c.bn == 128);
+                    (c.bn == 256 || c.bn == 128 || (c.bn == 192 && !dual));
   pl->tiles_p = c.swap ? ceil_div(N, 128) : ceil_div(M, pair ? 256 : 128);
   pl->tiles_q = c.swap ? ceil_div(M, c.bn) : ceil_div(N, c.bn);
   pl->nacc = c.bn * (dual ? 2 : 1);
@@ -1363,7 +1363,7 @@ int plan_gemm(int a_type, long long M, long long N, long long K, int epi, const 
            ((c.flags & SO101_GEMM_PERSISTENT) || tiles >= sm_count()))
     pl->kind = kPersistent;
   if (!pair) c.flags &= ~SO101_GEMM_PAIR;
-  if (c.bn == 192 && pl->kind != kPersistent) return SO101_ERR_ARG;
+  if (c.bn == 192 && pl->kind != kPersistent && pl->kind != kPair) return SO101_ERR_ARG;
   pl->cluster = 1;
   if (pl->kind == kTile && pl->splits > 1 && pl->splits <= kMaxCluster && !(c.flags & SO101_GEMM_GLOBAL_SPLITK))
     pl->cluster = pl->splits;
@@ -1483,8 +1483,11 @@ int launch_bn(const CUtensorMap& tx, const CUtensorMap& tw, const GemmArgs& a, c
     const bool pers = pl.kind == kPersistent;
     if (pl.kind == kPair) {
       if (pl.cfg.bn == 128) return launch_pair<128, DUAL, I8>(tx, tw, a, pl, stream, pdl);
-      if constexpr (!DUAL)
+      if constexpr (!DUAL) {
         if (pl.cfg.bn == 256) return launch_pair<256, DUAL, I8>(tx, tw, a, pl, stream, pdl);
+        // N = 720 in four 256 x 192 tiles: 52 pairs on 104 SMs, 224 operand rows per SM
+        if (pl.cfg.bn == 192) return launch_pair<192, DUAL, I8>(tx, tw, a, pl, stream, pdl);
+      }
       return SO101_ERR_ARG;
     }
     switch (pl.cfg.bn) {

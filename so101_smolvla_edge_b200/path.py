@@ -39,11 +39,11 @@ from .spec import ModelSpec, vision_linear_names
 REPRS = {"absolute": 0, "delta": 1, "velocity": 2}
 STAT_SLOTS = 64  # statistics slots per row for the RMSNorm finished in a GEMM (so101_epilogue.rms_ss)
 # Plans `B200Path.autotune` times for a GEMM with many token rows (so101_gemm_config: swap, bn,
-# splits, stages, flags): the library's pick, the persistent kernel at three tile widths and the
-# CTA pair at two. None of them splits K, so the choice never changes the accumulation order.
+# splits, stages, flags): the library's pick, the persistent kernel and the CTA pair at three tile
+# widths each. None of them splits K, so the choice never changes the accumulation order.
 TUNE_CANDIDATES = (None, (0, 256, 1, 0, L.GEMM_PERSISTENT), (0, 192, 1, 0, L.GEMM_PERSISTENT),
                    (0, 128, 1, 0, L.GEMM_PERSISTENT), (0, 256, 1, 0, L.GEMM_PAIR),
-                   (0, 128, 1, 0, L.GEMM_PAIR))  # fmt: skip
+                   (0, 192, 1, 0, L.GEMM_PAIR), (0, 128, 1, 0, L.GEMM_PAIR))  # fmt: skip
 TUNE_MIN_ROWS = 1024  # token-tile candidates from this many rows on
 # Weight-streaming plans for at most 256 token rows (the expert and the prefix at batch 1): 32- and
 # 64-token tiles with 1-8 K splits over a cluster.

@@ -50,7 +50,8 @@ def candidates(m: int, dual: bool, int8: bool):
         if bn >= 128:
             out.append((0, bn, 1, 0, L.GEMM_PAIR))
     if not dual:
-        out.append((0, 192, 1, 0, L.GEMM_PERSISTENT))  # 192-wide persistent tiles (N = 720 in four)
+        out.append((0, 192, 1, 0, L.GEMM_PERSISTENT))  # 192-wide tiles (N = 720 in four)
+        out.append((0, 192, 1, 0, L.GEMM_PAIR))
     return out
 
 

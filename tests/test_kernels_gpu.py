@@ -141,19 +141,20 @@ def test_silu_gate_tiles(swap, bn, split, flags):
 
 @pytest.mark.parametrize("m,n,k", [(3072, 2304, 768), (3072, 768, 3072), (1000, 5120, 960), (300, 720, 200)])
 @pytest.mark.parametrize("epi", ["gelu", "residual", "silu_gate"])
-@pytest.mark.parametrize("plan", ["persistent", "one_tile", "pair", "persistent192"])
+@pytest.mark.parametrize("plan", ["persistent", "one_tile", "pair", "persistent192", "pair192"])
 def test_persistent_matches_one_tile_per_cta(m, n, k, epi, plan):
     """The persistent kernel (256 or 192 columns), one tile per CTA and the CTA-pair kernel (256-row
-    tiles over two SMs, cta_group::2) all match the reference, including tile counts that are not a
-    multiple of the grid and pair tiles whose second CTA lies wholly past the last row."""
-    flags = {"persistent": 2, "one_tile": 4, "pair": 8, "persistent192": 2}[plan]
+    tiles over two SMs, cta_group::2, 256 or 192 columns) all match the reference, including tile
+    counts that are not a multiple of the grid and pair tiles whose second CTA lies wholly past the
+    last row."""
+    flags = {"persistent": 2, "one_tile": 4, "pair": 8, "persistent192": 2, "pair192": 8}[plan]
     from so101_smolvla_edge_b200.ops import linear
 
     x = rnd(m, k, dtype=torch.bfloat16)
     w = rnd(2 * n if epi == "silu_gate" else n, k, dtype=torch.bfloat16, scale=k**-0.5, seed=1)
     kw = {"gelu": {"gelu": True, "bias": rnd(n, seed=2)}, "residual": {"residual": rnd(m, n, seed=3)},
           "silu_gate": {"silu_gate": True}}[epi]
-    bn = 128 if epi == "silu_gate" else (192 if plan == "persistent192" else 256)
+    bn = 128 if epi == "silu_gate" else (192 if plan.endswith("192") else 256)
     got = linear(x, w, config=(0, bn, 1, 0, flags), **kw)
     ok, err = close(got, gemm_ref(x, w, **kw), got.dtype)
     assert ok, err
