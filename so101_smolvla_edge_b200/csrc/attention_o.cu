@@ -124,7 +124,7 @@ __global__ void __launch_bounds__(128 * G, 1) attention_o_kernel(const __grid_co
   cluster_sync();
 
   cluster_token_reduce<kAoMaxHeads, kAoThreads>(a.ep, part, a.at.nq, nv, row0, tile, pf);
-  cluster_sync();  // no CTA leaves while a peer still reads its partial
+  cluster_sync_relaxed();  // no CTA leaves while a peer still reads its partial
   tc_fence_after();
   if (warp == 0) tmem_dealloc(tmem, kCols);
 }

@@ -465,7 +465,7 @@ __device__ __forceinline__ void attention_body(const AttnArgs& a, int split, int
         }
       }
     }
-    cluster_sync();  // peers keep their shared memory until every merge has read it
+    cluster_sync_relaxed();  // peers keep their shared memory until every merge has read it
     return;
   }
   const float inv0 = 1.f / l0, inv1 = 1.f / l1;

@@ -732,7 +732,7 @@ __global__ void __launch_bounds__(kTileThreads, (SWAP && DUAL) ? 1 : 2)
         }
       }
     }
-    cluster_sync();  // no CTA leaves while a peer still reads its shared memory
+    cluster_sync_relaxed();  // no CTA leaves while a peer still reads its shared memory
   } else {
     const int tile = p_tile * a.tiles_q + q_tile;
     uint32_t* ws = static_cast<uint32_t*>(a.ws);

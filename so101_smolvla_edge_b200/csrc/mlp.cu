@@ -231,7 +231,7 @@ __global__ void __launch_bounds__(kMlpThreads, 1) mlp_kernel(const __grid_consta
   tc_fence_before();
   cluster_sync();
   cluster_token_reduce<kMlpMaxCluster, kMlpThreads>(a.ep, part, static_cast<int>(gridDim.x), nv, row0, tile, pf);
-  cluster_sync();  // no CTA leaves while a peer still reads its partial
+  cluster_sync_relaxed();  // no CTA leaves while a peer still reads its partial
   tc_fence_after();
   if (warp == 0) tmem_dealloc(tmem, kCols);
 }
