@@ -8,11 +8,11 @@
 // output tile and 64-row query block. Each CTA
 //   1  issues the TMA load of its W_o block (128 features x 64, SWIZZLE_128B) before waiting for
 //      the previous grid: the weights do not depend on it;
-//   2  runs the flash attention of its head over all key tiles (attention_tile.cuh; a six-tile K/V
-//      ring, so the expert's 291 keys arrive in one round of loads; two or three warp groups
-//      taking the tiles in turn, whichever needs fewer rounds, merged at the end), writing the
-//      normalised rows as bf16 straight into the MMA's B operand tile in shared memory (the same
-//      bf16 rounding the unfused path applies before storing them);
+//   2  runs the attention of its head over all keys, writing the normalised rows as bf16 straight
+//      into the MMA's B operand tile in shared memory (the same bf16 rounding the unfused path
+//      applies before storing them): the mma.sync flash loop of attention_tile.cuh (a six-tile
+//      K/V ring; two or three warp groups taking the tiles in turn, merged at the end), or, opt-in
+//      (SO101_ATTN_O_TC=1) and when the keys fit six 64-key tiles, on tcgen05 (attention_head_tc);
 //   3  issues one M=128, N=64, K=64 tcgen05.mma: its head's fp32 partial (features x tokens) in
 //      TMEM, staged to shared memory;
 //   4  after a cluster barrier, sums whole tokens over the nq partials through DSMEM in head
@@ -21,9 +21,11 @@
 // Redundancy: every output tile's cluster recomputes the attention (a few microseconds of tensor
 // work on the key/value rows that L2 holds); what it saves is a dependent launch and the round
 // trip of the attention output through global memory.
+#include <cstdlib>
 #include <mutex>
 
 #include "attention_tile.cuh"
+#include "tc_attn.cuh"
 #include "token_reduce.cuh"
 
 namespace so101 {
@@ -32,6 +34,7 @@ struct AttnOArgs {
   AttnArgs at;       // at.o unused
   TokenEpilogue ep;  // output tile epilogue
   int q_blocks;      // 64-row query blocks per problem
+  int tc;            // 1: the attention on tcgen05 (every query block's keys fit kAoTcTiles tiles)
   int* status;
 };
 
@@ -46,6 +49,270 @@ static_assert(attention_smem_bytes<64, kAoBuf>() >= 64 * 128 * 4, "the fp32 part
 
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
+// ------------------------------------------------------------------ attention of one head on tcgen05
+// Query rows [q0, q0 + 64) of head h against all keys it can see, in one pass (no online rescaling):
+//   1  every thread: K and V rows into shared memory (cp.async, K-major SWIZZLE_128B rows of 128
+//      bytes, 64-key tiles back to back; rows past Lk zero), the step's own keys loaded, rotated
+//      (the RoPE K/V cache kernel's arithmetic) and stored by the threads; warp group 0: the query
+//      rows, rotated, into the Q operand tile (rows 64..127 zero);
+//   2  one thread: S = Q K^T, one M = 128, N = 64, K = 64 MMA per key tile, into TMEM columns
+//      [64 t, 64 t + 64);
+//   3  the warps of TMEM lanes 0..63 (G per lane quarter, key tiles dealt round robin): the row
+//      maximum of the scaled, masked scores, exchanged through shared memory; then
+//      p = 2^(s * scale - max) rounded to bf16 and the row sums; once every score is read, P is
+//      written over S (two keys per column, columns [32 t, 32 t + 32));
+//   4  one thread: O = P V (A = P from TMEM, B = V MN-major, K = 16 per MMA) into columns
+//      [kAoTcColO, +64);
+//   5  the first warp of each lane quarter: O / l (l summed over the G partial sums in order) as bf16
+//      into the output tile (the mma.sync path's layout: row r, chunk c at c ^ (r % 8); rows at or
+//      past Lq zero).
+// TMEM: 512 columns (S or P up to 384, O at 384). Shared memory: the attention area of the kernel.
+constexpr int kAoTcTiles = 6;  // 384 keys
+constexpr uint32_t kAoTcColO = 384;
+constexpr int kAoTcOffQ = 0;
+constexpr int kAoTcOffK = kAoTcOffQ + 128 * 128;
+constexpr int kAoTcOffV = kAoTcOffK + kAoTcTiles * 64 * 128;
+constexpr int kAoTcOffX = kAoTcOffV + kAoTcTiles * 64 * 128;  // [2][3][64] fp32: row maxima, row sums
+static_assert(kAoTcOffX + 2 * 3 * 64 * 4 <= attention_smem_bytes<64, kAoBuf>(), "the tcgen05 attention fits the area");
+
+// key tiles of 64 keys that query rows [q0, q0 + 64) can see (attention_body's count)
+__device__ __forceinline__ int ao_key_tiles(const AttnArgs& a, int q0) {
+  long long last = a.causal_from - 1;
+  const long long diag = static_cast<long long>(q0 + 63) + a.q_offset;
+  if (diag > last) last = diag;
+  if (last > a.Lk - 1) last = a.Lk - 1;
+  return static_cast<int>((last + 64) / 64);
+}
+
+// bf16 row pieces: chunks c (dims 8c..8c+7) and c + 4 (their rotary partners) rotated by the eight
+// cos/sin values of those dims, per-operation rounding, one rounding to bf16.
+__device__ __forceinline__ void ao_rotate(const uint4& u1, const uint4& u2, const float* cs, const float* sn, uint4& o1,
+                                          uint4& o2) {
+  const float4 ca = __ldg(reinterpret_cast<const float4*>(cs)), cb = __ldg(reinterpret_cast<const float4*>(cs + 4));
+  const float4 sa = __ldg(reinterpret_cast<const float4*>(sn)), sb = __ldg(reinterpret_cast<const float4*>(sn + 4));
+  const float cv[8] = {ca.x, ca.y, ca.z, ca.w, cb.x, cb.y, cb.z, cb.w};
+  const float sv[8] = {sa.x, sa.y, sa.z, sa.w, sb.x, sb.y, sb.z, sb.w};
+  const __nv_bfloat162* h1 = reinterpret_cast<const __nv_bfloat162*>(&u1);
+  const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&u2);
+  __nv_bfloat162* p1 = reinterpret_cast<__nv_bfloat162*>(&o1);
+  __nv_bfloat162* p2 = reinterpret_cast<__nv_bfloat162*>(&o2);
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const float2 x1 = __bfloat1622float2(h1[e]), x2 = __bfloat1622float2(h2[e]);
+    const float c0 = cv[2 * e], c1 = cv[2 * e + 1], s0 = sv[2 * e], s1 = sv[2 * e + 1];
+    p1[e] = __floats2bfloat162_rn(__fsub_rn(__fmul_rn(x1.x, c0), __fmul_rn(x2.x, s0)),
+                                  __fsub_rn(__fmul_rn(x1.y, c1), __fmul_rn(x2.y, s1)));
+    p2[e] = __floats2bfloat162_rn(__fadd_rn(__fmul_rn(x2.x, c0), __fmul_rn(x1.x, s0)),
+                                  __fadd_rn(__fmul_rn(x2.y, c1), __fmul_rn(x1.y, s1)));
+  }
+}
+
+// All 128 G threads call it. False when an MMA wait ran out (SO101_ERR_TIMEOUT recorded); the
+// output tile is then not written.
+template <int G>
+__device__ __forceinline__ bool attention_head_tc(const AttnArgs& a, int q0, int h, int bi, uint8_t* area,
+                                                  uint8_t* o_tile, uint32_t tmem, uint64_t* s_done, uint64_t* o_done,
+                                                  int* status) {
+  constexpr int NT = 128 * G;
+  constexpr int TPW = (kAoTcTiles + G - 1) / G;  // key tiles per softmax warp
+  const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+  const int kvh = h / (a.nq / a.nkv);
+  const __nv_bfloat16* K = a.k + bi * a.bk + static_cast<long long>(kvh) * 64;
+  const __nv_bfloat16* V = a.v + bi * a.bv + static_cast<long long>(kvh) * 64;
+  const bool own = a.k_own != nullptr;
+  const __nv_bfloat16* K_own = own ? a.k_own + bi * a.b_own + static_cast<long long>(kvh) * 64 : nullptr;
+  const __nv_bfloat16* V_own = own ? a.v_own + bi * a.b_own + static_cast<long long>(kvh) * 64 : nullptr;
+  const int n_tiles = ao_key_tiles(a, q0);
+  const int n_rows = n_tiles * 64;
+  const long long own_from = own ? a.own_from : a.Lk;
+  uint8_t* q_s = area + kAoTcOffQ;
+  uint8_t* k_s = area + kAoTcOffK;
+  uint8_t* v_s = area + kAoTcOffV;
+  float* x_max = reinterpret_cast<float*>(area + kAoTcOffX);  // [G][64]
+  float* x_sum = x_max + 3 * 64;                               // [G][64]
+
+  // 1. keys and values (own keys are rotated below), queries
+  for (int c = t; c < n_rows * 8; c += NT) {
+    const int j = c >> 3, cc = c & 7;
+    const bool ok = j < a.Lk;
+    const long long jj = ok ? j : 0;
+    const bool mine = jj >= own_from;
+    const uint32_t off = static_cast<uint32_t>(j * 128 + ((cc ^ (j & 7)) << 4));
+    if (!mine || !ok) cp_async16(smem_u32(k_s) + off, K + jj * a.ldk + cc * 8, ok ? 16 : 0);
+    const __nv_bfloat16* vs = mine ? V_own + (jj - own_from) * a.ld_own : V + jj * a.ldv;
+    cp_async16(smem_u32(v_s) + off, vs + cc * 8, ok ? 16 : 0);
+  }
+  cp_async_commit();
+  if (t < 128) {
+    const int i = q0 + t;
+    uint4 out[8];
+#pragma unroll
+    for (int c = 0; c < 8; ++c) out[c] = make_uint4(0u, 0u, 0u, 0u);
+    if (t < 64 && i < a.Lq) {
+      const uint4* qr = reinterpret_cast<const uint4*>(a.q + bi * a.bq + static_cast<long long>(i) * a.ldq + h * 64);
+      uint4 u[8];
+#pragma unroll
+      for (int c = 0; c < 8; ++c) u[c] = __ldcg(qr + c);
+      if (a.cos) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+          ao_rotate(u[c], u[c + 4], a.cos + static_cast<long long>(i) * 32 + 8 * c,
+                    a.sin + static_cast<long long>(i) * 32 + 8 * c, out[c], out[c + 4]);
+      } else {
+#pragma unroll
+        for (int c = 0; c < 8; ++c) out[c] = u[c];
+      }
+    }
+#pragma unroll
+    for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(q_s + t * 128 + ((c ^ (t & 7)) << 4)) = out[c];
+  }
+  if (own) {
+    const int j_lo = static_cast<int>(own_from), j_hi = min(a.Lk, n_rows);
+    for (int idx = t; idx < (j_hi - j_lo) * 4; idx += NT) {
+      const int j = j_lo + (idx >> 2), c = idx & 3;
+      const long long jr = j - own_from;
+      const uint4* kr = reinterpret_cast<const uint4*>(K_own + jr * a.ld_own);
+      uint4 o1, o2;
+      ao_rotate(__ldcg(kr + c), __ldcg(kr + c + 4), a.k_cos + jr * 32 + 8 * c, a.k_sin + jr * 32 + 8 * c, o1, o2);
+      *reinterpret_cast<uint4*>(k_s + j * 128 + ((c ^ (j & 7)) << 4)) = o1;
+      *reinterpret_cast<uint4*>(k_s + j * 128 + (((c + 4) ^ (j & 7)) << 4)) = o2;
+    }
+  }
+  cp_async_wait<0>();
+  fence_async_smem();  // cp.async and plain stores, before the tensor core reads them
+  tc_fence_before();
+  __syncthreads();
+
+  // 2. S = Q K^T
+  if (t == 0) {
+    tc_fence_after();
+    constexpr uint32_t ID_S = idesc_attn(64, 0);
+    const uint64_t qd = sw128_desc(smem_u32(q_s));
+    for (int tile = 0; tile < n_tiles; ++tile) {
+      const uint64_t kd = sw128_desc(smem_u32(k_s + tile * 64 * 128));
+#pragma unroll
+      for (int k = 0; k < 4; ++k) mma_f16(tmem + 64 * tile, qd + 2 * k, kd + 2 * k, ID_S, k > 0 ? 1u : 0u);
+    }
+    mma_commit(s_done);
+  }
+
+  // 3. softmax over TMEM lanes 0..63: quarter q = warp % 4 < 2, warp group g = warp / 4
+  const int quarter = warp & 3, g = warp >> 2;
+  const int row = quarter * 32 + lane, i = q0 + row;
+  const bool soft = quarter < 2;
+  const bool live = soft && i < a.Lq;
+  const uint32_t lane_base = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+  const float sc = a.scale_log2;
+  // keys [0, vis_end) are visible to row i
+  long long vis_end = static_cast<long long>(i) + a.q_offset + 1;
+  if (vis_end < a.causal_from) vis_end = a.causal_from;
+  if (vis_end > a.Lk) vis_end = a.Lk;
+  bool ok = true;
+  if (soft) {
+    ok = __all_sync(0xffffffffu, mbar_wait(s_done, 0, status) ? 1 : 0) != 0;
+    tc_fence_after();
+    float m = -INFINITY;
+    if (ok) {
+      for (int u = 0; u < TPW; ++u) {
+        const int tile = g + u * G;
+        if (tile >= n_tiles) break;
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          uint32_t sv[32];
+          tmem_ld32(lane_base + 64 * tile + 32 * half, sv);
+          tmem_ld_wait();
+          const int j0 = 64 * tile + 32 * half;
+#pragma unroll
+          for (int e = 0; e < 32; ++e)
+            if (j0 + e < vis_end) m = fmaxf(m, __uint_as_float(sv[e]) * sc);
+        }
+      }
+    }
+    x_max[g * 64 + row] = m;
+  }
+  __syncthreads();
+  uint32_t pk[TPW][32];
+  if (soft) {
+    float mx = x_max[row];
+#pragma unroll
+    for (int gg = 1; gg < G; ++gg) mx = fmaxf(mx, x_max[gg * 64 + row]);
+    const float neg_m = (live && mx != -INFINITY) ? -mx : 0.f;
+    float ls = 0.f;
+#pragma unroll
+    for (int u = 0; u < TPW; ++u) {
+      const int tile = g + u * G;
+      if (tile >= n_tiles || !ok) break;
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        uint32_t sv[32];
+        tmem_ld32(lane_base + 64 * tile + 32 * half, sv);
+        tmem_ld_wait();
+        const int j0 = 64 * tile + 32 * half;
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) {
+          float x0, x1;
+          fma2(x0, x1, __uint_as_float(sv[e]), __uint_as_float(sv[e + 1]), sc, neg_m);
+          const float p0 = (live && j0 + e < vis_end) ? ex2(x0) : 0.f;
+          const float p1 = (live && j0 + e + 1 < vis_end) ? ex2(x1) : 0.f;
+          ls += p0 + p1;
+          pk[u][16 * half + (e >> 1)] = bf16x2(p0, p1);
+        }
+      }
+    }
+    x_sum[g * 64 + row] = ls;
+  }
+  tc_fence_before();
+  __syncthreads();  // every score is read: P may overwrite S
+  if (soft && ok) {
+    tc_fence_after();
+#pragma unroll
+    for (int u = 0; u < TPW; ++u) {
+      const int tile = g + u * G;
+      if (tile >= n_tiles) break;
+      tmem_st16(lane_base + 32 * tile, pk[u]);
+      tmem_st16(lane_base + 32 * tile + 16, pk[u] + 16);
+    }
+    tmem_st_wait();
+  }
+  tc_fence_before();
+  __syncthreads();
+
+  // 4. O = P V
+  if (t == 0 && ok) {
+    tc_fence_after();
+    constexpr uint32_t ID_O = idesc_attn(64, 1);
+    const uint64_t vd = sw128_desc(smem_u32(v_s));
+    for (int k = 0; k < 4 * n_tiles; ++k)
+      mma_f16_ta(tmem + kAoTcColO, tmem + 8 * k, vd + static_cast<uint64_t>(k) * (2048 >> 4), ID_O, k > 0 ? 1u : 0u);
+    mma_commit(o_done);
+  }
+
+  // 5. O / l into the output tile
+  if (soft && g == 0) {
+    ok = ok && __all_sync(0xffffffffu, mbar_wait(o_done, 0, status) ? 1 : 0) != 0;
+    tc_fence_after();
+    if (ok) {
+      uint32_t ov[64];
+      tmem_ld32(lane_base + kAoTcColO, ov);
+      tmem_ld32(lane_base + kAoTcColO + 32, ov + 32);
+      tmem_ld_wait();
+      float l = x_sum[row];
+#pragma unroll
+      for (int gg = 1; gg < G; ++gg) l += x_sum[gg * 64 + row];
+      const float inv = live ? 1.f / l : 0.f;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        const float* v = reinterpret_cast<const float*>(ov) + 8 * c;
+        const uint4 val = live ? make_uint4(bf16x2(v[0] * inv, v[1] * inv), bf16x2(v[2] * inv, v[3] * inv),
+                                            bf16x2(v[4] * inv, v[5] * inv), bf16x2(v[6] * inv, v[7] * inv))
+                               : make_uint4(0u, 0u, 0u, 0u);
+        *reinterpret_cast<uint4*>(o_tile + row * 128 + ((c ^ (row & 7)) << 4)) = val;
+      }
+    }
+  }
+  return ok;
+}
+
 // G warp groups of 128 threads take the key tiles in turn (attention_body's WG).
 template <int G>
 __global__ void __launch_bounds__(128 * G, 1) attention_o_kernel(const __grid_constant__ CUtensorMap tm_w,
@@ -55,16 +322,20 @@ __global__ void __launch_bounds__(128 * G, 1) attention_o_kernel(const __grid_co
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* w_full = reinterpret_cast<uint64_t*>(smem + kAoOffBar);
   uint64_t* mma_done = w_full + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+  uint64_t* s_done = mma_done + 1;  // tcgen05 attention: the scores, then the output rows
+  uint64_t* o_done = s_done + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_done + 1);
   const int t = threadIdx.x, warp = t >> 5;
   const int h = blockIdx.x, tile = blockIdx.y;
   const int qb = blockIdx.z % a.q_blocks, bi = blockIdx.z / a.q_blocks;
   const int q0 = qb * 64;
-  constexpr uint32_t kCols = 64;
+  const uint32_t kCols = a.tc ? 512 : 64;
 
   if (t == 0) {
     mbar_init(w_full, 1);
     mbar_init(mma_done, 1);
+    mbar_init(s_done, 1);
+    mbar_init(o_done, 1);
     fence_mbar_init();
   }
   if (warp == 0) {
@@ -86,7 +357,10 @@ __global__ void __launch_bounds__(128 * G, 1) attention_o_kernel(const __grid_co
   const long long row0 = static_cast<long long>(bi) * a.at.Lq + q0;
   const TokenPrefetch pf = token_prefetch<kAoThreads>(a.ep, a.at.nq, nv, row0, tile);
 
-  attention_body<64, false, true, kAoBuf, G>(a.at, 0, q0, h, bi, smem + kAoOffAttn, smem + kAoOffO);
+  if (a.tc)
+    attention_head_tc<G>(a.at, q0, h, bi, smem + kAoOffAttn, smem + kAoOffO, tmem, s_done, o_done, a.status);
+  else
+    attention_body<64, false, true, kAoBuf, G>(a.at, 0, q0, h, bi, smem + kAoOffAttn, smem + kAoOffO);
   fence_async_smem();  // the O tile's generic-proxy stores, before the tensor core reads them
   __syncthreads();
   if (t == 0) {
@@ -153,6 +427,16 @@ EncodeFn encode_fn() {
 }
 
 bool aligned16(const void* p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; }
+
+// SO101_ATTN_O_TC=1 runs the attention of so101_attention_o on tcgen05 (read per call: the engine
+// calls it while it records its programs). Off by default: at the expert's 50 query rows the
+// attention is bound by loading the kv head's 291 keys and values (80 KB per CTA, 3 us), and the
+// tcgen05 form's two dependent MMA rounds and two softmax passes measured 0.1 ms per chunk slower
+// than the mma.sync flash loop.
+bool ao_tc_enabled() {
+  const char* e = std::getenv("SO101_ATTN_O_TC");
+  return e && e[0] == '1';
+}
 
 // Whether a cluster of `heads` CTAs of attention_o_kernel<G> can be resident at all (non-portable
 // sizes above 8 depend on the GPU); cached per group count and cluster size.
@@ -285,6 +569,9 @@ extern "C" int so101_attention_o(const void* q, int64_t ldq, const void* k, int6
   a.ep = TokenEpilogue{y, ldy, residual, ldr, static_cast<__nv_bfloat16*>(y16), ld16, y16_scale, stat_ss, stat_ld,
                        static_cast<int>(n_out)};
   a.q_blocks = static_cast<int>(q_blocks);
+  // (the tcgen05 path reads the own keys' rotary tables as float4 rows)
+  const bool tables16 = !k_own || (aligned16(k_cos) && aligned16(k_sin));
+  a.tc = (key_tiles <= kAoTcTiles && tables16 && ao_tc_enabled()) ? 1 : 0;
   a.status = status_ptr();
 
   cudaLaunchConfig_t lc = {};

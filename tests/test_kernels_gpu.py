@@ -359,11 +359,12 @@ def test_attention_own_rows_equal_rope_cache_then_attention(batch):
     assert torch.equal(got, want)
 
 
+@pytest.mark.parametrize("tc", ["0", "1"])
 @pytest.mark.parametrize(
     "kind,batch,n_out",
-    [("self", 1, 720), ("cross", 1, 720), ("self", 2, 720), ("prefix", 1, 960), ("cross", 1, 100)],
+    [("self", 1, 720), ("cross", 1, 720), ("self", 2, 720), ("prefix", 1, 960), ("cross", 1, 100), ("long", 1, 720)],
 )
-def test_attention_o_equals_attention_then_projection(kind, batch, n_out):
+def test_attention_o_equals_attention_then_projection(kind, batch, n_out, tc, monkeypatch):
     """so101_attention_o (attention, output projection and residual in one launch, the heads of
     each 128-feature tile summed across a cluster) against the float32 expression (fp32 softmax
     attention, fp32 projection): no further from it than twice the two-launch chain
@@ -372,10 +373,13 @@ def test_attention_o_equals_attention_then_projection(kind, batch, n_out):
     itself: bf16(y * w) exactly, per-tile sums of squares to fp32 rounding; a second call repeats
     the bits. The expert's self (own rows rotated on chip, causal onto its own rows) and cross
     attention at 50 rows, a batch of two, a 241-row prefix (4 query blocks) and a ragged
-    100-feature output."""
+    100-feature output, with the attention as the mma.sync flash loop and on tcgen05
+    (SO101_ATTN_O_TC=1); cross attention over 420 keys (more than the tcgen05 form's six key tiles)
+    always takes the flash loop."""
     from so101_smolvla_edge_b200.ops import attention, attention_o, rope_kv
 
-    L_, nq, nk, hd = 241, 15, 5, 64
+    monkeypatch.setenv("SO101_ATTN_O_TC", tc)
+    L_, nq, nk, hd = (420 if kind == "long" else 241), 15, 5, 64
     H = 241 if kind == "prefix" else 50
     qd = (nq + 2 * nk) * hd
     qkv = rnd(batch, H, qd, dtype=torch.bfloat16, scale=2.0)
@@ -386,7 +390,7 @@ def test_attention_o_equals_attention_then_projection(kind, batch, n_out):
         cos, sin = rope_tables(torch.arange(L_, L_ + H, device="cuda"), hd, 100000.0)
         kw = dict(cos=cos, sin=sin, causal_from=L_, q_offset=L_,
                   own=(qkv[:, :, nq * hd : (nq + nk) * hd], qkv[:, :, (nq + nk) * hd :], L_, cos, sin))
-    elif kind == "cross":
+    elif kind in ("cross", "long"):
         k = rnd(batch, L_, nk * hd, dtype=torch.bfloat16, seed=1)
         v = rnd(batch, L_, nk * hd, dtype=torch.bfloat16, seed=2)
         cos, sin = rope_tables(torch.arange(H, device="cuda"), hd, 100000.0)
