@@ -710,7 +710,7 @@ def case_fc2(g, reps: int) -> None:
 def case_expert_down64(g, reps: int) -> None:
     """so101_gemm: the batched expert's down projection at 64 observations (3200 rows, 2048 -> 720)
     with the residual epilogue that writes the next norm's bf16 operand and statistics, on the
-    persistent 192-wide plan the engine's autotune picks for it."""
+    192-wide CTA-pair plan the engine's autotune picks for it."""
     import torch
 
     from so101_smolvla_edge_b200.ops import linear
@@ -722,7 +722,7 @@ def case_expert_down64(g, reps: int) -> None:
     ss = torch.zeros(3200, 64, device="cuda")
     nw = torch.ones(720, device="cuda")
     for _ in range(reps):
-        linear(x, w, residual=e, out=e, stat=(ss, x16, nw), config=(0, 192, 1, 0, 2))
+        linear(x, w, residual=e, out=e, stat=(ss, x16, nw), config=(0, 192, 1, 0, 8))
 
 
 def case_gqa_prefix(g, reps: int) -> None:
