@@ -2,14 +2,14 @@
 // observations (the batched engine): head_dim 64, RoPE on the queries, the block-causal mask
 // `key j visible to query i  <=>  j < Lk and (j < causal_from or j <= i + q_offset)`.
 //
-// One CTA holds up to 256 query rows as two groups of 128 (MMA M = 128): either one query head's
-// positions [256 b, 256 b + 256) (the prefix: 241 rows per head), or the query heads of one kv
-// head stacked (the expert: 3 heads x 50 rows = 150), so that each key tile serves every query
-// head that reads it. Per 128-key tile j:
-//   warp 0 (one thread)  TMA: K_j and V_j of this observation's kv head into four-stage rings
+// The kernel is written for NG groups of 128 query rows per CTA (MMA M = 128); the plan runs one:
+// either one query head's positions [128 b, 128 b + 128) (the prefix: 241 rows per head in two
+// blocks), or the query heads of one kv head stacked (the expert: two of its three 50-row heads),
+// so that each key tile serves every query head that reads it. Per 128-key tile j:
+//   warp 0 (one thread)  TMA: K_j and V_j of this observation's kv head into two-stage rings
 //   warp 1 (one thread)  S_g = Q_g K_j^T (M 128, N 128, K 64) -> TMEM; O_g += P_g V_j with P_g
 //                        read from TMEM (the SigLIP kernel's scheme, attention_tc.cu)
-//   warps 2-9            first the queries: each thread loads its row, rotates it in fp32 (the
+//   warps 2-5            first the queries: each thread loads its row, rotates it in fp32 (the
 //                        reference's rope, rounded once to bf16) and writes it into the swizzled
 //                        Q operand tile; then the softmax of its row, one TMEM lane, with the mask
 //                        computed from the key index, and at the end O / l to the output rows.
@@ -43,9 +43,10 @@ constexpr int kGqTile = kGqRows * kGqHd * 2;  // 16 KB
 constexpr float kGqStaleMax = 8.f;
 constexpr int kGqBarBytes = 512;
 
-// NG query groups of 128 rows per CTA. Two (the prefix's 241-row heads): all 512 TMEM columns, a
-// four-stage K/V ring, one CTA per SM. One (the expert's 50-row heads, two per CTA): 256 columns
-// and a two-stage ring, two CTAs per SM, so the short, latency-bound CTAs overlap.
+// NG query groups of 128 rows per CTA. One: 256 TMEM columns and a two-stage ring, two CTAs per
+// SM, so the short, latency-bound CTAs overlap. (Two groups per CTA, all 512 columns, a four-stage
+// ring and one CTA per SM, measured 86.7 against 70.6 us for the prefix's attention at 64
+// observations, so the plan no longer picks them.)
 template <int NG>
 struct GqCfg {
   static constexpr int kStages = NG == 2 ? 4 : 2;
@@ -60,7 +61,7 @@ struct GqCfg {
   static constexpr uint32_t kColS = 0, kColP = NG * 128, kColO = NG * 128 + NG * 64;
 };
 static_assert((1 + 4 * 4 + 8) * 8 + 4 <= kGqBarBytes, "barrier region");
-static_assert(GqCfg<2>::kSmem <= 232448 && 2 * GqCfg<1>::kSmem <= 232448, "shared memory per CTA / SM");
+static_assert(2 * GqCfg<1>::kSmem <= 232448, "shared memory per CTA / SM");
 
 // Query row r of this CTA: its head and position, or false for a padding row. One head per CTA:
 // positions [rows qb, rows (qb + 1)); several: heads head0 .. head0 + n_heads - 1 stacked, Lq rows
@@ -418,7 +419,7 @@ struct GqPlan {
 GqPlan gqa_plan(long long Lq, int nq, int nkv) {
   GqPlan p;
   const int group = nq / nkv;
-  p.ng = Lq <= 64 ? 1 : 2;
+  p.ng = 1;
   const long long rows = static_cast<long long>(p.ng) * kGqRows;
   p.heads_per_cta = Lq <= rows ? static_cast<int>(rows / Lq) : 1;
   if (p.heads_per_cta > group) p.heads_per_cta = group;
@@ -457,14 +458,12 @@ int attention_gqa_tc_launch(const void* q, long long ldq, const void* k, long lo
   int rc = gq_map(&tk, k, k_rows * batch, static_cast<long long>(nkv) * 64, ldk);
   if (!rc) rc = gq_map(&tv, v, v_rows * batch, static_cast<long long>(nkv) * 64, ldv);
   if (rc) return rc;
-  static bool configured[2] = {false, false};
-  if (!configured[pl.ng - 1]) {
-    const cudaError_t e = pl.ng == 1 ? cudaFuncSetAttribute(attention_gqa_tc_kernel<1>,
-                                                            cudaFuncAttributeMaxDynamicSharedMemorySize, GqCfg<1>::kSmem)
-                                     : cudaFuncSetAttribute(attention_gqa_tc_kernel<2>,
-                                                            cudaFuncAttributeMaxDynamicSharedMemorySize, GqCfg<2>::kSmem);
+  static bool configured = false;
+  if (!configured) {
+    const cudaError_t e =
+        cudaFuncSetAttribute(attention_gqa_tc_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, GqCfg<1>::kSmem);
     if (e != cudaSuccess) return launch_error(e);
-    configured[pl.ng - 1] = true;
+    configured = true;
   }
   GqaArgs a;
   a.q = static_cast<const __nv_bfloat16*>(q);
@@ -489,9 +488,7 @@ int attention_gqa_tc_launch(const void* q, long long ldq, const void* k, long lo
   a.status = status_ptr();
   const dim3 grid(static_cast<unsigned>(pl.q_blocks * pl.head_groups), static_cast<unsigned>(nkv),
                   static_cast<unsigned>(batch));
-  if (pl.ng == 1)
-    return launch_kernel(attention_gqa_tc_kernel<1>, grid, dim3(GqCfg<1>::kThreads), GqCfg<1>::kSmem, stream, tk, tv, a);
-  return launch_kernel(attention_gqa_tc_kernel<2>, grid, dim3(GqCfg<2>::kThreads), GqCfg<2>::kSmem, stream, tk, tv, a);
+  return launch_kernel(attention_gqa_tc_kernel<1>, grid, dim3(GqCfg<1>::kThreads), GqCfg<1>::kSmem, stream, tk, tv, a);
 }
 
 }  // namespace so101
