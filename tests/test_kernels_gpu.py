@@ -127,6 +127,31 @@ def test_tiles_and_split_k_agree_and_repeat(swap, bn, split, flags):
     assert ok, err
 
 
+@pytest.mark.parametrize("m", [1, 7, 129])
+@pytest.mark.parametrize("n,k", [(8, 8), (24, 40), (136, 72), (200, 1000)])
+@pytest.mark.parametrize("plan", [None, (1, 16, 1, 0, 0), (1, 64, 2, 0, 1), (0, 64, 1, 0, 4), (0, 128, 1, 0, 2),
+                                  (0, 128, 1, 0, 8)])
+def test_gemm_edge_shapes(m, n, k, plan):
+    """Edge shapes beside the model's: a single token row, ragged rows, outputs narrower than one
+    tile, K of one 16-byte piece and K that ends inside a 64-wide block, on the default plan and on
+    every tile kind (swap, split over a cluster and through the workspace, one tile per CTA,
+    persistent, CTA pair). Results match the float32 product plus residual and repeat bit for bit;
+    plans a shape cannot take are refused, never run."""
+    from so101_smolvla_edge_b200.ops import linear
+
+    x = rnd(m, k, dtype=torch.bfloat16)
+    w = rnd(n, k, dtype=torch.bfloat16, scale=k**-0.5, seed=1)
+    r = rnd(m, n, seed=2)
+    try:
+        a = linear(x, w, residual=r, config=plan)
+    except ValueError:  # a plan this shape cannot take: refused on the host (SO101_ERR_ARG)
+        assert plan is not None
+        return
+    assert torch.equal(a, linear(x, w, residual=r, config=plan))
+    ok, err = close(a, gemm_ref(x, w, residual=r), torch.float32)
+    assert ok, err
+
+
 @pytest.mark.parametrize("swap,bn,split,flags", [(1, 64, 1, 0), (1, 64, 5, 0), (1, 64, 5, 1), (0, 128, 1, 0),
                                                  (0, 64, 3, 0), (0, 64, 3, 1), (0, 128, 1, 2)])
 def test_silu_gate_tiles(swap, bn, split, flags):
@@ -239,7 +264,8 @@ def visibility(lq, lk, causal_from, q_offset):
     return (j < causal_from) | (j <= i + q_offset)
 
 
-@pytest.mark.parametrize("case", ["prefix", "expert_self", "expert_cross", "small", "siglip", "odd"])
+@pytest.mark.parametrize("case", ["prefix", "expert_self", "expert_cross", "small", "siglip", "odd", "single",
+                                  "boundary"])
 def test_attention(case):
     """the prefix-LM mask over 241 tokens (192 image + 48 text bidirectional, the
     state token last), expert self attention (50 queries over 241 prefix + 50 causal keys),
@@ -261,6 +287,12 @@ def test_attention(case):
     elif case == "odd":  # key tiles that do not divide evenly over the split cluster, head_dim 128
         nq, nk, hd = 4, 1, 128
         lq, lk, pos, cf, qo = 37, 450, torch.arange(413, 450), 413, 413
+    elif case == "single":  # one query, one key
+        nq, nk = 1, 1
+        lq, lk, pos, cf, qo = 1, 1, torch.arange(1), 1, 0
+    elif case == "boundary":  # 64 queries over 65 keys, causal from the first: the second key tile holds one key
+        nq, nk = 3, 1
+        lq, lk, pos, cf, qo = 64, 65, torch.arange(1, 65), 0, 1
     else:
         nq, nk, hd, rope = 12, 12, 64, False
         lq, lk, pos, cf, qo = 1024, 1024, torch.arange(1024), 1024, 0
