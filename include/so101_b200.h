@@ -272,6 +272,14 @@ SO101_API int so101_linear_f32(const float* x, int64_t ldx, const float* w, int6
                      const float* bias2, float* y, int64_t ldy, int64_t M, int64_t N, int64_t K,
                      int act, cudaStream_t stream);
 
+/* x (M x K fp32, row stride ldx) -> y (M x 3K bf16, row stride ldy) = [bf16(x) | bf16(x) |
+ * bf16(x - bf16(x))]: with w3 = [W_hi | W_lo | W_hi] (W_hi = bf16(W), W_lo = bf16(W - W_hi)),
+ * so101_gemm(y, w3) is the fp32 linear x W^T to about 2^-16 relative on the tensor cores (the
+ * split's lo x lo term dropped). K a multiple of 4, x 16-byte and y 8-byte aligned. No reference
+ * counterpart: the engine's batched form of the fp32 linear of model/smolvla.py:285. */
+SO101_API int so101_split_bf16x3(const float* x, int64_t ldx, int64_t M, int64_t K, void* y, int64_t ldy,
+                                 cudaStream_t stream);
+
 /* The expert's output head and Euler step, per row m of e (M x K): x_t[m, :] += dt *
  * (rms_norm(e[m], norm_w) @ w_out^T + b_out). Replaces model/smolvla.py:308-309 and
  * engine.py:263-271 (x_t + dt * v_t). */

@@ -107,6 +107,7 @@ SIGNATURES = {
     "so101_patchify": [P, I, I, I, P, I, F, S],
     "so101_patch_embed": [P, I, I, P, I64, I64, P, P, I64, P, I64, S],
     "so101_linear_f32": [P, I64, P, I64, P, P, P, I64, I64, I64, I64, I, S],
+    "so101_split_bf16x3": [P, I64, I64, I64, P, I64, S],
     "so101_expert_out": [P, I64, P, F, P, P, P, I64, I64, I64, I64, F, S],
     "so101_prefix_tail": [P, I, P, P, P, I, P, P, I, I, P, I64, I64, I64, I, S],
     "so101_finish": [P, I, P, I, P, P, P, P, P, P, P, I, I, I, I, S],

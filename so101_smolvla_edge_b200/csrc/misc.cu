@@ -430,9 +430,47 @@ __global__ void patchify_kernel(const float* __restrict__ px, int n_img, int S, 
   }
 }
 
+// x (M x K fp32) -> y (M x 3K bf16) = [hi | hi | lo] with hi = bf16(x), lo = bf16(x - hi): the
+// operand of a bf16 GEMM against [W_hi | W_lo | W_hi] that sums x_hi W_hi + x_hi W_lo + x_lo W_hi
+// (the two-term split of each operand, its lo x lo product dropped): an fp32 linear on the tensor
+// cores to about 2^-16 relative. One thread per 4 columns.
+__global__ void split_bf16x3_kernel(const float* __restrict__ x, long long ldx, int M, int K,
+                                    __nv_bfloat16* __restrict__ y, long long ldy) {
+  grid_dep_launch();
+  grid_dep_wait();
+  const int q4 = K / 4;
+  const long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
+  if (i >= static_cast<long long>(M) * q4) return;
+  const long long m = i / q4;
+  const int c = static_cast<int>(i % q4) * 4;
+  const float4 v = *reinterpret_cast<const float4*>(x + m * ldx + c);
+  const __nv_bfloat162 h01 = __floats2bfloat162_rn(v.x, v.y), h23 = __floats2bfloat162_rn(v.z, v.w);
+  const float2 f01 = __bfloat1622float2(h01), f23 = __bfloat1622float2(h23);
+  const __nv_bfloat162 l01 = __floats2bfloat162_rn(v.x - f01.x, v.y - f01.y);
+  const __nv_bfloat162 l23 = __floats2bfloat162_rn(v.z - f23.x, v.w - f23.y);
+  uint2 hi, lo;
+  hi.x = *reinterpret_cast<const uint32_t*>(&h01), hi.y = *reinterpret_cast<const uint32_t*>(&h23);
+  lo.x = *reinterpret_cast<const uint32_t*>(&l01), lo.y = *reinterpret_cast<const uint32_t*>(&l23);
+  __nv_bfloat16* row = y + m * ldy + c;
+  *reinterpret_cast<uint2*>(row) = hi;
+  *reinterpret_cast<uint2*>(row + K) = hi;
+  *reinterpret_cast<uint2*>(row + 2 * K) = lo;
+}
+
 }  // namespace so101
 
 using namespace so101;
+
+extern "C" int so101_split_bf16x3(const float* x, int64_t ldx, int64_t M, int64_t K, void* y, int64_t ldy,
+                                  cudaStream_t stream) {
+  if (!x || !y || M <= 0 || K <= 0 || K % 4 || ldx < K || ldx % 4 || ldy < 3 * K || ldy % 4) return SO101_ERR_ARG;
+  if (reinterpret_cast<uintptr_t>(x) % 16 || reinterpret_cast<uintptr_t>(y) % 8 || M > 0x7fffffffLL || K > (1 << 24))
+    return SO101_ERR_ARG;
+  const long long blocks = (M * (K / 4) + 255) / 256;
+  if (blocks > 0x7fffffffLL) return SO101_ERR_ARG;
+  return launch_kernel(split_bf16x3_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, stream, x, ldx,
+                       static_cast<int>(M), static_cast<int>(K), static_cast<__nv_bfloat16*>(y), ldy);
+}
 
 extern "C" int so101_patchify(const float* px, int n_img, int S, int P, void* patches, int y_type, float y_qscale,
                               cudaStream_t stream) {

@@ -50,6 +50,11 @@ TUNE_MIN_ROWS = 1024  # token-tile candidates from this many rows on
 TUNE_SMALL = (None,) + tuple((1, bn, s, 0, 0) for bn in (32, 64) for s in (1, 2, 3, 4, 6, 8))
 TUNE_SMALL_ROWS = 256
 TUNE_MARGIN = 0.97  # a candidate replaces the pick only when at least 3% faster
+# From this many expert rows (observations x 50 actions) on, the action/time MLP's fp32 output
+# projection runs as one bf16 tensor-core GEMM over split operands (so101_split_bf16x3, about 2^-16
+# relative; the reference rounds its output to the run dtype right after: model/smolvla.py:285)
+# instead of the fp32 CUDA-core linear: 120 -> ~30 us per step at 64 observations.
+SPLIT_TIME_OUT_ROWS = 1024
 
 
 def unsupported(spec: ModelSpec) -> str | None:
@@ -361,6 +366,13 @@ class B200Path:
         self.tp_seam = z(s.exp_dim)
         self.px_seam = z(B * C_, 3, s.image_size, s.image_size)
         self.ss_e = z(B * H, STAT_SLOTS)  # per-row sums of squares of the expert residual stream
+        # the batched time MLP output: split activations and [W_hi | W_lo | W_hi]
+        self.split_out = B * H >= SPLIT_TIME_OUT_ROWS
+        if self.split_out:
+            wt = self.w["act.time_out.w"]
+            hi = wt.to(bf)
+            self.w3_time_out = torch.cat([hi, (wt - hi.float()).to(bf), hi], dim=1).contiguous()
+            self.h0_3 = z(B * H, 3 * s.exp_dim, dtype=bf)
 
     def _expert_step(self, mode: str) -> L.ExpertStep | None:
         """The persistent expert-step problem for one observation, or None (per-op launches).
@@ -673,14 +685,24 @@ class B200Path:
         p.add(f"s{k}.act_time_in", self.lib.so101_linear_f32, x_in.data_ptr(), s.max_action,
               w["act.ain.w"].data_ptr(), s.max_action, w["act.ain.b"].data_ptr(), tp.data_ptr(),
               self.h0.data_ptr(), s.exp_dim, M, s.exp_dim, s.max_action, 2)  # fmt: skip
-        p.add(f"s{k}.time_out", self.lib.so101_linear_f32, self.h0.data_ptr(), s.exp_dim,
-              w["act.time_out.w"].data_ptr(), s.exp_dim, w["act.time_out.b"].data_ptr(), None,
-              self.e.data_ptr(), s.exp_dim, M, s.exp_dim, s.exp_dim, 0)  # fmt: skip
         e = self.e
+        fold = self.fold and self.xs is None
+        slots = 0
+        if self.split_out and self.xs is None:
+            # fp32 linear on the tensor cores: [h_hi | h_hi | h_lo] [W_hi | W_lo | W_hi]^T + b, with
+            # the first layer's norm statistics and bf16 operand in the same epilogue
+            p.add(f"s{k}.time_split", self.lib.so101_split_bf16x3, self.h0.data_ptr(), s.exp_dim, M, s.exp_dim,
+                  self.h0_3.data_ptr(), 3 * s.exp_dim)  # fmt: skip
+            slots = self._gemm(p, f"s{k}.time_out", self.h0_3, self.w3_time_out, e, bias=w["act.time_out.b"],
+                               stat=(self.ss_e, self.h_e, w["exp.0.ln_in"]) if fold else None)  # fmt: skip
+        else:
+            p.add(f"s{k}.time_out", self.lib.so101_linear_f32, self.h0.data_ptr(), s.exp_dim,
+                  w["act.time_out.w"].data_ptr(), s.exp_dim, w["act.time_out.b"].data_ptr(), None,
+                  self.e.data_ptr(), s.exp_dim, M, s.exp_dim, s.exp_dim, 0)  # fmt: skip
+            if fold:
+                slots = self._stats(p, f"s{k}.stats", e, w["exp.0.ln_in"], self.h_e, self.ss_e)
         if self.xs is not None:
             p.add(f"s{k}.expert_layers", self.lib.so101_expert_step_run, C.byref(self.xs), keep=(self.xs,))
-        fold = self.fold and self.xs is None
-        slots = self._stats(p, f"s{k}.stats", e, w["exp.0.ln_in"], self.h_e, self.ss_e) if fold else 0
         for i in range(s.n_layers if self.xs is None else 0):
             pre = f"exp.{i}."
             if not fold:

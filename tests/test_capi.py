@@ -17,7 +17,7 @@ def lib():
 
 def test_library_loads_and_exports_every_header_symbol(lib):
     names = L.header_symbols()
-    assert len(names) == 30
+    assert len(names) == 31
     missing = [n for n in names if not hasattr(lib, n)]
     assert not missing, missing
     assert lib.so101_version().decode().endswith("sm_100a")

@@ -542,6 +542,33 @@ def test_linear_f32_tiles_agree_bit_for_bit(silu):
     assert torch.allclose(odd.double(), x[:1000, :32].double() @ w[:77, :32].double().T, rtol=1e-5, atol=1e-5)
 
 
+def test_split_bf16x3_linear_matches_fp32():
+    """The batched time MLP's output projection on the tensor cores: so101_split_bf16x3 writes
+    [hi | hi | lo] of the fp32 activations, one bf16 GEMM against [W_hi | W_lo | W_hi] sums the three
+    cross products in fp32; the result is the fp32 linear to about 2^-16 relative (the split's
+    lo x lo term and the bf16 rounding of each lo part), far inside the bf16 rounding the reference
+    applies to it next (model/smolvla.py:285)."""
+    from so101_smolvla_edge_b200 import _lib as L
+    from so101_smolvla_edge_b200.ops import linear
+
+    x = rnd(3200, 720)
+    w = rnd(720, 720, scale=720**-0.5, seed=1)
+    b = rnd(720, seed=2)
+    x3 = torch.empty(3200, 3 * 720, dtype=torch.bfloat16, device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+    L.check(L.lib().so101_split_bf16x3(x.data_ptr(), 720, 3200, 720, x3.data_ptr(), 3 * 720, stream), "split")
+    hi = x.to(torch.bfloat16)
+    assert torch.equal(x3[:, :720], hi) and torch.equal(x3[:, 720:1440], hi)
+    assert torch.equal(x3[:, 1440:], (x - hi.float()).to(torch.bfloat16))
+    wh = w.to(torch.bfloat16)
+    w3 = torch.cat([wh, (w - wh.float()).to(torch.bfloat16), wh], dim=1).contiguous()
+    got = linear(x3, w3, bias=b, out_dtype=torch.float32)
+    want = x.double() @ w.double().T + b.double()
+    assert (got.double() - want).abs().max() <= 2**-15 * want.abs().max()
+    # odd sizes are refused on the host: K not a multiple of 4
+    assert L.lib().so101_split_bf16x3(x.data_ptr(), 720, 3200, 718, x3.data_ptr(), 3 * 720, stream) == L.ERR_ARG
+
+
 # ------------------------------------------------------------------ RMSNorm finished in the GEMM
 def _rms_ref(x, w, eps):
     x = x.float()
