@@ -569,6 +569,26 @@ def test_split_bf16x3_linear_matches_fp32():
     assert L.lib().so101_split_bf16x3(x.data_ptr(), 720, 3200, 718, x3.data_ptr(), 3 * 720, stream) == L.ERR_ARG
 
 
+@pytest.mark.parametrize("rows", [50, 3200, 1037])
+def test_expert_out_head_and_euler_step(rows):
+    """so101_expert_out: x_t += dt * (rms_norm(e) @ w_out^T + b_out), one block per row, at one and
+    at 64 observations and a ragged count, within fp32 rounding of float64."""
+    from so101_smolvla_edge_b200 import _lib as L
+
+    K, N, eps, dt = 720, 32, 1e-6, -0.1
+    e = rnd(rows, K, scale=3.0)
+    nw = 1.0 + 0.1 * rnd(K, seed=1)
+    w = rnd(N, K, scale=K**-0.5, seed=2)
+    b = rnd(N, seed=3)
+    x = rnd(rows, N, seed=4)
+    want = x.double() + dt * (((e.double() * torch.rsqrt((e.double() ** 2).mean(-1, keepdim=True) + eps)) * nw.double())
+                              @ w.double().T + b.double())  # fmt: skip
+    stream = torch.cuda.current_stream().cuda_stream
+    L.check(L.lib().so101_expert_out(e.data_ptr(), K, nw.data_ptr(), eps, w.data_ptr(), b.data_ptr(), x.data_ptr(),
+                                     N, rows, N, K, dt, stream), "expert_out")  # fmt: skip
+    assert (x.double() - want).abs().max() <= 1e-5 * want.abs().max()
+
+
 # ------------------------------------------------------------------ RMSNorm finished in the GEMM
 def _rms_ref(x, w, eps):
     x = x.float()
