@@ -49,11 +49,14 @@ int attention_tc_launch(const void* q, long long ldq, const void* k, long long l
 bool attention_gqa_tc_eligible(const void* q, long long ldq, const void* k, long long ldk, const void* v,
                                long long ldv, const void* o, long long ldo, int o_type, long long Lq, long long Lk,
                                int nq, int nkv, int hd, const float* cos, long long bq, long long bk, long long bv,
-                               long long bo, int batch);
+                               long long bo, int batch, const void* k_own, const void* v_own, long long ld_own,
+                               long long b_own, long long own_from, const float* k_cos, const float* k_sin);
 int attention_gqa_tc_launch(const void* q, long long ldq, const void* k, long long ldk, const void* v, long long ldv,
                             void* o, long long ldo, long long Lq, long long Lk, int nq, int nkv,
                             long long causal_from, long long q_offset, const float* cos, const float* sin, int batch,
-                            long long bq, long long bk, long long bv, long long bo, cudaStream_t stream);
+                            long long bq, long long bk, long long bv, long long bo, const void* k_own,
+                            const void* v_own, long long ld_own, long long b_own, long long own_from,
+                            const float* k_cos, const float* k_sin, cudaStream_t stream);
 
 // The masked tcgen05 kernel for many observations; SO101_ATTN_GQA_TC=0 keeps the mma.sync kernel
 // (for comparisons).
@@ -107,11 +110,12 @@ int attention_impl(const void* q, int64_t ldq, const void* k, int64_t ldk, const
       attention_tc_eligible(q, ldq, k, ldk, v, ldv, Lq, Lk, nq, nkv, hd, causal_from, cos, bq, bk, bv, o_type) &&
       ldo % 8 == 0 && bo == Lq * ldo && reinterpret_cast<uintptr_t>(o) % 16 == 0)
     return attention_tc_launch(q, ldq, k, ldk, v, ldv, o, ldo, o_type, o_qscale, Lq, nq, batch, stream);
-  if (!own.k && gqa_tc_enabled() &&
+  if (gqa_tc_enabled() &&
       attention_gqa_tc_eligible(q, ldq, k, ldk, v, ldv, o, ldo, o_type, Lq, Lk, nq, nkv, hd, cos, bq, bk, bv, bo,
-                                batch))
+                                batch, own.k, own.v, own.ld, own.b, own.from, own.cos, own.sin))
     return attention_gqa_tc_launch(q, ldq, k, ldk, v, ldv, o, ldo, Lq, Lk, nq, nkv, causal_from, q_offset, cos, sin,
-                                   batch, bq, bk, bv, bo, stream);
+                                   batch, bq, bk, bv, bo, own.k, own.v, own.ld, own.b, own.from, own.cos, own.sin,
+                                   stream);
   AttnArgs a;
   a.q = static_cast<const __nv_bfloat16*>(q);
   a.k = static_cast<const __nv_bfloat16*>(k);

@@ -34,12 +34,22 @@ struct GqaArgs {
   const float* sin;
   float scale_log2;
   int* status;
+  // Keys j >= own_from (at most kGqOwn of them) are the step's own rows, read from k_own / v_own
+  // (row stride ld_own, observation stride b_own, kv head at columns 64 kvh) instead of the K / V
+  // maps, the keys rotated by k_cos / k_sin (row j - own_from) as the RoPE K/V cache kernel would;
+  // the cache rows there are never read. k_own == nullptr: own_from = Lk, none.
+  const __nv_bfloat16* k_own = nullptr;
+  const __nv_bfloat16* v_own = nullptr;
+  long long ld_own = 0, b_own = 0, own_from = 0;
+  const float* k_cos = nullptr;
+  const float* k_sin = nullptr;
 };
 
 constexpr int kGqRows = 128;
 constexpr int kGqKeys = 128;
 constexpr int kGqHd = 64;
 constexpr int kGqTile = kGqRows * kGqHd * 2;  // 16 KB
+constexpr int kGqOwn = 64;                     // most own keys: one 64-key tile (the expert's 50)
 constexpr float kGqStaleMax = 8.f;
 constexpr int kGqBarBytes = 512;
 
@@ -54,7 +64,9 @@ struct GqCfg {
   static constexpr int kOffQ = 0;
   static constexpr int kOffK = kOffQ + NG * kGqTile;
   static constexpr int kOffV = kOffK + kStages * kGqTile;
-  static constexpr int kOffBar = kOffV + kStages * kGqTile;
+  static constexpr int kOffOwnK = kOffV + kStages * kGqTile;  // the own keys, rotated (64 rows)
+  static constexpr int kOffOwnV = kOffOwnK + kGqOwn * 128;    // the own values
+  static constexpr int kOffBar = kOffOwnV + kGqOwn * 128;
   static constexpr int kSmem = kOffBar + kGqBarBytes + 1024;
   static constexpr uint32_t kCols = NG == 2 ? 512 : 256;
   // TMEM columns: S (128 per group), P (64 per group: 128 bf16 keys in pairs), O (64 per group)
@@ -62,6 +74,30 @@ struct GqCfg {
 };
 static_assert((1 + 4 * 4 + 8) * 8 + 4 <= kGqBarBytes, "barrier region");
 static_assert(2 * GqCfg<1>::kSmem <= 232448, "shared memory per CTA / SM");
+
+// Two 8-dim chunks of a bf16 row, u1 (dims 8c..8c+7) and u2 (their rotary partners 32 later),
+// rotated by cos / sin (8 floats each, 16-byte aligned): per-operation rounding, one rounding to
+// bf16, as the reference's rope and the RoPE K/V cache kernel.
+__device__ __forceinline__ void gq_rotate(const uint4& u1, const uint4& u2, const float* cs, const float* sn, uint4& o1,
+                                          uint4& o2) {
+  const float4 ca = __ldg(reinterpret_cast<const float4*>(cs)), cb = __ldg(reinterpret_cast<const float4*>(cs + 4));
+  const float4 sa = __ldg(reinterpret_cast<const float4*>(sn)), sb = __ldg(reinterpret_cast<const float4*>(sn + 4));
+  const float cv[8] = {ca.x, ca.y, ca.z, ca.w, cb.x, cb.y, cb.z, cb.w};
+  const float sv[8] = {sa.x, sa.y, sa.z, sa.w, sb.x, sb.y, sb.z, sb.w};
+  const __nv_bfloat162* h1 = reinterpret_cast<const __nv_bfloat162*>(&u1);
+  const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&u2);
+  __nv_bfloat162* p1 = reinterpret_cast<__nv_bfloat162*>(&o1);
+  __nv_bfloat162* p2 = reinterpret_cast<__nv_bfloat162*>(&o2);
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const float2 x1 = __bfloat1622float2(h1[e]), x2 = __bfloat1622float2(h2[e]);
+    const float c0 = cv[2 * e], c1 = cv[2 * e + 1], s0 = sv[2 * e], s1 = sv[2 * e + 1];
+    p1[e] = __floats2bfloat162_rn(__fsub_rn(__fmul_rn(x1.x, c0), __fmul_rn(x2.x, s0)),
+                                  __fsub_rn(__fmul_rn(x1.y, c1), __fmul_rn(x2.y, s1)));
+    p2[e] = __floats2bfloat162_rn(__fadd_rn(__fmul_rn(x2.x, c0), __fmul_rn(x1.x, s0)),
+                                  __fadd_rn(__fmul_rn(x2.y, c1), __fmul_rn(x1.y, s1)));
+  }
+}
 
 // Query row r of this CTA: its head and position, or false for a padding row. One head per CTA:
 // positions [rows qb, rows (qb + 1)); several: heads head0 .. head0 + n_heads - 1 stacked, Lq rows
@@ -113,7 +149,14 @@ __global__ void __launch_bounds__(GqCfg<NG>::kThreads, NG == 1 ? 2 : 1)
   long long last_key = a.causal_from - 1;
   if (last_pos + a.q_offset > last_key) last_key = last_pos + a.q_offset;
   if (last_key > a.Lk - 1) last_key = a.Lk - 1;
-  const int n_tiles = static_cast<int>(last_key / kGqKeys) + 1;
+  // 128-key tiles of cache keys [0, min(last_key + 1, own_from)) through the TMA rings, then (with
+  // own rows this CTA can see) one 64-key tile of the own keys from shared memory
+  const bool own = a.k_own != nullptr;
+  const long long own_from = own ? a.own_from : a.Lk;
+  const long long cache_end = last_key + 1 < own_from ? last_key + 1 : own_from;
+  const int n_cache = static_cast<int>((cache_end + kGqKeys - 1) / kGqKeys);
+  const bool own_tile = own && last_key >= own_from;
+  const int n_tiles = n_cache + (own_tile ? 1 : 0);
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 4 * NG);
@@ -149,7 +192,7 @@ __global__ void __launch_bounds__(GqCfg<NG>::kThreads, NG == 1 ? 2 : 1)
       const uint64_t keep = policy_evict_normal();
       const int x = kvh * kGqHd;
       const int yk = static_cast<int>(obs * a.k_rows), yv = static_cast<int>(obs * a.v_rows);
-      for (int j = 0; j < n_tiles; ++j) {
+      for (int j = 0; j < n_cache; ++j) {
         const int st = j % kGqStages;
         const uint32_t back = static_cast<uint32_t>(j / kGqStages - 1) & 1u;
         if (j >= kGqStages && !mbar_wait(&k_empty[st], back, a.status)) break;
@@ -164,25 +207,31 @@ __global__ void __launch_bounds__(GqCfg<NG>::kThreads, NG == 1 ? 2 : 1)
     if (lane == 0) {
       constexpr uint32_t ID_S = idesc_attn(kGqKeys, 0);
       constexpr uint32_t ID_O = idesc_attn(kGqHd, 1);
+      constexpr uint32_t ID_S_OWN = idesc_attn(kGqOwn, 0);
+      // tile j: a cache tile from the K ring (N 128), or the own tile (j == n_cache: N 64, staged
+      // with the queries, so no ring barrier)
       auto issue_s = [&](int j, int g) {
         const uint64_t qd = sw128_desc(smem_u32(smem + kGqOffQ + g * kGqTile));
-        const uint64_t kd = sw128_desc(smem_u32(smem + kGqOffK + (j % kGqStages) * kGqTile));
+        const bool mine = j == n_cache;
+        const uint64_t kd = sw128_desc(smem_u32(smem + (mine ? Cfg::kOffOwnK : kGqOffK + (j % kGqStages) * kGqTile)));
 #pragma unroll
         for (int k = 0; k < kGqHd / 16; ++k)
-          mma_f16(tmem + kGqColS + g * kGqKeys, qd + 2 * k, kd + 2 * k, ID_S, k > 0 ? 1u : 0u);
+          mma_f16(tmem + kGqColS + g * kGqKeys, qd + 2 * k, kd + 2 * k, mine ? ID_S_OWN : ID_S, k > 0 ? 1u : 0u);
         mma_commit(&s_full[g]);
       };
-      bool ok = mbar_wait(q_full, 0, a.status) && mbar_wait(&k_full[0], 0, a.status);
+      bool ok = mbar_wait(q_full, 0, a.status) && (n_cache == 0 || mbar_wait(&k_full[0], 0, a.status));
       if (ok) {
         tc_fence_after();
         for (int g = 0; g < NG; ++g) issue_s(0, g);
-        mma_commit(&k_empty[0]);
+        if (n_cache > 0) mma_commit(&k_empty[0]);
       }
       for (int j = 0; j < n_tiles && ok; ++j) {
         const int st = j % kGqStages;
+        const bool mine = j == n_cache;
         if (j + 1 < n_tiles) {
           const int sn = (j + 1) % kGqStages;
-          ok = mbar_wait(&k_full[sn], static_cast<uint32_t>((j + 1) / kGqStages) & 1u, a.status);
+          const bool next_mine = j + 1 == n_cache;
+          if (!next_mine) ok = mbar_wait(&k_full[sn], static_cast<uint32_t>((j + 1) / kGqStages) & 1u, a.status);
           for (int g = 0; g < NG && ok; ++g) {
             ok = mbar_wait(&s_free[g], j & 1u, a.status);
             if (ok) {
@@ -191,21 +240,21 @@ __global__ void __launch_bounds__(GqCfg<NG>::kThreads, NG == 1 ? 2 : 1)
             }
           }
           if (!ok) break;
-          mma_commit(&k_empty[sn]);
+          if (!next_mine) mma_commit(&k_empty[sn]);
         }
-        if (!mbar_wait(&v_full[st], static_cast<uint32_t>(j / kGqStages) & 1u, a.status)) break;
-        const uint64_t vd = sw128_desc(smem_u32(smem + kGqOffV + st * kGqTile));
+        if (!mine && !mbar_wait(&v_full[st], static_cast<uint32_t>(j / kGqStages) & 1u, a.status)) break;
+        const uint64_t vd = sw128_desc(smem_u32(smem + (mine ? Cfg::kOffOwnV : kGqOffV + st * kGqTile)));
+        const int ksteps = (mine ? kGqOwn : kGqKeys) / 16;
         for (int g = 0; g < NG && ok; ++g) {
           ok = mbar_wait(&p_full[g], j & 1u, a.status);
           if (!ok) break;
           tc_fence_after();
-#pragma unroll
-          for (int k = 0; k < kGqKeys / 16; ++k)
+          for (int k = 0; k < ksteps; ++k)
             mma_f16_ta(tmem + kGqColO + g * kGqHd, tmem + kGqColP + g * (kGqKeys / 2) + 8 * k,
                        vd + static_cast<uint64_t>(k) * (2048 >> 4), ID_O, (j > 0 || k > 0) ? 1u : 0u);
           mma_commit(&o_full[g]);
         }
-        mma_commit(&v_empty[st]);
+        if (!mine) mma_commit(&v_empty[st]);
       }
     }
   } else {
@@ -213,6 +262,46 @@ __global__ void __launch_bounds__(GqCfg<NG>::kThreads, NG == 1 ? 2 : 1)
     const int g = (warp - 2) >> 2;
     const int quad = warp & 3;
     const int rl = quad * 32 + lane;  // TMEM lane = row within the group
+    // the own keys (rotated) and values into their 64-row tiles, in the rings' layout, by the
+    // softmax threads of group 0 (two key and four value pieces each, every load in flight
+    // together); rows past the own rows zero (their probabilities are zero, and zero values keep
+    // P V finite)
+    auto stage_own = [&]() {
+      if (g != 0) return;
+      const int n_own = static_cast<int>(a.Lk - own_from);
+      const __nv_bfloat16* ko = a.k_own + obs * a.b_own + static_cast<long long>(kvh) * kGqHd;
+      const __nv_bfloat16* vo = a.v_own + obs * a.b_own + static_cast<long long>(kvh) * kGqHd;
+      uint8_t* okt = smem + Cfg::kOffOwnK;
+      uint8_t* ovt = smem + Cfg::kOffOwnV;
+      static_assert(kGqOwn * 4 == 2 * 128 && kGqOwn * 8 == 4 * 128, "pieces per thread");
+      uint4 kv[2][2], vv[4];
+#pragma unroll
+      for (int it = 0; it < 2; ++it) {  // keys: row r, chunks c and c + 4
+        const int idx = rl + 128 * it, r = idx >> 2, c = idx & 3;
+        const uint4* kr = reinterpret_cast<const uint4*>(ko + static_cast<long long>(r < n_own ? r : 0) * a.ld_own);
+        kv[it][0] = r < n_own ? __ldg(kr + c) : make_uint4(0u, 0u, 0u, 0u);
+        kv[it][1] = r < n_own ? __ldg(kr + c + 4) : make_uint4(0u, 0u, 0u, 0u);
+      }
+#pragma unroll
+      for (int it = 0; it < 4; ++it) {  // values: row r, chunk c
+        const int idx = rl + 128 * it, r = idx >> 3, c = idx & 7;
+        vv[it] = r < n_own ? __ldg(reinterpret_cast<const uint4*>(vo + static_cast<long long>(r) * a.ld_own) + c)
+                           : make_uint4(0u, 0u, 0u, 0u);
+      }
+#pragma unroll
+      for (int it = 0; it < 2; ++it) {
+        const int idx = rl + 128 * it, r = idx >> 2, c = idx & 3;
+        uint4 o1 = make_uint4(0u, 0u, 0u, 0u), o2 = o1;
+        if (r < n_own) gq_rotate(kv[it][0], kv[it][1], a.k_cos + r * 32 + 8 * c, a.k_sin + r * 32 + 8 * c, o1, o2);
+        *reinterpret_cast<uint4*>(okt + r * 128 + ((c ^ (r & 7)) << 4)) = o1;
+        *reinterpret_cast<uint4*>(okt + r * 128 + (((c + 4) ^ (r & 7)) << 4)) = o2;
+      }
+#pragma unroll
+      for (int it = 0; it < 4; ++it) {
+        const int idx = rl + 128 * it, r = idx >> 3, c = idx & 7;
+        *reinterpret_cast<uint4*>(ovt + r * 128 + ((c ^ (r & 7)) << 4)) = vv[it];
+      }
+    };
     const int r = g * kGqRows + rl;
     int head = 0, pos = 0;
     const bool live = gqa_row<NG>(a, r, head0, n_heads, qb, head, pos);
@@ -261,6 +350,7 @@ __global__ void __launch_bounds__(GqCfg<NG>::kThreads, NG == 1 ? 2 : 1)
       }
 #pragma unroll
       for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(qt + ((c ^ (rl & 7)) << 4)) = out[c];
+      if (own_tile) stage_own();
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       __syncwarp();
       if (lane == 0) mbar_arrive(q_full);
@@ -275,6 +365,9 @@ __global__ void __launch_bounds__(GqCfg<NG>::kThreads, NG == 1 ? 2 : 1)
     long long vis_end = live ? pos + a.q_offset + 1 : 1;
     if (vis_end < a.causal_from) vis_end = a.causal_from;
     if (vis_end > a.Lk) vis_end = a.Lk;
+    // visible keys of the cache tiles (below own_from) and of the own tile
+    const int vis_cache = static_cast<int>(vis_end < own_from ? vis_end : own_from);
+    const int vis_own = static_cast<int>(min(max(vis_end - own_from, 0LL), static_cast<long long>(kGqKeys)));
     float m = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < n_tiles && ok; ++j) {
@@ -290,9 +383,9 @@ __global__ void __launch_bounds__(GqCfg<NG>::kThreads, NG == 1 ? 2 : 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&s_free[g]);
-      // mask: keys at or past vis_end get -inf
-      const int nvis = static_cast<int>(min(max(vis_end - static_cast<long long>(j) * kGqKeys, 0LL),
-                                            static_cast<long long>(kGqKeys)));
+      // mask: keys at or past vis_end get -inf, and in a cache tile the cache rows of the own keys
+      // (the own tile's column e is key own_from + e)
+      const int nvis = j == n_cache ? vis_own : min(max(vis_cache - j * kGqKeys, 0), kGqKeys);
       if (nvis < kGqKeys) {
 #pragma unroll
         for (int e = 0; e < kGqKeys; ++e)
@@ -434,8 +527,15 @@ GqPlan gqa_plan(long long Lq, int nq, int nkv) {
 bool attention_gqa_tc_eligible(const void* q, long long ldq, const void* k, long long ldk, const void* v,
                                long long ldv, const void* o, long long ldo, int o_type, long long Lq, long long Lk,
                                int nq, int nkv, int hd, const float* cos, long long bq, long long bk, long long bv,
-                               long long bo, int batch) {
+                               long long bo, int batch, const void* k_own, const void* v_own, long long ld_own,
+                               long long b_own, long long own_from, const float* k_cos, const float* k_sin) {
   if (hd != 64 || o_type != SO101_BF16 || nq % nkv || Lq < 1 || Lk < 1) return false;
+  if (k_own) {  // own rows: at most one 64-key tile, rows and rotary tables read in 16-byte pieces
+    const auto a16 = [](const void* p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; };
+    if (!v_own || !k_cos || !k_sin || own_from < 0 || own_from > Lk || Lk - own_from > kGqOwn) return false;
+    if (!a16(k_own) || !a16(v_own) || !a16(k_cos) || !a16(k_sin) || (ld_own * 2) % 16 || (b_own * 2) % 16)
+      return false;
+  }
   if (bk % ldk || bv % ldv || bk / ldk < Lk || bv / ldv < Lk || (batch > 1 && (bq < Lq * ldq || bo < Lq * ldo)))
     return false;
   const auto al = [](const void* p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; };
@@ -451,7 +551,9 @@ bool attention_gqa_tc_eligible(const void* q, long long ldq, const void* k, long
 int attention_gqa_tc_launch(const void* q, long long ldq, const void* k, long long ldk, const void* v, long long ldv,
                             void* o, long long ldo, long long Lq, long long Lk, int nq, int nkv,
                             long long causal_from, long long q_offset, const float* cos, const float* sin, int batch,
-                            long long bq, long long bk, long long bv, long long bo, cudaStream_t stream) {
+                            long long bq, long long bk, long long bv, long long bo, const void* k_own,
+                            const void* v_own, long long ld_own, long long b_own, long long own_from,
+                            const float* k_cos, const float* k_sin, cudaStream_t stream) {
   const GqPlan pl = gqa_plan(Lq, nq, nkv);
   CUtensorMap tk, tv;
   const long long k_rows = bk / ldk, v_rows = bv / ldv;
@@ -486,6 +588,13 @@ int attention_gqa_tc_launch(const void* q, long long ldq, const void* k, long lo
   a.sin = sin;
   a.scale_log2 = static_cast<float>(1.4426950408889634 / 8.0);
   a.status = status_ptr();
+  a.k_own = static_cast<const __nv_bfloat16*>(k_own);
+  a.v_own = static_cast<const __nv_bfloat16*>(v_own);
+  a.ld_own = ld_own;
+  a.b_own = b_own;
+  a.own_from = k_own ? own_from : Lk;
+  a.k_cos = k_cos;
+  a.k_sin = k_sin;
   const dim3 grid(static_cast<unsigned>(pl.q_blocks * pl.head_groups), static_cast<unsigned>(nkv),
                   static_cast<unsigned>(batch));
   return launch_kernel(attention_gqa_tc_kernel<1>, grid, dim3(GqCfg<1>::kThreads), GqCfg<1>::kSmem, stream, tk, tv, a);

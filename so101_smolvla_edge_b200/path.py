@@ -238,8 +238,8 @@ class B200Path:
         self.attn_o_layers = {i for i in range(s.n_layers)
                               if ok and (mode == "all" or (mode == "cross" and not s.is_self_attn(i)))}  # fmt: skip
         # many observations: the masked tcgen05 attention (attention_gqa_tc.cu) serves the expert too;
-        # it reads the step's own keys from the cache, so a rope_kv launch writes them there first
-        # (few observations: the mma.sync kernel rotates them on chip)
+        # both it and the mma.sync kernel (few observations) read the step's own keys and values from
+        # the fused qkv rows and rotate the keys on chip (no rope_kv launch into the cache)
         self.gqa_tc = (s.head_dim == 64 and self.B * s.n_kv >= 64
                        and os.environ.get("SO101_ATTN_GQA_TC", "1") != "0")  # fmt: skip
         self.ws = workspace(device)  # split-K partials and tickets exist before any capture
@@ -712,7 +712,7 @@ class B200Path:
                 self._gemm(p, f"s{k}.{i}.qkv", self.h_e, w[pre + "qkv"], self.qkv_e, rms=rms)
                 bk = (L_ + H) * kv
                 own = None
-                if hd == 64 and not self.gqa_tc:  # the step's own keys and values from the qkv rows
+                if hd == 64 and (H <= 64 or not self.gqa_tc):  # the step's own keys and values from the qkv rows
                     k_own = self.qkv_e.data_ptr() + nq * hd * 2
                     own = (k_own, k_own + nk * hd * 2, qd, H * qd, L_, w["cos_s"], w["sin_s"])
                 else:  # RoPE and the K/V cache rows in a separate launch

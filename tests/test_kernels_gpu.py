@@ -367,13 +367,14 @@ def test_attention_gqa_batched(case):
     assert torch.equal(got, attention(q, k, v, nq, nkv, cos=cos, sin=sin, causal_from=cf, q_offset=qo))
 
 
-@pytest.mark.parametrize("batch", [1, 8])
+@pytest.mark.parametrize("batch", [1, 8, 64])
 def test_attention_own_rows_equal_rope_cache_then_attention(batch):
     """so101_attention_rows (the step's own keys and values read from the fused qkv rows, the keys
-    rotated on chip) gives the same bits as rope_kv writing them into the K/V cache followed by
-    attention over the cache: the action expert's self-attention, at batches that stay on the
-    mma.sync kernel (from 13 observations the cache path takes the tcgen05 kernel). The cache's own
-    rows hold unrelated values for the fused call, so they are shown not to be read."""
+    rotated on chip) against rope_kv writing them into the K/V cache followed by attention over the
+    cache: the action expert's self-attention. On the mma.sync kernel (up to 12 observations) the
+    bits are the same; on the tcgen05 kernel (from 13) the own keys form their own 64-key tile, so
+    the key tiles and the order of the P V sums differ, and the two agree to bf16 rounding. The
+    cache's own rows hold unrelated values for the fused call, so they are shown not to be read."""
     from so101_smolvla_edge_b200.ops import attention, rope_kv
 
     L_, H, nq, nk, hd = 241, 50, 15, 5, 64
@@ -388,7 +389,11 @@ def test_attention_own_rows_equal_rope_cache_then_attention(batch):
     for b in range(batch):
         rope_kv(qkv[b], nq, nk, cos, sin, cache_k[b, L_:], cache_v[b, L_:])
     want = attention(q, cache_k, cache_v, nq, nk, cos=cos, sin=sin, causal_from=L_, q_offset=L_)
-    assert torch.equal(got, want)
+    if batch <= 12:
+        assert torch.equal(got, want)
+    else:
+        err = (got.float() - want.float()).abs()
+        assert err.max() <= 2**-7 * want.float().abs().max() and err.mean() <= 2**-9 * want.float().abs().mean()
 
 
 @pytest.mark.parametrize("tc", ["0", "1"])
