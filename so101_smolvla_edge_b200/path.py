@@ -50,6 +50,7 @@ TUNE_MIN_ROWS = 1024  # token-tile candidates from this many rows on
 TUNE_SMALL = (None,) + tuple((1, bn, s, 0, 0) for bn in (32, 64) for s in (1, 2, 3, 4, 6, 8))
 TUNE_SMALL_ROWS = 256
 TUNE_MARGIN = 0.97  # a candidate replaces the pick only when at least 3% faster
+TUNE_MARGIN_STAGE = 0.998  # in a stage's chain: at least 0.2% of the stage faster
 # From this many expert rows (observations x 50 actions) on, the action/time MLP's fp32 output
 # projection runs as one bf16 tensor-core GEMM over split operands (so101_split_bf16x3, about 2^-16
 # relative; the reference rounds its output to the run dtype right after: model/smolvla.py:285)
@@ -302,8 +303,56 @@ class B200Path:
             self.tuned[key] = best
             report[what] = {"plan": best, "ms": {str(c): t for c, t in times.items()}}
         torch.cuda.synchronize(self.dev)
+        self._refine_small(report)
         self._build_all()
         return report
+
+    def _refine_small(self, report: dict[str, dict], runs: int = 3) -> None:
+        """The few-row GEMMs (the expert and the prefix at one observation) once more, each
+        candidate timed inside its stage's own launch chain rather than alone: there a kernel's
+        prologue overlaps its predecessor's tail, which decides among these microsecond GEMMs.
+        Coordinate descent, one site at a time, keeping the others' current plans; the stage runs
+        eagerly on the engine's buffers (whatever they hold: the next chunk recomputes them)."""
+        stream = torch.cuda.current_stream(self.dev)
+
+        def stage_ms(build) -> float:
+            prog = Program("refine")
+            build(prog)
+            prog.run(stream.cuda_stream)  # warm
+            best = float("inf")
+            for _ in range(runs):
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                prog.run(stream.cuda_stream)
+                e1.record(stream)
+                e1.synchronize()
+                best = min(best, e0.elapsed_time(e1))
+            return best
+
+        for build, name in ((self._build_denoise, "denoise"), (self._build_prefix, "prefix")):
+            names = {c[0] for c in self.progs[name].calls}
+            keys = [k for k, (what, _) in self._sites.items()
+                    if k[1] <= TUNE_SMALL_ROWS and k[0] == L.BF16 and what in names]  # fmt: skip
+            for key in keys:
+                what = self._sites[key][0]
+                keep = self.tuned.get(key)
+                times: dict[tuple | None, float] = {}
+                for cand in TUNE_SMALL:
+                    self.tuned[key] = cand
+                    try:
+                        times[cand] = stage_ms(build)
+                    except (ValueError, RuntimeError):  # a plan this GEMM cannot take
+                        continue
+                if not times:
+                    self.tuned[key] = keep
+                    continue
+                best = min(times, key=times.get)
+                if keep in times and times[best] > TUNE_MARGIN_STAGE * times[keep]:
+                    best = keep  # within noise of the alone-timed pick
+                self.tuned[key] = best
+                if what in report:
+                    report[what]["plan"] = best
+                    report[what]["stage_ms"] = {str(c): t for c, t in times.items()}
 
     # ------------------------------------------------------------------ weights and buffers
     def _upload(self, b: Bundle) -> None:
