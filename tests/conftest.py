@@ -84,7 +84,7 @@ INT8_FP32_DRIFT = 1.5  # no further from float32 than 1.5x the reference's own i
 
 def int8_band_check(g, acts) -> dict:
     """configs[0] W8A8 parity over the golden seeds: acts (>= seeds, 50, 12) against the reference's
-    int8 chunks, judged against the reference's own one-ulp reproducibility band."""
+    int8 chunks, checked against the reference's own one-ulp reproducibility band."""
     ref, fp, ulp = g["actions_int8"], g["actions_fp32"], g["actions_int8_ulp"]
     n = ref.shape[0]
     band_max = float(np.abs(ulp - ref[None]).max())
