@@ -145,7 +145,33 @@ class _StubLib:
             self.calls.append((name, args))
             return 0
 
+        fn.__name__ = name
         return fn
+
+
+def test_batched_denoise_launches_on_a_stub_library():
+    """The denoising step's launch structure, built against a stub library on the CPU: from 1024
+    expert rows on, the time MLP's output projection is so101_split_bf16x3 followed by one
+    so101_gemm (with the first layer's norm statistics), not so101_linear_f32; self-attention layers
+    read the step's own keys and values from the qkv rows (so101_attention_rows) with no rope_kv
+    launch into the cache; at one observation the fp32 linear stays."""
+    import torch
+    from conftest import case_bundle
+
+    from so101_smolvla_edge_b200.path import B200Path
+
+    b = case_bundle("small64_absolute")
+    s = b.spec
+    many = B200Path(b, torch.device("cpu"), batch=-(-1024 // s.chunk), lib=_StubLib())
+    fns = {what: fn.__name__ for what, fn, _ in many.progs["denoise"].calls}
+    assert fns["s0.time_split"] == "so101_split_bf16x3" and fns["s0.time_out"] == "so101_gemm"
+    assert many.w3_time_out.shape == (s.exp_dim, 3 * s.exp_dim)
+    selfs = [i for i in range(s.n_layers) if s.is_self_attn(i)]
+    assert selfs and all(fns[f"s0.{i}.attn"] == "so101_attention_rows" for i in selfs)
+    assert not any(".rope_kv" in what for what in fns if what.startswith("s"))
+    one = B200Path(b, torch.device("cpu"), lib=_StubLib())
+    fns1 = {what: fn.__name__ for what, fn, _ in one.progs["denoise"].calls}
+    assert fns1["s0.time_out"] == "so101_linear_f32" and "s0.time_split" not in fns1
 
 
 def test_backend_seams_on_a_stub_library():
