@@ -5,7 +5,7 @@
 // tile j:
 //   warp 0 (one thread)  TMA: Q once, then K_j and V_j into separate four-stage rings (a K stage
 //                        frees as soon as S_j is computed, so keys stream several tiles ahead)
-//   warp 1 (one thread)  S_g = Q_g K_j^T  (M 128, N 128, K 64)       -> TMEM S_g
+//   warp 1 (elected lane) S_g = Q_g K_j^T  (M 128, N 128, K 64)      -> TMEM S_g
 //                        O_g += P_g V_j   (M 128, N 64,  K 128 keys) -> TMEM O_g, A operand P_g
 //                                                                       read from TMEM
 //   warps 2-5 / 6-9      softmax for group A / B, one thread per query row (its TMEM lane): the
@@ -159,10 +159,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       }
     }
   } else if (warp <= kIssuers) {
-    // MMA issue: one thread per issuing warp, for groups [g_lo, g_hi). An issuing thread stalls
-    // while the tensor pipe drains its MMAs; with one issuer per group (kIssuers = 2) the other
-    // group's barrier waits and issues proceed meanwhile.
-    if (lane == 0) {
+    // MMA issue: the whole issuing warp runs the waits, its elected lane issues the MMAs and
+    // commits, for groups [g_lo, g_hi). An issuing thread stalls while the tensor pipe takes its
+    // MMAs; with one issuer per group (kIssuers = 2) the other group's barrier waits and issues
+    // proceed meanwhile. A wait's outcome is made warp-uniform (a timeout in any lane ends the loop).
+    {
       constexpr uint32_t ID_S = idesc_attn(kTcKeys, 0);
       constexpr uint32_t ID_O = idesc_attn(kTcHd, 1);
       const int g_lo = kIssuers == 2 ? warp - 1 : 0, g_hi = kIssuers == 2 ? warp : 2;
@@ -170,45 +171,52 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       auto issue_s = [&](int j, int g) {
         const uint64_t qd = sw128_desc(smem_u32(smem + kOffQ + g * kTcTile));
         const uint64_t kd = sw128_desc(smem_u32(smem + kOffK + (j % kStages) * kTcTile));
+        if (elect_one()) {
 #pragma unroll
-        for (int k = 0; k < kTcHd / 16; ++k)
-          mma_f16(tmem + kColS + g * kTcKeys, qd + 2 * k, kd + 2 * k, ID_S, k > 0 ? 1u : 0u);
-        mma_commit(&s_full[g]);
+          for (int k = 0; k < kTcHd / 16; ++k)
+            mma_f16(tmem + kColS + g * kTcKeys, qd + 2 * k, kd + 2 * k, ID_S, k > 0 ? 1u : 0u);
+          mma_commit(&s_full[g]);
+        }
       };
-      bool ok = mbar_wait(q_full, 0, a.status) && mbar_wait(&k_full[0], 0, a.status);
+      auto wait = [&](uint64_t* bar, uint32_t parity) {
+        return __all_sync(0xffffffffu, mbar_wait(bar, parity, a.status));
+      };
+      bool ok = wait(q_full, 0) && wait(&k_full[0], 0);
       if (ok) {
         tc_fence_after();
         for (int g = g_lo; g < g_hi; ++g) issue_s(0, g);
-        mma_commit(&k_empty[0]);  // the K stage is free once every issuer's S MMAs read it
+        if (elect_one()) mma_commit(&k_empty[0]);  // the K stage is free once every issuer's S MMAs read it
       }
       for (int j = 0; j < n_tiles && ok; ++j) {
         const int st = j % kStages;
         if (j + 1 < n_tiles) {
           const int sn = (j + 1) % kStages;
-          ok = mbar_wait(&k_full[sn], static_cast<uint32_t>((j + 1) / kStages) & 1u, a.status);
+          ok = wait(&k_full[sn], static_cast<uint32_t>((j + 1) / kStages) & 1u);
           for (int g = g_lo; g < g_hi && ok; ++g) {
-            ok = mbar_wait(&s_free[g], j & 1u, a.status);
+            ok = wait(&s_free[g], j & 1u);
             if (ok) {
               tc_fence_after();
               issue_s(j + 1, g);
             }
           }
           if (!ok) break;
-          mma_commit(&k_empty[sn]);
+          if (elect_one()) mma_commit(&k_empty[sn]);
         }
-        if (!mbar_wait(&v_full[st], static_cast<uint32_t>(j / kStages) & 1u, a.status)) break;
+        if (!wait(&v_full[st], static_cast<uint32_t>(j / kStages) & 1u)) break;
         const uint64_t vd = sw128_desc(smem_u32(smem + kOffV + st * kTcTile));
         for (int g = g_lo; g < g_hi && ok; ++g) {
-          ok = mbar_wait(&p_full[g], j & 1u, a.status);
+          ok = wait(&p_full[g], j & 1u);
           if (!ok) break;
           tc_fence_after();
+          if (elect_one()) {
 #pragma unroll
-          for (int k = 0; k < kTcKeys / 16; ++k)  // 16 keys = 8 P columns; V: 16 key rows = 2048 bytes
-            mma_f16_ta(tmem + kColO + g * kTcHd, tmem + kColP + g * (kTcKeys / 2) + 8 * k,
-                       vd + static_cast<uint64_t>(k) * (2048 >> 4), ID_O, (j > 0 || k > 0) ? 1u : 0u);
-          mma_commit(&o_full[g]);
+            for (int k = 0; k < kTcKeys / 16; ++k)  // 16 keys = 8 P columns; V: 16 key rows = 2048 bytes
+              mma_f16_ta(tmem + kColO + g * kTcHd, tmem + kColP + g * (kTcKeys / 2) + 8 * k,
+                         vd + static_cast<uint64_t>(k) * (2048 >> 4), ID_O, (j > 0 || k > 0) ? 1u : 0u);
+            mma_commit(&o_full[g]);
+          }
         }
-        mma_commit(&v_empty[st]);
+        if (elect_one()) mma_commit(&v_empty[st]);
       }
     }
   } else {
