@@ -1,10 +1,13 @@
 // Flash attention on tcgen05 for the unmasked, equal-length case (SigLIP: 1024 tokens per image,
 // 12 heads of 64, no RoPE): the vision tower's dominant kernel at batch 64.
 //
-// One CTA = 256 query rows of one (image, head), as two groups of 128 (MMA M = 128). Per 128-key
-// tile j:
-//   warp 0 (one thread)  TMA: Q once, then K_j and V_j into separate four-stage rings (a K stage
-//                        frees as soon as S_j is computed, so keys stream several tiles ahead)
+// Persistent: one CTA per SM loops over work items, an item being 256 query rows of one (image,
+// head) as two groups of 128 (MMA M = 128). The queries sit in two buffers (the next item's land
+// while this one runs), the K/V rings and the group barriers run on across items, the next item's
+// first S is issued before this item's last P V, and an item's output is stored while the next
+// item's scores are computed. Per 128-key tile j:
+//   warp 0 (one thread)  TMA: Q once per item, then K_j and V_j into separate four-stage rings (a K
+//                        stage frees as soon as S_j is computed, so keys stream several tiles ahead)
 //   warp 1 (elected lane) S_g = Q_g K_j^T  (M 128, N 128, K 64)      -> TMEM S_g
 //                        O_g += P_g V_j   (M 128, N 64,  K 128 keys) -> TMEM O_g, A operand P_g
 //                                                                       read from TMEM
@@ -28,6 +31,8 @@ struct AttnTcArgs {
   int o_type;
   float o_qinv;
   int L;            // tokens per image (queries = keys)
+  int heads;
+  int items;        // (L / 256) x heads x images work items
   float scale_log2;
   int* status;
 };
@@ -36,11 +41,7 @@ constexpr int kTcRows = 128;   // rows per group (MMA M)
 constexpr int kTcKeys = 128;   // keys per tile (MMA N of S, K of P V)
 constexpr int kTcHd = 64;
 constexpr int kTcTile = kTcRows * kTcHd * 2;   // 16 KB: a 128 x 64 bf16 tile
-#ifndef SO101_ATTN_ISSUERS
-#define SO101_ATTN_ISSUERS 1
-#endif
-constexpr int kIssuers = SO101_ATTN_ISSUERS;     // MMA-issuing warps (1: both groups, 2: one each)
-constexpr int kTcThreads = 32 * (1 + kIssuers + 8);
+constexpr int kTcThreads = 32 * (2 + 8);       // TMA warp, MMA warp, two softmax warp groups
 constexpr float kStaleMax = 8.f;               // log2 of the largest factor a stale maximum allows
 #ifndef SO101_ATTN_POLY_PAIRS
 #define SO101_ATTN_POLY_PAIRS 2  // batch 64: 1049 us against 1090 us with none, 1087 with 4, 1142 with 8
@@ -53,12 +54,12 @@ constexpr int kPolyPairs = SO101_ATTN_POLY_PAIRS;
 #define SO101_ATTN_STAGES 4
 #endif
 constexpr int kStages = SO101_ATTN_STAGES;  // K and V ring depth (16 KB per stage each)
-constexpr int kOffQ = 0;                              // 2 groups x 16 KB
-constexpr int kOffK = kOffQ + 2 * kTcTile;            // kStages x 16 KB
+constexpr int kOffQ = 0;                              // 2 buffers x 2 groups x 16 KB
+constexpr int kOffK = kOffQ + 4 * kTcTile;            // kStages x 16 KB
 constexpr int kOffV = kOffK + kStages * kTcTile;      // kStages x 16 KB
 constexpr int kOffBar = kOffV + kStages * kTcTile;
-constexpr int kBarBytes = 512;  // q_full, 4 x kStages ring barriers, 8 group barriers, TMEM slot
-static_assert((1 + 4 * kStages + 8) * 8 + 4 <= kBarBytes, "barrier region");
+constexpr int kBarBytes = 512;  // 4 Q-buffer barriers, 4 x kStages ring barriers, 10 group barriers, TMEM slot
+static_assert((4 + 4 * kStages + 10) * 8 + 4 <= kBarBytes, "barrier region");
 constexpr int kTcSmem = kOffBar + kBarBytes + 1024;
 static_assert(kTcSmem <= 232448, "227 KB of shared memory per CTA");
 
@@ -91,8 +92,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + kOffBar);
-  uint64_t* q_full = bar;                       // [1]
-  uint64_t* k_full = bar + 1;                   // [kStages]
+  uint64_t* q_full = bar;                       // [2] per Q buffer: the item's queries landed
+  uint64_t* q_empty = q_full + 2;               // [2] per Q buffer: the item's S MMAs have read them
+  uint64_t* k_full = q_empty + 2;               // [kStages]
   uint64_t* k_empty = k_full + kStages;         // [kStages]
   uint64_t* v_full = k_empty + kStages;         // [kStages]
   uint64_t* v_empty = v_full + kStages;         // [kStages]
@@ -100,27 +102,37 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   uint64_t* s_free = s_full + 2;                // [2] per group: S_g read into registers
   uint64_t* p_full = s_free + 2;                // [2] per group: P_g written (and O_g rescaled)
   uint64_t* o_full = p_full + 2;                // [2] per group: P_g V accumulated into O_g
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_full + 2);
+  uint64_t* o_free = o_full + 2;                // [2] per group: the item's O_g read out
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_free + 2);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int head = blockIdx.y, img = blockIdx.z;
-  const int row0 = img * a.L + blockIdx.x * 2 * kTcRows;  // first query row (global token row)
-  const int key0 = img * a.L;
   const int n_tiles = a.L / kTcKeys;
+  const int qblocks = a.L / (2 * kTcRows);
+  // work item w: query block w % qblocks of head (w / qblocks) % heads of image w / (qblocks * heads)
+  auto item_rows = [&](int w, int& row0, int& key0, int& head) {
+    const int img = w / (qblocks * a.heads);
+    head = (w / qblocks) % a.heads;
+    key0 = img * a.L;
+    row0 = key0 + (w % qblocks) * 2 * kTcRows;
+  };
 
   if (threadIdx.x == 0) {
-    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&q_full[i], 1);
+      mbar_init(&q_empty[i], 1);
+    }
     for (int i = 0; i < kStages; ++i) {
       mbar_init(&k_full[i], 1);
-      mbar_init(&k_empty[i], kIssuers);  // one commit per issuer
+      mbar_init(&k_empty[i], 1);
       mbar_init(&v_full[i], 1);
-      mbar_init(&v_empty[i], kIssuers);
+      mbar_init(&v_empty[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
       mbar_init(&s_free[i], 4);
       mbar_init(&p_full[i], 4);
       mbar_init(&o_full[i], 1);
+      mbar_init(&o_free[i], 4);
     }
     fence_mbar_init();
   }
@@ -140,89 +152,111 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       tma_prefetch_desc(&tm_k);
       tma_prefetch_desc(&tm_v);
       grid_dep_wait();
-      // Q is read once; K and V are read by the L / 256 CTAs of this (image, head), which run at
-      // the same time, so they need no protection beyond the normal policy
+      // Q is read once; K and V are read by the L / 256 items of this (image, head), which
+      // neighbouring CTAs run at the same time, so they need no protection beyond the normal policy
       const uint64_t once = policy_evict_first(), keep = policy_evict_normal();
-      const int xq = head * kTcHd;
-      mbar_arrive_expect_tx(q_full, 2 * kTcTile);
-      tma_load_2d(smem + kOffQ, &tm_q, q_full, xq, row0, once);
-      tma_load_2d(smem + kOffQ + kTcTile, &tm_q, q_full, xq, row0 + kTcRows, once);
-      for (int j = 0; j < n_tiles; ++j) {
-        const int st = j % kStages;
-        const uint32_t back = static_cast<uint32_t>(j / kStages - 1) & 1u;  // phase of the use kStages ago
-        if (j >= kStages && !mbar_wait(&k_empty[st], back, a.status)) break;
-        mbar_arrive_expect_tx(&k_full[st], kTcTile);
-        tma_load_2d(smem + kOffK + st * kTcTile, &tm_k, &k_full[st], xq, key0 + j * kTcKeys, keep);
-        if (j >= kStages && !mbar_wait(&v_empty[st], back, a.status)) break;
-        mbar_arrive_expect_tx(&v_full[st], kTcTile);
-        tma_load_2d(smem + kOffV + st * kTcTile, &tm_v, &v_full[st], xq, key0 + j * kTcKeys, keep);
+      bool ok = true;
+      int t = 0;  // this CTA's key tile counter over all its items (ring slot and phase)
+      for (int w = blockIdx.x, it = 0; w < a.items && ok; w += gridDim.x, ++it) {
+        int row0, key0, head;
+        item_rows(w, row0, key0, head);
+        const int xq = head * kTcHd;
+        const int qb = it & 1;
+        if (it >= 2 && !mbar_wait(&q_empty[qb], static_cast<uint32_t>((it >> 1) - 1) & 1u, a.status)) break;
+        mbar_arrive_expect_tx(&q_full[qb], 2 * kTcTile);
+        tma_load_2d(smem + kOffQ + 2 * qb * kTcTile, &tm_q, &q_full[qb], xq, row0, once);
+        tma_load_2d(smem + kOffQ + (2 * qb + 1) * kTcTile, &tm_q, &q_full[qb], xq, row0 + kTcRows, once);
+        for (int j = 0; j < n_tiles; ++j, ++t) {
+          const int st = t % kStages;
+          const uint32_t back = static_cast<uint32_t>(t / kStages - 1) & 1u;  // phase of the use kStages ago
+          if (t >= kStages && !mbar_wait(&k_empty[st], back, a.status)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&k_full[st], kTcTile);
+          tma_load_2d(smem + kOffK + st * kTcTile, &tm_k, &k_full[st], xq, key0 + j * kTcKeys, keep);
+          if (t >= kStages && !mbar_wait(&v_empty[st], back, a.status)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&v_full[st], kTcTile);
+          tma_load_2d(smem + kOffV + st * kTcTile, &tm_v, &v_full[st], xq, key0 + j * kTcKeys, keep);
+        }
       }
     }
-  } else if (warp <= kIssuers) {
-    // MMA issue: the whole issuing warp runs the waits, its elected lane issues the MMAs and
-    // commits, for groups [g_lo, g_hi). An issuing thread stalls while the tensor pipe takes its
-    // MMAs; with one issuer per group (kIssuers = 2) the other group's barrier waits and issues
-    // proceed meanwhile. A wait's outcome is made warp-uniform (a timeout in any lane ends the loop).
-    {
-      constexpr uint32_t ID_S = idesc_attn(kTcKeys, 0);
-      constexpr uint32_t ID_O = idesc_attn(kTcHd, 1);
-      const int g_lo = kIssuers == 2 ? warp - 1 : 0, g_hi = kIssuers == 2 ? warp : 2;
-      // S_j(g) = Q_g K_j^T into TMEM S_g
-      auto issue_s = [&](int j, int g) {
-        const uint64_t qd = sw128_desc(smem_u32(smem + kOffQ + g * kTcTile));
-        const uint64_t kd = sw128_desc(smem_u32(smem + kOffK + (j % kStages) * kTcTile));
+  } else if (warp == 1) {
+    // MMA issue: the whole warp runs the waits (their outcomes made warp-uniform: a timeout in any
+    // lane ends the loop), its elected lane issues the MMAs and commits. The tile sequence runs
+    // across this CTA's items: the next tile's S (possibly the next item's first) is issued
+    // before this tile's P V, so the tensor pipe never waits for an item boundary.
+    constexpr uint32_t ID_S = idesc_attn(kTcKeys, 0);
+    constexpr uint32_t ID_O = idesc_attn(kTcHd, 1);
+    auto wait = [&](uint64_t* b, uint32_t parity) { return __all_sync(0xffffffffu, mbar_wait(b, parity, a.status)); };
+    // S_t(g) = Q_g K_t^T into TMEM S_g, for key tile t of the item whose queries sit in buffer qb;
+    // the queries' buffer is released after the S of the item's last tile
+    auto issue_s = [&](int t, int qb, bool last_of_item) {
+      const uint64_t kd = sw128_desc(smem_u32(smem + kOffK + (t % kStages) * kTcTile));
+      bool ok = true;
+      for (int g = 0; g < 2 && ok; ++g) {
+        ok = t == 0 || wait(&s_free[g], static_cast<uint32_t>(t - 1) & 1u);  // S_g of tile t - 1 read
+        if (!ok) break;
+        tc_fence_after();
+        const uint64_t qd = sw128_desc(smem_u32(smem + kOffQ + (2 * qb + g) * kTcTile));
         if (elect_one()) {
 #pragma unroll
           for (int k = 0; k < kTcHd / 16; ++k)
             mma_f16(tmem + kColS + g * kTcKeys, qd + 2 * k, kd + 2 * k, ID_S, k > 0 ? 1u : 0u);
           mma_commit(&s_full[g]);
         }
-      };
-      auto wait = [&](uint64_t* bar, uint32_t parity) {
-        return __all_sync(0xffffffffu, mbar_wait(bar, parity, a.status));
-      };
-      bool ok = wait(q_full, 0) && wait(&k_full[0], 0);
-      if (ok) {
+      }
+      if (ok && elect_one()) {
+        mma_commit(&k_empty[t % kStages]);  // the K stage is free once both groups' S MMAs read it
+        if (last_of_item) mma_commit(&q_empty[qb]);
+      }
+      return ok;
+    };
+    int w = blockIdx.x, it = 0, j = 0, t = 0;
+    bool ok = w < a.items && wait(&q_full[0], 0) && wait(&k_full[0], 0) && issue_s(0, 0, n_tiles == 1);
+    while (ok) {
+      // tile t = tile j of item it, whose S is issued: issue the next tile's S, then P_t V_t
+      const bool item_end = j + 1 == n_tiles;
+      const int w_next = item_end ? w + static_cast<int>(gridDim.x) : w;
+      const int it_next = item_end ? it + 1 : it;
+      const int j_next = item_end ? 0 : j + 1;
+      const bool more = w_next < a.items;
+      if (more) {
+        ok = (!item_end || wait(&q_full[it_next & 1], static_cast<uint32_t>(it_next >> 1) & 1u)) &&
+             wait(&k_full[(t + 1) % kStages], static_cast<uint32_t>((t + 1) / kStages) & 1u) &&
+             issue_s(t + 1, it_next & 1, j_next + 1 == n_tiles);
+        if (!ok) break;
+      }
+      const int st = t % kStages;
+      if (!wait(&v_full[st], static_cast<uint32_t>(t / kStages) & 1u)) break;
+      const uint64_t vd = sw128_desc(smem_u32(smem + kOffV + st * kTcTile));
+      for (int g = 0; g < 2 && ok; ++g) {
+        // P_t written; on an item's first tile also the previous item's O_g read out (this P V
+        // starts O_g afresh)
+        ok = wait(&p_full[g], static_cast<uint32_t>(t) & 1u) &&
+             (j > 0 || it == 0 || wait(&o_free[g], static_cast<uint32_t>(it - 1) & 1u));
+        if (!ok) break;
         tc_fence_after();
-        for (int g = g_lo; g < g_hi; ++g) issue_s(0, g);
-        if (elect_one()) mma_commit(&k_empty[0]);  // the K stage is free once every issuer's S MMAs read it
-      }
-      for (int j = 0; j < n_tiles && ok; ++j) {
-        const int st = j % kStages;
-        if (j + 1 < n_tiles) {
-          const int sn = (j + 1) % kStages;
-          ok = wait(&k_full[sn], static_cast<uint32_t>((j + 1) / kStages) & 1u);
-          for (int g = g_lo; g < g_hi && ok; ++g) {
-            ok = wait(&s_free[g], j & 1u);
-            if (ok) {
-              tc_fence_after();
-              issue_s(j + 1, g);
-            }
-          }
-          if (!ok) break;
-          if (elect_one()) mma_commit(&k_empty[sn]);
-        }
-        if (!wait(&v_full[st], static_cast<uint32_t>(j / kStages) & 1u)) break;
-        const uint64_t vd = sw128_desc(smem_u32(smem + kOffV + st * kTcTile));
-        for (int g = g_lo; g < g_hi && ok; ++g) {
-          ok = wait(&p_full[g], j & 1u);
-          if (!ok) break;
-          tc_fence_after();
-          if (elect_one()) {
+        if (elect_one()) {
 #pragma unroll
-            for (int k = 0; k < kTcKeys / 16; ++k)  // 16 keys = 8 P columns; V: 16 key rows = 2048 bytes
-              mma_f16_ta(tmem + kColO + g * kTcHd, tmem + kColP + g * (kTcKeys / 2) + 8 * k,
-                         vd + static_cast<uint64_t>(k) * (2048 >> 4), ID_O, (j > 0 || k > 0) ? 1u : 0u);
-            mma_commit(&o_full[g]);
-          }
+          for (int k = 0; k < kTcKeys / 16; ++k)  // 16 keys = 8 P columns; V: 16 key rows = 2048 bytes
+            mma_f16_ta(tmem + kColO + g * kTcHd, tmem + kColP + g * (kTcKeys / 2) + 8 * k,
+                       vd + static_cast<uint64_t>(k) * (2048 >> 4), ID_O, (j > 0 || k > 0) ? 1u : 0u);
+          mma_commit(&o_full[g]);
         }
-        if (elect_one()) mma_commit(&v_empty[st]);
       }
+      if (!ok) break;
+      if (elect_one()) mma_commit(&v_empty[st]);
+      if (!more) break;
+      w = w_next, it = it_next, j = j_next, ++t;
     }
   } else {
-    // ---------------- softmax: group g = (warp - 1 - kIssuers) / 4, row r = quad * 32 + lane
+    // ---------------- softmax: group g = (warp - 2) / 4, row r = quad * 32 + lane
     grid_dep_wait();
-    const int g = (warp - 1 - kIssuers) >> 2;
+    const int g = (warp - 2) >> 2;
     const int quad = warp & 3;
     const int r = quad * 32 + lane;
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(quad * 32) << 16);
@@ -230,91 +264,103 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const uint32_t p_addr = lane_base + kColP + g * (kTcKeys / 2);
     const uint32_t o_addr = lane_base + kColO + g * kTcHd;
     const float sc = a.scale_log2;
-    float m = -INFINITY, l = 0.f;
     bool ok = true;
-    for (int j = 0; j < n_tiles && ok; ++j) {
-      if (!mbar_wait(&s_full[g], j & 1u, a.status)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      uint32_t sv[kTcKeys];
-#pragma unroll
-      for (int c = 0; c < kTcKeys; c += 32) tmem_ld32(s_addr + c, sv + c);
-      tmem_ld_wait();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&s_free[g]);  // the MMA may write S_{j+1} now
-      // row maximum over eight independent chains (short dependency chains keep the pipe busy)
-      float mx[8];
-#pragma unroll
-      for (int t = 0; t < 8; ++t) mx[t] = __uint_as_float(sv[t]);
-#pragma unroll
-      for (int e = 8; e < kTcKeys; e += 8)
-#pragma unroll
-        for (int t = 0; t < 8; ++t) mx[t] = fmaxf(mx[t], __uint_as_float(sv[e + t]));
-      const float m_tile =
-          fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7]))) * sc;
-      const bool raise = m_tile > m + kStaleMax;
-      const float alpha = raise ? ex2(m - m_tile) : 1.f;  // 0 on the first tile (m = -inf)
-      if (raise) m = m_tile;
-      const float neg_m = -m;
-      // P = exp2(s * scale - m) as bf16 pairs, in registers first: the previous tile's P V may
-      // still be reading P_g, and it runs while these exponentials are computed
-      uint32_t pk[kTcKeys / 2];
-      float ls[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // row sum over four packed chains
-#pragma unroll
-      for (int e = 0; e < kTcKeys; e += 2) {
-        float x0, x1;
-        fma2(x0, x1, __uint_as_float(sv[e]), __uint_as_float(sv[e + 1]), sc, neg_m);
-        float p0, p1;
-        if (((e >> 1) & 15) < kPolyPairs) {
-          const float2 pp = exp2_poly2(make_float2(x0, x1));
-          p0 = pp.x, p1 = pp.y;
-        } else {
-          p0 = ex2(x0), p1 = ex2(x1);
-        }
-        const int t = (e >> 1) & 3;
-        add2(ls[2 * t], ls[2 * t + 1], p0, p1);
-        pk[e >> 1] = bf16x2(p0, p1);
-      }
-      const float s0 = (ls[0] + ls[2]) + (ls[4] + ls[6]), s1 = (ls[1] + ls[3]) + (ls[5] + ls[7]);
-      if (j > 0) {
-        // P_{j-1} V has landed: P_g may be overwritten and O_g is stable for a rescale
-        if (!mbar_wait(&o_full[g], (j - 1) & 1u, a.status)) {
+    int t = 0;  // key tile counter over this CTA's items (the group barriers' phases)
+    for (int w = blockIdx.x; w < a.items && ok; w += gridDim.x) {
+      float m = -INFINITY, l = 0.f;
+      for (int j = 0; j < n_tiles; ++j, ++t) {
+        if (!mbar_wait(&s_full[g], static_cast<uint32_t>(t) & 1u, a.status)) {
           ok = false;
           break;
         }
         tc_fence_after();
-      }
+        uint32_t sv[kTcKeys];
 #pragma unroll
-      for (int c = 0; c < kTcKeys / 2; c += 16) tmem_st16(p_addr + c, pk + c);
-      if (j > 0 && __any_sync(0xffffffffu, raise)) {
-        // the row maximum rose by more than 2^8 somewhere in this warp: rescale O_g rows
+        for (int c = 0; c < kTcKeys; c += 32) tmem_ld32(s_addr + c, sv + c);
+        tmem_ld_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s_free[g]);  // the MMA may write the next tile's S now
+        // row maximum over eight independent chains (short dependency chains keep the pipe busy)
+        float mx[8];
 #pragma unroll
-        for (int c = 0; c < kTcHd; c += 32) {
-          uint32_t ov[32];
-          tmem_ld32(o_addr + c, ov);
-          tmem_ld_wait();
+        for (int e = 0; e < 8; ++e) mx[e] = __uint_as_float(sv[e]);
 #pragma unroll
-          for (int e = 0; e < 32; ++e) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * alpha);
-          tmem_st16(o_addr + c, ov);
-          tmem_st16(o_addr + c + 16, ov + 16);
+        for (int e = 8; e < kTcKeys; e += 8)
+#pragma unroll
+          for (int c = 0; c < 8; ++c) mx[c] = fmaxf(mx[c], __uint_as_float(sv[e + c]));
+        const float m_tile =
+            fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7]))) * sc;
+        const bool raise = m_tile > m + kStaleMax;
+        const float alpha = raise ? ex2(m - m_tile) : 1.f;  // 0 on an item's first tile (m = -inf)
+        if (raise) m = m_tile;
+        const float neg_m = -m;
+        // P = exp2(s * scale - m) as bf16 pairs, in registers first: the previous tile's P V may
+        // still be reading P_g, and it runs while these exponentials are computed
+        uint32_t pk[kTcKeys / 2];
+        float ls[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // row sum over four packed chains
+#pragma unroll
+        for (int e = 0; e < kTcKeys; e += 2) {
+          float x0, x1;
+          fma2(x0, x1, __uint_as_float(sv[e]), __uint_as_float(sv[e + 1]), sc, neg_m);
+          float p0, p1;
+          if (((e >> 1) & 15) < kPolyPairs) {
+            const float2 pp = exp2_poly2(make_float2(x0, x1));
+            p0 = pp.x, p1 = pp.y;
+          } else {
+            p0 = ex2(x0), p1 = ex2(x1);
+          }
+          const int c = (e >> 1) & 3;
+          add2(ls[2 * c], ls[2 * c + 1], p0, p1);
+          pk[e >> 1] = bf16x2(p0, p1);
         }
+        const float s0 = (ls[0] + ls[2]) + (ls[4] + ls[6]), s1 = (ls[1] + ls[3]) + (ls[5] + ls[7]);
+        if (j > 0) {
+          // P_{t-1} V has landed: P_g may be overwritten and O_g is stable for a rescale (on an
+          // item's first tile the previous item's read-out already waited for it)
+          if (!mbar_wait(&o_full[g], static_cast<uint32_t>(t - 1) & 1u, a.status)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+        }
+#pragma unroll
+        for (int c = 0; c < kTcKeys / 2; c += 16) tmem_st16(p_addr + c, pk + c);
+        if (j > 0 && __any_sync(0xffffffffu, raise)) {
+          // the row maximum rose by more than 2^8 somewhere in this warp: rescale O_g rows
+#pragma unroll
+          for (int c = 0; c < kTcHd; c += 32) {
+            uint32_t ov[32];
+            tmem_ld32(o_addr + c, ov);
+            tmem_ld_wait();
+#pragma unroll
+            for (int e = 0; e < 32; ++e) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * alpha);
+            tmem_st16(o_addr + c, ov);
+            tmem_st16(o_addr + c + 16, ov + 16);
+          }
+        }
+        l = l * alpha + (s0 + s1);
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&p_full[g]);
       }
-      l = l * alpha + (s0 + s1);
-      tmem_st_wait();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[g]);
-    }
-    // O / l for this row
-    if (ok && mbar_wait(&o_full[g], (n_tiles - 1) & 1u, a.status)) {
+      // O / l for this row: read O_g out, hand it back to the MMA (the next item's first P V
+      // overwrites it), then store while the next item's scores are computed
+      if (!ok || !mbar_wait(&o_full[g], static_cast<uint32_t>(t - 1) & 1u, a.status)) {
+        ok = false;
+        break;
+      }
       tc_fence_after();
       uint32_t ov[kTcHd];
       tmem_ld32(o_addr, ov);
       tmem_ld32(o_addr + 32, ov + 32);
       tmem_ld_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&o_free[g]);
+      int row0, key0, head;
+      item_rows(w, row0, key0, head);
       const float inv = 1.f / l;
       const long long orow = row0 + g * kTcRows + r;
       if (a.o_type == SO101_BF16) {
@@ -411,10 +457,20 @@ int attention_tc_launch(const void* q, long long ldq, const void* k, long long l
   a.o_type = o_type;
   a.o_qinv = o_type == SO101_I8 ? static_cast<float>(1.0 / static_cast<double>(o_qscale)) : 0.f;
   a.L = static_cast<int>(L);
+  a.heads = heads;
+  a.items = static_cast<int>(L / 256) * heads * batch;
   a.scale_log2 = static_cast<float>(1.4426950408889634 / 8.0);
   a.status = status_ptr();
-  return launch_kernel(attention_tc_kernel, dim3(static_cast<unsigned>(L / 256), heads, batch), dim3(kTcThreads),
-                       kTcSmem, stream, tq, tk, tv, a);
+  // persistent: one CTA per SM (TMEM and shared memory allow no more), each looping over items
+  static int sms = 0;
+  if (!sms) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms < 1) sms = 148;
+  }
+  const int grid = a.items < sms ? a.items : sms;
+  return launch_kernel(attention_tc_kernel, dim3(static_cast<unsigned>(grid)), dim3(kTcThreads), kTcSmem, stream,
+                       tq, tk, tv, a);
 }
 
 }  // namespace so101
