@@ -511,35 +511,39 @@ __global__ void __launch_bounds__(kTileThreads, (SWAP && DUAL) ? 1 : 2)
       load_w(i, st, &full[s]);
       load_x(i, st, &full[s]);
     }
-  } else if (warp == 1 && lane == 0) {
-    // MMA issuer
+  } else if (warp == 1) {
+    // MMA issuer: the whole warp runs the waits (outcomes made warp-uniform), the elected lane
+    // issues and commits
     for (int i = 0; i < nkb; ++i) {
       const int s = i % stages;
       const uint32_t round = static_cast<uint32_t>(i / stages);
-      if (!mbar_wait(&full[s], round & 1u, a.status)) break;
+      if (!__all_sync(0xffffffffu, mbar_wait(&full[s], round & 1u, a.status))) break;
       tc_fence_after();
       const uint32_t base = smem_u32(smem + s * STAGE_BYTES);
       const uint64_t a0 = sw128_desc(base);
       const uint64_t b0 = sw128_desc(base + NA * A_BYTES);
+      if (elect_one()) {
 #pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const uint32_t acc = (i > 0 || k > 0) ? 1u : 0u;
-        if (I8)
-          mma_i8(tmem, a0 + 2 * k, b0 + 2 * k, IDESC, acc);
-        else
-          mma_f16(tmem, a0 + 2 * k, b0 + 2 * k, IDESC, acc);
-        if (DUAL) {
-          const uint64_t a1 = SWAP ? sw128_desc(base + A_BYTES) : a0;
-          const uint64_t b1 = SWAP ? b0 : sw128_desc(base + NA * A_BYTES + B_BYTES);
+        for (int k = 0; k < 4; ++k) {
+          const uint32_t acc = (i > 0 || k > 0) ? 1u : 0u;
           if (I8)
-            mma_i8(tmem + BN, a1 + 2 * k, b1 + 2 * k, IDESC, acc);
+            mma_i8(tmem, a0 + 2 * k, b0 + 2 * k, IDESC, acc);
           else
-            mma_f16(tmem + BN, a1 + 2 * k, b1 + 2 * k, IDESC, acc);
+            mma_f16(tmem, a0 + 2 * k, b0 + 2 * k, IDESC, acc);
+          if (DUAL) {
+            const uint64_t a1 = SWAP ? sw128_desc(base + A_BYTES) : a0;
+            const uint64_t b1 = SWAP ? b0 : sw128_desc(base + NA * A_BYTES + B_BYTES);
+            if (I8)
+              mma_i8(tmem + BN, a1 + 2 * k, b1 + 2 * k, IDESC, acc);
+            else
+              mma_f16(tmem + BN, a1 + 2 * k, b1 + 2 * k, IDESC, acc);
+          }
         }
+        mma_commit(&empty[s]);
       }
-      mma_commit(&empty[s]);
+      __syncwarp();
     }
-    mma_commit(accum);
+    if (elect_one()) mma_commit(accum);
     grid_dep_wait();
   } else {
     grid_dep_wait();
@@ -893,19 +897,29 @@ __global__ void __launch_bounds__(32 * (2 + kEpiWarps), 1)
       grid_dep_launch();
     }
   } else if (warp == 1) {
-    if (lane == 0) {
+    // MMA issuer. bf16: the whole warp runs the waits (outcomes made warp-uniform) and its elected
+    // lane issues and commits, which keeps the descriptors warp-uniform (expert and prefix GEMMs
+    // 10-25% faster). int8: lane 0 alone, which measured 2-8% faster for the vision GEMMs, whose
+    // dequantizing epilogue is the bound.
+    constexpr bool kWarp = !I8;
+    auto wait = [&](uint64_t* b, uint32_t parity) {
+      const bool ok = mbar_wait(b, parity, a.status);
+      return kWarp ? __all_sync(0xffffffffu, ok) : ok;
+    };
+    auto issuer = [&]() { return kWarp ? elect_one() : true; };
+    if (kWarp || lane == 0) {
       int it = 0, local = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < a.num_tiles && ok; tile += gridDim.x, ++local) {
         const int buf = local & 1;
         const uint32_t use = static_cast<uint32_t>(local >> 1);
-        if (local >= 2 && !mbar_wait(&acc_empty[buf], (use - 1) & 1u, a.status)) break;
+        if (local >= 2 && !wait(&acc_empty[buf], (use - 1) & 1u)) break;
         tc_fence_after();
         const uint32_t d = tmem + static_cast<uint32_t>(buf * NACC);
         for (int kb = 0; kb < kb_total; ++kb, ++it) {
           const int s = it % stages;
           const uint32_t round = static_cast<uint32_t>(it / stages);
-          if (!mbar_wait(&full[s], round & 1u, a.status)) {
+          if (!wait(&full[s], round & 1u)) {
             ok = false;
             break;
           }
@@ -913,24 +927,27 @@ __global__ void __launch_bounds__(32 * (2 + kEpiWarps), 1)
           const uint32_t base = smem_u32(smem + s * STAGE_BYTES);
           const uint64_t a0 = sw128_desc(base);
           const uint64_t b0 = sw128_desc(base + A_BYTES);
+          if (issuer()) {
 #pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const uint32_t acc = (kb > 0 || k > 0) ? 1u : 0u;
-            if (I8)
-              mma_i8(d, a0 + 2 * k, b0 + 2 * k, IDESC, acc);
-            else
-              mma_f16(d, a0 + 2 * k, b0 + 2 * k, IDESC, acc);
-            if (DUAL) {
-              const uint64_t b1 = sw128_desc(base + A_BYTES + B_BYTES);
+            for (int k = 0; k < 4; ++k) {
+              const uint32_t acc = (kb > 0 || k > 0) ? 1u : 0u;
               if (I8)
-                mma_i8(d + BN, a0 + 2 * k, b1 + 2 * k, IDESC, acc);
+                mma_i8(d, a0 + 2 * k, b0 + 2 * k, IDESC, acc);
               else
-                mma_f16(d + BN, a0 + 2 * k, b1 + 2 * k, IDESC, acc);
+                mma_f16(d, a0 + 2 * k, b0 + 2 * k, IDESC, acc);
+              if (DUAL) {
+                const uint64_t b1 = sw128_desc(base + A_BYTES + B_BYTES);
+                if (I8)
+                  mma_i8(d + BN, a0 + 2 * k, b1 + 2 * k, IDESC, acc);
+                else
+                  mma_f16(d + BN, a0 + 2 * k, b1 + 2 * k, IDESC, acc);
+              }
             }
+            mma_commit(&empty[s]);
           }
-          mma_commit(&empty[s]);
+          if (kWarp) __syncwarp();
         }
-        mma_commit(&acc_full[buf]);
+        if (issuer()) mma_commit(&acc_full[buf]);
       }
     }
   } else {
@@ -1107,19 +1124,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(32 * (2 + kEpiWarps)
       }
     }
   } else if (warp == 1) {
-    if (lane == 0 && leader) {
+    // MMA issuer (the even CTA): the whole warp runs the waits (outcomes made warp-uniform), the
+    // elected lane issues and commits
+    if (leader) {
       int it = 0, local = 0;
       bool ok = true;
       for (int tile = pair; tile < a.num_tiles && ok; tile += npairs, ++local) {
         const int buf = local & 1;
         const uint32_t use = static_cast<uint32_t>(local >> 1);
-        if (local >= 2 && !mbar_wait(&acc_empty[buf], (use - 1) & 1u, a.status)) break;
+        if (local >= 2 && !__all_sync(0xffffffffu, mbar_wait(&acc_empty[buf], (use - 1) & 1u, a.status))) break;
         tc_fence_after();
         const uint32_t d = tmem + static_cast<uint32_t>(buf * NACC);
         for (int kb = 0; kb < kb_total; ++kb, ++it) {
           const int s = it % stages;
           const uint32_t round = static_cast<uint32_t>(it / stages);
-          if (!mbar_wait(&full[s], round & 1u, a.status)) {
+          if (!__all_sync(0xffffffffu, mbar_wait(&full[s], round & 1u, a.status))) {
             ok = false;
             break;
           }
@@ -1127,24 +1146,27 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(32 * (2 + kEpiWarps)
           const uint32_t base = smem_u32(smem + s * STAGE_BYTES);
           const uint64_t a0 = sw128_desc(base);
           const uint64_t b0 = sw128_desc(base + A_BYTES);
+          if (elect_one()) {
 #pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const uint32_t acc = (kb > 0 || k > 0) ? 1u : 0u;
-            if (I8)
-              mma_i8_pair(d, a0 + 2 * k, b0 + 2 * k, IDESC, acc);
-            else
-              mma_f16_pair(d, a0 + 2 * k, b0 + 2 * k, IDESC, acc);
-            if (DUAL) {
-              const uint64_t b1 = sw128_desc(base + A_BYTES + B_BYTES);
+            for (int k = 0; k < 4; ++k) {
+              const uint32_t acc = (kb > 0 || k > 0) ? 1u : 0u;
               if (I8)
-                mma_i8_pair(d + BN, a0 + 2 * k, b1 + 2 * k, IDESC, acc);
+                mma_i8_pair(d, a0 + 2 * k, b0 + 2 * k, IDESC, acc);
               else
-                mma_f16_pair(d + BN, a0 + 2 * k, b1 + 2 * k, IDESC, acc);
+                mma_f16_pair(d, a0 + 2 * k, b0 + 2 * k, IDESC, acc);
+              if (DUAL) {
+                const uint64_t b1 = sw128_desc(base + A_BYTES + B_BYTES);
+                if (I8)
+                  mma_i8_pair(d + BN, a0 + 2 * k, b1 + 2 * k, IDESC, acc);
+                else
+                  mma_f16_pair(d + BN, a0 + 2 * k, b1 + 2 * k, IDESC, acc);
+              }
             }
+            mma_commit_pair(&empty[s]);
           }
-          mma_commit_pair(&empty[s]);
+          __syncwarp();
         }
-        if (ok) mma_commit_pair(&acc_full[buf]);
+        if (ok && elect_one()) mma_commit_pair(&acc_full[buf]);
       }
     }
   } else {
