@@ -363,14 +363,17 @@ __global__ void __launch_bounds__(128 * G, 1) attention_o_kernel(const __grid_co
     attention_body<64, false, true, kAoBuf, G>(a.at, 0, q0, h, bi, smem + kAoOffAttn, smem + kAoOffO);
   fence_async_smem();  // the O tile's generic-proxy stores, before the tensor core reads them
   __syncthreads();
-  if (t == 0) {
-    if (mbar_wait(w_full, 0, a.status)) {
+  if (warp == 0) {
+    // warp 0 waits together, its elected lane issues (warp-uniform descriptors)
+    if (__all_sync(0xffffffffu, mbar_wait(w_full, 0, a.status))) {
       tc_fence_after();
       const uint64_t ad = sw128_desc(smem_u32(smem + kAoOffW)), bd = sw128_desc(smem_u32(smem + kAoOffO));
+      if (elect_one()) {
 #pragma unroll
-      for (int k = 0; k < 4; ++k) mma_f16(tmem, ad + 2 * k, bd + 2 * k, idesc_bf16(128, 64), k > 0 ? 1u : 0u);
-      mma_commit(mma_done);
-    } else {
+        for (int k = 0; k < 4; ++k) mma_f16(tmem, ad + 2 * k, bd + 2 * k, idesc_bf16(128, 64), k > 0 ? 1u : 0u);
+        mma_commit(mma_done);
+      }
+    } else if (elect_one()) {
       mbar_arrive(mma_done);  // the weights never came: unwind through the cluster barriers
     }
   }

@@ -129,29 +129,35 @@ __global__ void __launch_bounds__(kMlpThreads, 1) mlp_kernel(const __grid_consta
       tma_load_2d(st + kMlpWBlk, &tm_gu, &full[s], i * 64, a.mlp + r * 128, pol_w);
       tma_load_2d(st + 2 * kMlpWBlk, &tm_x, &full[s], i * 64, static_cast<int>(row0), pol_x);
     }
-  } else if (warp == 1 && lane == 0) {
-    // MMA issuer: gate and up accumulators
+  } else if (warp == 1) {
+    // MMA issuer, gate and up accumulators: the whole warp runs the waits (outcomes made
+    // warp-uniform), its elected lane issues and commits
     bool ok = true;
     for (int i = 0; i < a.kb && ok; ++i) {
       const int s = i % kMlpStages;
       const uint32_t round = static_cast<uint32_t>(i / kMlpStages);
-      ok = mbar_wait(&full[s], round & 1u, a.status);
+      ok = __all_sync(0xffffffffu, mbar_wait(&full[s], round & 1u, a.status));
       if (!ok) break;
       tc_fence_after();
       const uint32_t base = smem_u32(smem + s * kMlpStage);
       const uint64_t ag = sw128_desc(base), au = sw128_desc(base + kMlpWBlk), bx = sw128_desc(base + 2 * kMlpWBlk);
+      if (elect_one()) {
 #pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const uint32_t acc = (i > 0 || k > 0) ? 1u : 0u;
-        mma_f16(tmem, ag + 2 * k, bx + 2 * k, kIdesc, acc);
-        mma_f16(tmem + 64, au + 2 * k, bx + 2 * k, kIdesc, acc);
+        for (int k = 0; k < 4; ++k) {
+          const uint32_t acc = (i > 0 || k > 0) ? 1u : 0u;
+          mma_f16(tmem, ag + 2 * k, bx + 2 * k, kIdesc, acc);
+          mma_f16(tmem + 64, au + 2 * k, bx + 2 * k, kIdesc, acc);
+        }
+        mma_commit(&empty[s]);
       }
-      mma_commit(&empty[s]);
+      __syncwarp();
     }
-    if (ok)
-      mma_commit(accum);
-    else
-      mbar_arrive(accum);  // a stage never came: unwind with the error recorded
+    if (elect_one()) {
+      if (ok)
+        mma_commit(accum);
+      else
+        mbar_arrive(accum);  // a stage never came: unwind with the error recorded
+    }
     grid_dep_wait();
   } else {
     grid_dep_wait();
@@ -197,18 +203,21 @@ __global__ void __launch_bounds__(kMlpThreads, 1) mlp_kernel(const __grid_consta
   mlp_fence_async_smem();  // the activation tile's generic-proxy stores, before the MMA reads them
   tc_fence_before();
   __syncthreads();
-  if (t == 0) {
-    if (acc_ok && mbar_wait(down_full, 0, a.status)) {
+  if (warp == 0) {
+    // warp 0 waits together, its elected lane issues (warp-uniform descriptors)
+    if (acc_ok && __all_sync(0xffffffffu, mbar_wait(down_full, 0, a.status))) {
       tc_fence_after();
+      if (elect_one()) {
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const uint64_t ad = sw128_desc(smem_u32(smem + kMlpOffDown + h * kMlpWBlk));
-        const uint64_t bd = sw128_desc(smem_u32(smem + kMlpOffAct + h * kMlpXBlk));
+        for (int h = 0; h < 2; ++h) {
+          const uint64_t ad = sw128_desc(smem_u32(smem + kMlpOffDown + h * kMlpWBlk));
+          const uint64_t bd = sw128_desc(smem_u32(smem + kMlpOffAct + h * kMlpXBlk));
 #pragma unroll
-        for (int k = 0; k < 4; ++k) mma_f16(tmem + 128, ad + 2 * k, bd + 2 * k, kIdesc, (h > 0 || k > 0) ? 1u : 0u);
+          for (int k = 0; k < 4; ++k) mma_f16(tmem + 128, ad + 2 * k, bd + 2 * k, kIdesc, (h > 0 || k > 0) ? 1u : 0u);
+        }
+        mma_commit(down_done);
       }
-      mma_commit(down_done);
-    } else {
+    } else if (elect_one()) {
       mbar_arrive(down_done);
     }
   }
