@@ -333,6 +333,33 @@ def test_siglip_attention_batched(out):
     assert torch.equal(got, again)
 
 
+@pytest.mark.parametrize("shape", [(13, 1024, "bf16"), (13, 1024, "int8"), (40, 256, "bf16"), (7, 512, "bf16")])
+def test_siglip_attention_many_items(shape):
+    """The unmasked tcgen05 kernel is persistent: one CTA per SM loops over (query block, head,
+    image) items. These shapes give CTAs several items each, with a count that does not divide
+    the grid: 624 items of 8 key tiles, 480 items of 2 key tiles (every other tile's next S
+    belongs to the next item), 168 items of 4 key tiles (a few CTAs get a second item). The
+    queries' double buffer, the hand-back of O between items and the rings running on across
+    items are all exercised; sampled images against the float32 reference, replays equal."""
+    from so101_smolvla_edge_b200.ops import attention
+
+    B, L, out = shape
+    H, hd = 12, 64
+    qkv = rnd(B, L, 3 * H * hd, dtype=torch.bfloat16, scale=2.0, seed=B + L)
+    q, k, v = qkv[:, :, : H * hd], qkv[:, :, H * hd : 2 * H * hd], qkv[:, :, 2 * H * hd :]
+    qs = 0.02
+    kw = dict(out_dtype=torch.int8, out_qscale=qs) if out == "int8" else {}
+    got = attention(q, k, v, H, H, **kw)
+    for b in sorted({0, B // 2, B - 1}):
+        want = attention_ref(qkv[b], k[b], v[b], H, H, None)
+        if out == "int8":
+            assert (got[b].float() - torch.clamp(torch.round(want / qs), -128, 127)).abs().max() <= 1, b
+        else:
+            err = (got[b].float() - want).abs()
+            assert err.max() <= 0.02 * want.abs().max() and err.mean() <= 2e-3 * want.abs().mean() + 1e-4, b
+    assert torch.equal(got, attention(q, k, v, H, H, **kw))
+
+
 @pytest.mark.parametrize("case", ["expert_self", "expert_cross", "prefix", "five_heads_per_kv", "prefix_v_rows",
                                   "long_queries", "one_head_per_kv"])
 def test_attention_gqa_batched(case):
