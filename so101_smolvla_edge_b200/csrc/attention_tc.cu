@@ -44,9 +44,10 @@ constexpr int kTcTile = kTcRows * kTcHd * 2;   // 16 KB: a 128 x 64 bf16 tile
 constexpr int kTcThreads = 32 * (2 + 8);       // TMA warp, MMA warp, two softmax warp groups
 constexpr float kStaleMax = 8.f;               // log2 of the largest factor a stale maximum allows
 #ifndef SO101_ATTN_POLY_PAIRS
-// batch 64, persistent kernel, two orders on one box: 897 / 898 us against 904 / 911 with 2,
-// 1018 with 1, 1030 with none (the non-persistent kernel measured 1049 with 2, 1087 with 4)
-#define SO101_ATTN_POLY_PAIRS 3
+// batch 64, persistent kernel, two orders on one box: 904 / 911 us against 897 / 898 with 3
+// (which moves the configs[0] W8A8 chunks outside the reference's own one-ulp band), 1018 with 1,
+// 1030 with none; the non-persistent kernel measured 1049 with 2, 1087 with 4
+#define SO101_ATTN_POLY_PAIRS 2
 #endif
 // Of every 16 score pairs, how many take exp2 from the polynomial (FMA pipe) instead of MUFU.
 constexpr int kPolyPairs = SO101_ATTN_POLY_PAIRS;
