@@ -11,8 +11,9 @@
 //   2  runs the attention of its head over all keys, writing the normalised rows as bf16 straight
 //      into the MMA's B operand tile in shared memory (the same bf16 rounding the unfused path
 //      applies before storing them): the mma.sync flash loop of attention_tile.cuh (a six-tile
-//      K/V ring; two or three warp groups taking the tiles in turn, merged at the end), or, opt-in
-//      (SO101_ATTN_O_TC=1) and when the keys fit six 64-key tiles, on tcgen05 (attention_head_tc);
+//      K/V ring; two or three warp groups taking the tiles in turn, merged at the end), or, by
+//      default when the keys fit six 64-key tiles (SO101_ATTN_O_TC=0 turns it off), on tcgen05
+//      (attention_head_tc);
 //   3  issues one M=128, N=64, K=64 tcgen05.mma: its head's fp32 partial (features x tokens) in
 //      TMEM, staged to shared memory;
 //   4  after a cluster barrier, sums whole tokens over the nq partials through DSMEM in head
@@ -183,17 +184,20 @@ __device__ __forceinline__ bool attention_head_tc(const AttnArgs& a, int q0, int
   tc_fence_before();
   __syncthreads();
 
-  // 2. S = Q K^T
-  if (t == 0) {
+  // 2. S = Q K^T, issued by warp 0's elected lane (warp-uniform descriptors)
+  if ((t >> 5) == 0) {
     tc_fence_after();
     constexpr uint32_t ID_S = idesc_attn(64, 0);
     const uint64_t qd = sw128_desc(smem_u32(q_s));
-    for (int tile = 0; tile < n_tiles; ++tile) {
-      const uint64_t kd = sw128_desc(smem_u32(k_s + tile * 64 * 128));
+    if (elect_one()) {
+      for (int tile = 0; tile < n_tiles; ++tile) {
+        const uint64_t kd = sw128_desc(smem_u32(k_s + tile * 64 * 128));
 #pragma unroll
-      for (int k = 0; k < 4; ++k) mma_f16(tmem + 64 * tile, qd + 2 * k, kd + 2 * k, ID_S, k > 0 ? 1u : 0u);
+        for (int k = 0; k < 4; ++k) mma_f16(tmem + 64 * tile, qd + 2 * k, kd + 2 * k, ID_S, k > 0 ? 1u : 0u);
+      }
+      mma_commit(s_done);
     }
-    mma_commit(s_done);
+    __syncwarp();
   }
 
   // 3. softmax over TMEM lanes 0..63: quarter q = warp % 4 < 2, warp group g = warp / 4
@@ -277,14 +281,17 @@ __device__ __forceinline__ bool attention_head_tc(const AttnArgs& a, int q0, int
   tc_fence_before();
   __syncthreads();
 
-  // 4. O = P V
-  if (t == 0 && ok) {
+  // 4. O = P V, issued by warp 0's elected lane (ok is warp-uniform there)
+  if ((t >> 5) == 0 && ok) {
     tc_fence_after();
     constexpr uint32_t ID_O = idesc_attn(64, 1);
     const uint64_t vd = sw128_desc(smem_u32(v_s));
-    for (int k = 0; k < 4 * n_tiles; ++k)
-      mma_f16_ta(tmem + kAoTcColO, tmem + 8 * k, vd + static_cast<uint64_t>(k) * (2048 >> 4), ID_O, k > 0 ? 1u : 0u);
-    mma_commit(o_done);
+    if (elect_one()) {
+      for (int k = 0; k < 4 * n_tiles; ++k)
+        mma_f16_ta(tmem + kAoTcColO, tmem + 8 * k, vd + static_cast<uint64_t>(k) * (2048 >> 4), ID_O, k > 0 ? 1u : 0u);
+      mma_commit(o_done);
+    }
+    __syncwarp();
   }
 
   // 5. O / l into the output tile
@@ -431,14 +438,14 @@ EncodeFn encode_fn() {
 
 bool aligned16(const void* p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; }
 
-// SO101_ATTN_O_TC=1 runs the attention of so101_attention_o on tcgen05 (read per call: the engine
-// calls it while it records its programs). Off by default: at the expert's 50 query rows the
-// attention is bound by loading the kv head's 291 keys and values (80 KB per CTA, 3 us), and the
-// tcgen05 form's two dependent MMA rounds and two softmax passes measured 0.1 ms per chunk slower
-// than the mma.sync flash loop.
+// The attention of so101_attention_o runs on tcgen05 when the keys fit six 64-key tiles, unless
+// SO101_ATTN_O_TC=0 (read per call: the engine calls it while it records its programs) selects the
+// mma.sync flash loop. With its MMAs issued by an elected lane of a warp-uniform warp 0 the tcgen05
+// form measured denoise 5.155 against 5.286 ms per batch-1 chunk; issued by one thread it had been
+// 0.1 ms per chunk slower than the mma.sync loop.
 bool ao_tc_enabled() {
   const char* e = std::getenv("SO101_ATTN_O_TC");
-  return e && e[0] == '1';
+  return !(e && e[0] == '0');
 }
 
 // Whether a cluster of `heads` CTAs of attention_o_kernel<G> can be resident at all (non-portable

@@ -437,8 +437,8 @@ def test_attention_o_equals_attention_then_projection(kind, batch, n_out, tc, mo
     itself: bf16(y * w) exactly, per-tile sums of squares to fp32 rounding; a second call repeats
     the bits. The expert's self (own rows rotated on chip, causal onto its own rows) and cross
     attention at 50 rows, a batch of two, a 241-row prefix (4 query blocks) and a ragged
-    100-feature output, with the attention as the mma.sync flash loop and on tcgen05
-    (SO101_ATTN_O_TC=1); cross attention over 420 keys (more than the tcgen05 form's six key tiles)
+    100-feature output, with the attention on tcgen05 (the default) and as the mma.sync flash loop
+    (SO101_ATTN_O_TC=0); cross attention over 420 keys (more than the tcgen05 form's six key tiles)
     always takes the flash loop."""
     from so101_smolvla_edge_b200.ops import attention, attention_o, rope_kv
 
